@@ -1,0 +1,255 @@
+// C-ABI entry points of libqsdpa.so: argument validation, split planning,
+// workspace layout and kernel selection for the fused decode path.
+//
+// Mirrors the checks of the reference's quantized_sdpa
+// (mlx_qsdpa/dispatch.py:41-65) and its single-pass / split-K routing
+// (dispatch.py:98-111); the Python layer above raises the reference's
+// ValueError messages before calling in, so the codes returned here are a
+// second line of defence for other FFI callers.
+#include <stdarg.h>
+#include <stdio.h>
+
+#include <atomic>
+#include <string>
+
+#include "qsdpa_internal.cuh"
+
+namespace qsdpa {
+
+namespace {
+thread_local std::string g_last_error;
+std::atomic<int> g_sm_count[64];
+
+constexpr size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
+constexpr int kMaxSplits = 1024;
+constexpr int kMinChunk = 256;  // keys per CTA below which splitting stops paying
+}  // namespace
+
+int set_error(int code, const char* fmt, ...) {
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof(buf), fmt, ap);
+    va_end(ap);
+    g_last_error = buf;
+    return code;
+}
+
+int check_launch(const char* what) {
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return set_error(QSDPA_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+    return QSDPA_OK;
+}
+
+int sm_count() {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
+    int v = g_sm_count[dev].load(std::memory_order_relaxed);
+    if (v > 0) return v;
+    int n = 0;
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
+    g_sm_count[dev].store(n, std::memory_order_relaxed);
+    return n;
+}
+
+int simt_heads_per_block();
+
+namespace {
+
+struct Plan {
+    bool use_mma;
+    int heads_per_block;
+    int head_blocks;
+    int splits;
+    int chunk;
+    bool in_kernel_merge;
+    size_t ws_bytes;
+};
+
+int validate(const qsdpa_decode_params* p) {
+    if (!p) return set_error(QSDPA_ERR_INVALID, "qsdpa_decode: params is NULL");
+    if (p->bits != 4 && p->bits != 8) return set_error(QSDPA_ERR_INVALID, "bits must be 4 or 8, got %d", p->bits);
+    if (p->D <= 0 || p->D % 32) return set_error(QSDPA_ERR_INVALID, "D must be multiple of 32, got %d", p->D);
+    if (p->group_size != 32 && p->group_size != 64 && p->group_size != 128)
+        return set_error(QSDPA_ERR_INVALID, "group_size must be 32, 64 or 128, got %d", p->group_size);
+    if (p->D % p->group_size)
+        return set_error(QSDPA_ERR_INVALID, "D (%d) must be a multiple of group_size (%d)", p->D, p->group_size);
+    if (p->B <= 0 || p->Hq <= 0 || p->Hkv <= 0 || p->N < 0)
+        return set_error(QSDPA_ERR_INVALID, "bad sizes B=%d H_q=%d H_kv=%d N=%d", p->B, p->Hq, p->Hkv, p->N);
+    if (p->Hq % p->Hkv)
+        return set_error(QSDPA_ERR_INVALID, "H_q (%d) must be divisible by H_kv (%d)", p->Hq, p->Hkv);
+    if (p->dtype != QSDPA_F16 && p->dtype != QSDPA_BF16)
+        return set_error(QSDPA_ERR_INVALID, "dtype must be QSDPA_F16 or QSDPA_BF16, got %d", p->dtype);
+    if (p->mask_kind < QSDPA_MASK_NONE || p->mask_kind > QSDPA_MASK_ADD_F32)
+        return set_error(QSDPA_ERR_INVALID, "unknown mask kind %d", p->mask_kind);
+    if ((p->mask_kind != QSDPA_MASK_NONE) != (p->mask != nullptr))
+        return set_error(QSDPA_ERR_INVALID, "mask pointer and mask_kind disagree");
+    if ((p->k_biases == nullptr) != (p->v_biases == nullptr))
+        return set_error(QSDPA_ERR_INVALID, "pass both biases or neither (symmetric)");
+    if (p->out_mode != QSDPA_OUT_FINAL && p->out_mode != QSDPA_OUT_PARTIAL)
+        return set_error(QSDPA_ERR_INVALID, "unknown out_mode %d", p->out_mode);
+    if (!p->q || (p->N > 0 && (!p->k_packed || !p->v_packed || !p->k_scales || !p->v_scales)))
+        return set_error(QSDPA_ERR_INVALID, "qsdpa_decode: NULL tensor pointer");
+    if (p->out_mode == QSDPA_OUT_FINAL && !p->out) return set_error(QSDPA_ERR_INVALID, "out is NULL");
+    if (p->out_mode == QSDPA_OUT_PARTIAL && (!p->part_o || !p->part_ml))
+        return set_error(QSDPA_ERR_INVALID, "part_o / part_ml is NULL");
+    if (p->kv_start && !p->kv_len) return set_error(QSDPA_ERR_INVALID, "kv_start given without kv_len");
+    if (p->splits < 0 || p->splits > kMaxSplits)
+        return set_error(QSDPA_ERR_INVALID, "splits must be in [0, %d], got %d", kMaxSplits, p->splits);
+    if (p->D != 32 && p->D != 64 && p->D != 128 && p->D != 256)
+        return set_error(QSDPA_ERR_UNSUPPORTED, "fused decode supports D in {32, 64, 128, 256}, got %d", p->D);
+    return QSDPA_OK;
+}
+
+void fill_args(const qsdpa_decode_params* p, DecodeArgs& a) {
+    a.q = p->q;
+    a.q_sb = p->q_sb;
+    a.q_sh = p->q_sh;
+    a.kp = p->k_packed;
+    a.kp_sb = p->kp_sb;
+    a.kp_sh = p->kp_sh;
+    a.vp = p->v_packed;
+    a.vp_sb = p->vp_sb;
+    a.vp_sh = p->vp_sh;
+    a.ks = p->k_scales;
+    a.ks_sb = p->ks_sb;
+    a.ks_sh = p->ks_sh;
+    a.vs = p->v_scales;
+    a.vs_sb = p->vs_sb;
+    a.vs_sh = p->vs_sh;
+    a.kb = p->k_biases;
+    a.kb_sb = p->kb_sb;
+    a.kb_sh = p->kb_sh;
+    a.vb = p->v_biases;
+    a.vb_sb = p->vb_sb;
+    a.vb_sh = p->vb_sh;
+    a.mask = p->mask;
+    a.mask_kind = p->mask_kind;
+    a.m_sb = p->m_sb;
+    a.m_sh = p->m_sh;
+    a.kv_start = p->kv_start;
+    a.kv_len = p->kv_len;
+    a.out = p->out;
+    a.out_o = p->part_o;
+    a.out_ml = p->part_ml;
+    a.ws_o = nullptr;
+    a.ws_ml = nullptr;
+    a.counters = nullptr;
+    a.B = p->B;
+    a.Hq = p->Hq;
+    a.Hkv = p->Hkv;
+    a.N = p->N;
+    a.D = p->D;
+    a.bits = p->bits;
+    a.gs = p->group_size;
+    a.G = p->D / p->group_size;
+    a.pd = p->D * p->bits / 32;
+    a.gqa = p->Hq / p->Hkv;
+    a.out_mode = p->out_mode;
+    a.scale_log2 = p->scale * kLog2e;
+}
+
+Plan make_plan(const qsdpa_decode_params* p, const DecodeArgs& a) {
+    Plan pl;
+    pl.use_mma = mma_supported(a);
+    pl.heads_per_block = pl.use_mma ? mma_heads_per_block(a) : simt_heads_per_block();
+    pl.head_blocks = (a.gqa + pl.heads_per_block - 1) / pl.heads_per_block;
+    const int units = a.B * a.Hkv * pl.head_blocks;
+    int splits = p->splits;
+    if (splits == 0) {
+        // enough CTAs for ~2 waves on every SM, but no chunk below kMinChunk keys
+        const int per_sm = pl.use_mma ? 2 : 4;
+        const int target = sm_count() * per_sm * 2;
+        splits = (target + units - 1) / units;
+        const int by_len = (p->N + kMinChunk - 1) / kMinChunk;
+        if (splits > by_len) splits = by_len;
+        if (splits < 1) splits = 1;
+        if (splits > kMaxSplits) splits = kMaxSplits;
+    }
+    pl.splits = splits;
+    pl.chunk = p->N > 0 ? (p->N + splits - 1) / splits : 0;
+    pl.in_kernel_merge = (size_t)units * sizeof(unsigned) <= QSDPA_COUNTER_BYTES;
+    if (splits == 1) {
+        pl.ws_bytes = 0;
+    } else {
+        const size_t rows = (size_t)a.B * a.Hq;
+        pl.ws_bytes = QSDPA_COUNTER_BYTES + align256(rows * splits * a.D * sizeof(float)) +
+                      align256(rows * splits * 2 * sizeof(float));
+    }
+    return pl;
+}
+
+}  // namespace
+
+// Defaults until the tensor-core path is linked in (weak so the MMA
+// translation unit can override them).
+__attribute__((weak)) bool mma_supported(const DecodeArgs&) { return false; }
+__attribute__((weak)) int mma_heads_per_block(const DecodeArgs&) { return 16; }
+__attribute__((weak)) int launch_decode_mma(const DecodeArgs&, int, cudaStream_t) {
+    return set_error(QSDPA_ERR_UNSUPPORTED, "tensor-core decode path not built");
+}
+
+int launch_combine_strided(const float* po, const float* pml, int64_t so, int64_t sml, int64_t ro, int64_t rml,
+                           int parts, int rows, int D, void* out, int dtype, float* out_o, float* out_ml,
+                           cudaStream_t st);
+
+}  // namespace qsdpa
+
+using namespace qsdpa;
+
+extern "C" int qsdpa_decode_splits(const qsdpa_decode_params* p) {
+    int rc = validate(p);
+    if (rc) return rc;
+    DecodeArgs a;
+    fill_args(p, a);
+    return make_plan(p, a).splits;
+}
+
+extern "C" size_t qsdpa_decode_workspace_size(const qsdpa_decode_params* p) {
+    if (validate(p)) return 0;
+    DecodeArgs a;
+    fill_args(p, a);
+    return make_plan(p, a).ws_bytes;
+}
+
+extern "C" int qsdpa_decode(const qsdpa_decode_params* p, void* stream) {
+    int rc = validate(p);
+    if (rc) return rc;
+    DecodeArgs a;
+    fill_args(p, a);
+    const Plan pl = make_plan(p, a);
+    a.heads_per_block = pl.heads_per_block;
+    a.head_blocks = pl.head_blocks;
+    a.splits = pl.splits;
+    a.chunk = pl.chunk;
+    if (pl.ws_bytes) {
+        if (!p->workspace || p->workspace_bytes < pl.ws_bytes)
+            return set_error(QSDPA_ERR_WORKSPACE, "workspace of %zu bytes required, got %zu", pl.ws_bytes,
+                             p->workspace ? p->workspace_bytes : (size_t)0);
+        if ((uintptr_t)p->workspace % 256)
+            return set_error(QSDPA_ERR_WORKSPACE, "workspace must be 256-byte aligned");
+        char* ws = static_cast<char*>(p->workspace);
+        const size_t rows = (size_t)a.B * a.Hq;
+        a.counters = pl.in_kernel_merge ? reinterpret_cast<unsigned*>(ws) : nullptr;
+        a.ws_o = reinterpret_cast<float*>(ws + QSDPA_COUNTER_BYTES);
+        a.ws_ml = reinterpret_cast<float*>(ws + QSDPA_COUNTER_BYTES + align256(rows * pl.splits * a.D * sizeof(float)));
+    }
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    rc = pl.use_mma ? launch_decode_mma(a, p->dtype, st) : launch_decode_simt(a, p->dtype, st);
+    if (rc) return rc;
+    if (pl.splits > 1 && !pl.in_kernel_merge) {
+        // too many (unit, head block) pairs for the counter region: merge with
+        // a second launch over the (row, split, D) workspace layout
+        const int rows = a.B * a.Hq;
+        return launch_combine_strided(a.ws_o, a.ws_ml, a.D, 2, (int64_t)pl.splits * a.D, (int64_t)pl.splits * 2,
+                                      pl.splits, rows, a.D,
+                                      p->out_mode == QSDPA_OUT_FINAL ? p->out : nullptr, p->dtype,
+                                      p->out_mode == QSDPA_OUT_PARTIAL ? p->part_o : nullptr,
+                                      p->out_mode == QSDPA_OUT_PARTIAL ? p->part_ml : nullptr, st);
+    }
+    return QSDPA_OK;
+}
+
+extern "C" const char* qsdpa_last_error(void) { return g_last_error.c_str(); }
+
+extern "C" int qsdpa_abi_version(void) { return QSDPA_ABI_VERSION; }

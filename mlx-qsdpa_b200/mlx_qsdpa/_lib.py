@@ -1,0 +1,329 @@
+"""ctypes binding of libqsdpa.so (C ABI declared in include/qsdpa.h).
+
+This is the only module that talks to the native library.  Tensors cross the
+boundary as raw device pointers plus element strides; every call is enqueued
+on torch's current stream for the tensor's device.  There is no CPU or
+PyTorch fallback: if the library cannot be loaded or a call fails, a
+RuntimeError says why.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+import threading
+from typing import Optional, Tuple
+
+import torch
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.environ.get("QSDPA_LIB", os.path.join(_HERE, "libqsdpa.so"))
+
+QSDPA_F16, QSDPA_BF16 = 0, 1
+MASK_NONE, MASK_BOOL, MASK_ADD_F16, MASK_ADD_BF16, MASK_ADD_F32 = 0, 1, 2, 3, 4
+OUT_FINAL, OUT_PARTIAL = 0, 1
+COUNTER_BYTES = 65536
+
+_c_i32 = ctypes.c_int32
+_c_i64 = ctypes.c_int64
+_c_vp = ctypes.c_void_p
+
+
+class DecodeParams(ctypes.Structure):
+    """Mirror of ``qsdpa_decode_params``."""
+
+    _fields_ = [
+        ("q", _c_vp), ("q_sb", _c_i64), ("q_sh", _c_i64),
+        ("k_packed", _c_vp), ("kp_sb", _c_i64), ("kp_sh", _c_i64),
+        ("v_packed", _c_vp), ("vp_sb", _c_i64), ("vp_sh", _c_i64),
+        ("k_scales", _c_vp), ("ks_sb", _c_i64), ("ks_sh", _c_i64),
+        ("v_scales", _c_vp), ("vs_sb", _c_i64), ("vs_sh", _c_i64),
+        ("k_biases", _c_vp), ("kb_sb", _c_i64), ("kb_sh", _c_i64),
+        ("v_biases", _c_vp), ("vb_sb", _c_i64), ("vb_sh", _c_i64),
+        ("mask", _c_vp), ("mask_kind", _c_i32), ("m_sb", _c_i64), ("m_sh", _c_i64),
+        ("kv_start", _c_vp), ("kv_len", _c_vp),
+        ("out", _c_vp), ("part_o", _c_vp), ("part_ml", _c_vp),
+        ("workspace", _c_vp), ("workspace_bytes", ctypes.c_size_t),
+        ("B", _c_i32), ("Hq", _c_i32), ("Hkv", _c_i32), ("N", _c_i32), ("D", _c_i32),
+        ("bits", _c_i32), ("group_size", _c_i32), ("dtype", _c_i32),
+        ("scale", ctypes.c_float), ("splits", _c_i32), ("out_mode", _c_i32),
+    ]
+
+
+class QuantizeParams(ctypes.Structure):
+    """Mirror of ``qsdpa_quantize_params``."""
+
+    _fields_ = [
+        ("x", _c_vp), ("x_sb", _c_i64), ("x_sh", _c_i64), ("x_ss", _c_i64),
+        ("packed", _c_vp), ("p_sb", _c_i64), ("p_sh", _c_i64),
+        ("scales", _c_vp), ("s_sb", _c_i64), ("s_sh", _c_i64),
+        ("biases", _c_vp), ("b_sb", _c_i64), ("b_sh", _c_i64),
+        ("B", _c_i32), ("H", _c_i32), ("S", _c_i32), ("D", _c_i32),
+        ("bits", _c_i32), ("group_size", _c_i32), ("dtype", _c_i32),
+        ("slot0", _c_i64), ("cap", _c_i64), ("ring", _c_i32),
+    ]
+
+
+class DequantizeParams(ctypes.Structure):
+    """Mirror of ``qsdpa_dequantize_params``."""
+
+    _fields_ = [
+        ("packed", _c_vp), ("p_sb", _c_i64), ("p_sh", _c_i64),
+        ("scales", _c_vp), ("s_sb", _c_i64), ("s_sh", _c_i64),
+        ("biases", _c_vp), ("b_sb", _c_i64), ("b_sh", _c_i64),
+        ("out", _c_vp), ("o_sb", _c_i64), ("o_sh", _c_i64), ("o_ss", _c_i64),
+        ("B", _c_i32), ("H", _c_i32), ("n_out", _c_i32), ("D", _c_i32),
+        ("bits", _c_i32), ("group_size", _c_i32), ("dtype", _c_i32),
+        ("n_src", _c_i64), ("src_start", _c_i64), ("src_mod", _c_i64),
+    ]
+
+
+# Every function the C header declares (checked by the CPU test suite).
+EXPORTS = (
+    "qsdpa_decode", "qsdpa_decode_splits", "qsdpa_decode_workspace_size",
+    "qsdpa_combine", "qsdpa_quantize", "qsdpa_dequantize", "qsdpa_last_error",
+    "qsdpa_abi_version",
+)
+
+_lib = None
+_lib_lock = threading.Lock()
+
+
+def load() -> ctypes.CDLL:
+    """Load libqsdpa.so once (raises RuntimeError with the reason if absent)."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    with _lib_lock:
+        if _lib is not None:
+            return _lib
+        if not os.path.exists(LIB_PATH):
+            raise RuntimeError(
+                f"libqsdpa.so not found at {LIB_PATH}; build it with "
+                "`python mlx-qsdpa_b200/build.py` (nvcc, sm_100a)")
+        lib = ctypes.CDLL(LIB_PATH)
+        P = ctypes.POINTER
+        lib.qsdpa_decode.argtypes = [P(DecodeParams), _c_vp]
+        lib.qsdpa_decode.restype = ctypes.c_int
+        lib.qsdpa_decode_splits.argtypes = [P(DecodeParams)]
+        lib.qsdpa_decode_splits.restype = ctypes.c_int
+        lib.qsdpa_decode_workspace_size.argtypes = [P(DecodeParams)]
+        lib.qsdpa_decode_workspace_size.restype = ctypes.c_size_t
+        lib.qsdpa_combine.argtypes = [_c_vp, _c_vp, _c_i64, _c_i64, ctypes.c_int, ctypes.c_int,
+                                      ctypes.c_int, _c_vp, ctypes.c_int, _c_vp]
+        lib.qsdpa_combine.restype = ctypes.c_int
+        lib.qsdpa_quantize.argtypes = [P(QuantizeParams), _c_vp]
+        lib.qsdpa_quantize.restype = ctypes.c_int
+        lib.qsdpa_dequantize.argtypes = [P(DequantizeParams), _c_vp]
+        lib.qsdpa_dequantize.restype = ctypes.c_int
+        lib.qsdpa_last_error.argtypes = []
+        lib.qsdpa_last_error.restype = ctypes.c_char_p
+        lib.qsdpa_abi_version.argtypes = []
+        lib.qsdpa_abi_version.restype = ctypes.c_int
+        if lib.qsdpa_abi_version() != 1:
+            raise RuntimeError("libqsdpa.so ABI version mismatch")
+        _lib = lib
+        return lib
+
+
+def _check(rc: int, what: str):
+    if rc != 0:
+        msg = load().qsdpa_last_error().decode(errors="replace")
+        if rc == -2:
+            raise NotImplementedError(f"{what}: {msg}")
+        if rc == -1:
+            raise ValueError(f"{what}: {msg}")
+        raise RuntimeError(f"{what} failed ({rc}): {msg}")
+
+
+def dtype_code(dt: torch.dtype) -> int:
+    if dt == torch.float16:
+        return QSDPA_F16
+    if dt == torch.bfloat16:
+        return QSDPA_BF16
+    raise ValueError(f"unsupported dtype {dt}; expected float16 or bfloat16")
+
+
+def _ptr(t: Optional[torch.Tensor]) -> Optional[int]:
+    return None if t is None else t.data_ptr()
+
+
+def _stream(dev: torch.device) -> int:
+    return torch.cuda.current_stream(dev).cuda_stream
+
+
+def rows_contiguous(t: torch.Tensor) -> torch.Tensor:
+    """Return ``t`` (or a copy) whose last two dims are densely packed."""
+    if t.stride(-1) == 1 and (t.shape[-2] <= 1 or t.stride(-2) == t.shape[-1]):
+        return t
+    return t.contiguous()
+
+
+def _as_u32(t: torch.Tensor) -> torch.Tensor:
+    if t.dtype in (torch.uint32, torch.int32):
+        return t
+    raise ValueError(f"packed codes must be uint32, got {t.dtype}")
+
+
+# ------------------------------------------------------------ workspace ----
+_ws_cache: dict = {}
+_ws_lock = threading.Lock()
+
+
+def workspace(device: torch.device, nbytes: int) -> torch.Tensor:
+    """Per-(device, stream) zero-initialised decode workspace of >= nbytes.
+
+    The kernel leaves the counter region zero after every call, so the buffer
+    is zeroed only when it is (re)allocated.  Calls on one stream are ordered,
+    so sharing one workspace per stream is race-free.
+    """
+    key = (device.index, _stream(device))
+    with _ws_lock:
+        buf = _ws_cache.get(key)
+        if buf is None or buf.numel() < nbytes:
+            size = max(nbytes, 2 * (buf.numel() if buf is not None else 0), 1 << 20)
+            buf = torch.zeros(size + 256, dtype=torch.uint8, device=device)
+            _ws_cache[key] = buf
+        return buf
+
+
+def _aligned_ptr(buf: torch.Tensor) -> int:
+    p = buf.data_ptr()
+    return (p + 255) & ~255
+
+
+# ---------------------------------------------------------------- calls ----
+
+def decode(q: torch.Tensor, kp, vp, ks, vs, kb, vb, *, scale: float, bits: int, group_size: int,
+           mask: Optional[torch.Tensor] = None, mask_kind: int = MASK_NONE,
+           kv_start: Optional[torch.Tensor] = None, kv_len: Optional[torch.Tensor] = None,
+           splits: int = 0, out_mode: int = OUT_FINAL,
+           out: Optional[torch.Tensor] = None, part: Optional[Tuple[torch.Tensor, torch.Tensor]] = None):
+    """Fused decode through ``qsdpa_decode``.
+
+    q: (B, Hq, 1, D); kp/vp: (B, Hkv, N, pd) uint32; ks/vs/kb/vb: (B, Hkv, N, G).
+    mask (optional): 4-D (B|1, Hq|1, 1, N) with contiguous last dim.
+    Returns ``out`` (FINAL) or ``(part_o, part_ml)`` (PARTIAL).
+    """
+    lib = load()
+    B, Hq, qL, D = q.shape
+    _, Hkv, N, _ = kp.shape
+    dev = q.device
+    p = DecodeParams()
+    p.q = q.data_ptr(); p.q_sb = q.stride(0); p.q_sh = q.stride(1)
+    p.k_packed = kp.data_ptr(); p.kp_sb = kp.stride(0); p.kp_sh = kp.stride(1)
+    p.v_packed = vp.data_ptr(); p.vp_sb = vp.stride(0); p.vp_sh = vp.stride(1)
+    p.k_scales = ks.data_ptr(); p.ks_sb = ks.stride(0); p.ks_sh = ks.stride(1)
+    p.v_scales = vs.data_ptr(); p.vs_sb = vs.stride(0); p.vs_sh = vs.stride(1)
+    if kb is not None:
+        p.k_biases = kb.data_ptr(); p.kb_sb = kb.stride(0); p.kb_sh = kb.stride(1)
+        p.v_biases = vb.data_ptr(); p.vb_sb = vb.stride(0); p.vb_sh = vb.stride(1)
+    if mask is not None:
+        p.mask = mask.data_ptr(); p.mask_kind = mask_kind
+        p.m_sb = mask.stride(0) if mask.shape[0] > 1 else 0
+        p.m_sh = mask.stride(1) if mask.shape[1] > 1 else 0
+    if kv_len is not None:
+        p.kv_len = kv_len.data_ptr()
+        p.kv_start = _ptr(kv_start)
+    p.B, p.Hq, p.Hkv, p.N, p.D = B, Hq, Hkv, N, D
+    p.bits, p.group_size, p.dtype = bits, group_size, dtype_code(q.dtype)
+    p.scale = float(scale)
+    p.splits = int(splits)
+    p.out_mode = out_mode
+    if out_mode == OUT_FINAL:
+        if out is None:
+            out = torch.empty((B, Hq, 1, D), dtype=q.dtype, device=dev)
+        p.out = out.data_ptr()
+    else:
+        if part is None:
+            part = (torch.empty((B * Hq, D), dtype=torch.float32, device=dev),
+                    torch.empty((B * Hq, 2), dtype=torch.float32, device=dev))
+        p.part_o, p.part_ml = part[0].data_ptr(), part[1].data_ptr()
+    ref = ctypes.byref(p)
+    nbytes = lib.qsdpa_decode_workspace_size(ref)
+    if nbytes:
+        ws = workspace(dev, nbytes + 256)
+        p.workspace = _aligned_ptr(ws)
+        p.workspace_bytes = nbytes
+    _check(lib.qsdpa_decode(ref, _stream(dev)), "qsdpa_decode")
+    return out if out_mode == OUT_FINAL else part
+
+
+def decode_splits(q_shape, Hkv: int, N: int, D: int, bits: int, group_size: int, splits: int = 0) -> int:
+    """Split count the library would use (host-only query)."""
+    lib = load()
+    B, Hq = q_shape[0], q_shape[1]
+    p = DecodeParams()
+    p.q = 1; p.k_packed = 1; p.v_packed = 1; p.k_scales = 1; p.v_scales = 1; p.out = 1
+    p.B, p.Hq, p.Hkv, p.N, p.D = B, Hq, Hkv, N, D
+    p.bits, p.group_size, p.dtype, p.splits = bits, group_size, QSDPA_F16, splits
+    rc = lib.qsdpa_decode_splits(ctypes.byref(p))
+    _check(rc if rc < 0 else 0, "qsdpa_decode_splits")
+    return rc
+
+
+def quantize_into(x: torch.Tensor, packed: torch.Tensor, scales: torch.Tensor, biases: torch.Tensor,
+                  slot0: int, bits: int, group_size: int, ring: bool = False):
+    """Quantize x (B, H, S, D) into cache slots [slot0, slot0+S) (mod cap if ring)."""
+    lib = load()
+    if x.stride(-1) != 1:
+        x = x.contiguous()
+    B, H, S, D = x.shape
+    cap = packed.shape[2]
+    for t in (packed, scales, biases):
+        if t.stride(-1) != 1 or (t.shape[2] > 1 and t.stride(2) != t.shape[3]):
+            raise ValueError("cache buffers must have contiguous token rows")
+    p = QuantizeParams()
+    p.x = x.data_ptr(); p.x_sb, p.x_sh, p.x_ss = x.stride(0), x.stride(1), x.stride(2)
+    p.packed = packed.data_ptr(); p.p_sb, p.p_sh = packed.stride(0), packed.stride(1)
+    p.scales = scales.data_ptr(); p.s_sb, p.s_sh = scales.stride(0), scales.stride(1)
+    p.biases = biases.data_ptr(); p.b_sb, p.b_sh = biases.stride(0), biases.stride(1)
+    p.B, p.H, p.S, p.D = B, H, S, D
+    p.bits, p.group_size, p.dtype = bits, group_size, dtype_code(x.dtype)
+    p.slot0, p.cap, p.ring = int(slot0), int(cap), int(bool(ring))
+    _check(lib.qsdpa_quantize(ctypes.byref(p), _stream(x.device)), "qsdpa_quantize")
+
+
+def dequantize(packed: torch.Tensor, scales: torch.Tensor, biases: Optional[torch.Tensor],
+               bits: int, group_size: int, n_out: Optional[int] = None, src_start: int = 0,
+               src_mod: int = 0, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """Dequantize (B, H, N, pd) codes to (B, H, n_out, D) in the scales' dtype.
+
+    Output token i reads physical token (src_start + i) mod src_mod
+    (src_mod == 0: src_start + i).
+    """
+    lib = load()
+    packed = rows_contiguous(packed)
+    scales = rows_contiguous(scales)
+    if biases is not None:
+        biases = rows_contiguous(biases)
+    B, H, N, pd = packed.shape
+    D = pd * 32 // bits
+    if n_out is None:
+        n_out = N
+    if out is None:
+        out = torch.empty((B, H, n_out, D), dtype=scales.dtype, device=packed.device)
+    p = DequantizeParams()
+    p.packed = packed.data_ptr(); p.p_sb, p.p_sh = packed.stride(0), packed.stride(1)
+    p.scales = scales.data_ptr(); p.s_sb, p.s_sh = scales.stride(0), scales.stride(1)
+    if biases is not None:
+        p.biases = biases.data_ptr(); p.b_sb, p.b_sh = biases.stride(0), biases.stride(1)
+    p.out = out.data_ptr(); p.o_sb, p.o_sh, p.o_ss = out.stride(0), out.stride(1), out.stride(2)
+    p.B, p.H, p.n_out, p.D = B, H, n_out, D
+    p.bits, p.group_size, p.dtype = bits, group_size, dtype_code(scales.dtype)
+    p.n_src, p.src_start, p.src_mod = N, int(src_start), int(src_mod)
+    _check(lib.qsdpa_dequantize(ctypes.byref(p), _stream(packed.device)), "qsdpa_dequantize")
+    return out
+
+
+def combine(part_o: torch.Tensor, part_ml: torch.Tensor, dtype: torch.dtype) -> torch.Tensor:
+    """Merge gathered partial records: part_o (P, rows, D), part_ml (P, rows, 2)."""
+    lib = load()
+    P, rows, D = part_o.shape
+    part_o = part_o.contiguous()
+    part_ml = part_ml.contiguous()
+    out = torch.empty((rows, D), dtype=dtype, device=part_o.device)
+    rc = lib.qsdpa_combine(part_o.data_ptr(), part_ml.data_ptr(), rows * D, rows * 2, P, rows, D,
+                           out.data_ptr(), dtype_code(dtype), _stream(part_o.device))
+    _check(rc, "qsdpa_combine")
+    return out

@@ -1,0 +1,87 @@
+"""The C-ABI library loads and exports every symbol include/qsdpa.h declares,
+and the ctypes structures match the C layout (CPU only; no kernel calls)."""
+
+import ctypes
+import os
+import re
+import subprocess
+import sys
+
+import pytest
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+HEADER = os.path.join(ROOT, "include", "qsdpa.h")
+PKG = os.path.join(ROOT, "mlx-qsdpa_b200")
+
+
+def declared_functions():
+    src = open(HEADER).read()
+    src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
+    return sorted(set(re.findall(r"^\s*(?:const\s+)?\w[\w\s\*]*?\b(qsdpa_\w+)\s*\(", src, flags=re.M)))
+
+
+@pytest.fixture(scope="module")
+def lib_path():
+    sys.path.insert(0, PKG)
+    import build as b  # mlx-qsdpa_b200/build.py
+    if not os.path.exists(b.LIB):
+        b.build()
+    return b.LIB
+
+
+def test_header_declares_the_api():
+    fns = declared_functions()
+    assert "qsdpa_decode" in fns and "qsdpa_quantize" in fns and "qsdpa_last_error" in fns
+    from mlx_qsdpa import _lib
+    assert set(fns) == set(_lib.EXPORTS), (fns, _lib.EXPORTS)
+
+
+def test_library_exports_every_declared_symbol(lib_path):
+    lib = ctypes.CDLL(lib_path)
+    for fn in declared_functions():
+        assert hasattr(lib, fn), f"{fn} missing from {lib_path}"
+    lib.qsdpa_abi_version.restype = ctypes.c_int
+    assert lib.qsdpa_abi_version() == 1
+    lib.qsdpa_last_error.restype = ctypes.c_char_p
+    assert lib.qsdpa_last_error() == b""
+
+
+def test_invalid_args_rejected_without_gpu(lib_path):
+    """Argument validation runs on the host and returns an error code."""
+    from mlx_qsdpa import _lib
+    lib = _lib.load()
+    p = _lib.DecodeParams()
+    p.B, p.Hq, p.Hkv, p.N, p.D, p.bits, p.group_size = 1, 4, 3, 16, 128, 4, 32
+    p.q = p.k_packed = p.v_packed = p.k_scales = p.v_scales = p.out = 1
+    assert lib.qsdpa_decode(ctypes.byref(p), None) == -1
+    assert b"divisible" in lib.qsdpa_last_error()
+    p.Hkv, p.bits = 2, 5
+    assert lib.qsdpa_decode(ctypes.byref(p), None) == -1
+    p.bits, p.D = 4, 192
+    assert lib.qsdpa_decode(ctypes.byref(p), None) == -2
+    assert lib.qsdpa_quantize(None, None) == -1
+
+
+def test_struct_layout_matches_c(tmp_path):
+    """sizeof / offsetof of the C structs equal the ctypes mirrors."""
+    from mlx_qsdpa import _lib
+    src = tmp_path / "layout.c"
+    lines = ['#include <stdio.h>', '#include <stddef.h>', '#include "qsdpa.h"', 'int main(void){']
+    for cname, py in (("qsdpa_decode_params", _lib.DecodeParams),
+                      ("qsdpa_quantize_params", _lib.QuantizeParams),
+                      ("qsdpa_dequantize_params", _lib.DequantizeParams)):
+        lines.append(f'printf("{cname} %zu\\n", sizeof({cname}));')
+        for f, _ in py._fields_:
+            lines.append(f'printf("{cname}.{f} %zu\\n", offsetof({cname}, {f}));')
+    lines.append("return 0;}")
+    src.write_text("\n".join(lines))
+    exe = tmp_path / "layout"
+    subprocess.run(["gcc", "-I", os.path.join(ROOT, "include"), str(src), "-o", str(exe)], check=True)
+    got = dict(l.rsplit(" ", 1) for l in subprocess.run([str(exe)], capture_output=True, text=True,
+                                                         check=True).stdout.split("\n") if l)
+    for cname, py in (("qsdpa_decode_params", _lib.DecodeParams),
+                      ("qsdpa_quantize_params", _lib.QuantizeParams),
+                      ("qsdpa_dequantize_params", _lib.DequantizeParams)):
+        assert int(got[cname]) == ctypes.sizeof(py), cname
+        for f, _ in py._fields_:
+            assert int(got[f"{cname}.{f}"]) == getattr(py, f).offset, f"{cname}.{f}"
