@@ -23,6 +23,7 @@ std::atomic<int> g_sm_count[64];
 constexpr size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
 constexpr int kMaxSplits = 1024;
 constexpr int kMinChunk = 256;  // keys per CTA below which splitting stops paying
+constexpr int kMaxTicketSplits = 16;
 }  // namespace
 
 int set_error(int code, const char* fmt, ...) {
@@ -53,6 +54,7 @@ int sm_count() {
 }
 
 int simt_heads_per_block();
+int mma_tile();
 
 namespace {
 
@@ -157,18 +159,27 @@ Plan make_plan(const qsdpa_decode_params* p, const DecodeArgs& a) {
     const int units = a.B * a.Hkv * pl.head_blocks;
     int splits = p->splits;
     if (splits == 0) {
-        // enough CTAs for ~2 waves on every SM, but no chunk below kMinChunk keys
-        const int per_sm = pl.use_mma ? 2 : 4;
-        const int target = sm_count() * per_sm * 2;
+        // one full wave of resident CTAs (tensor-core kernel: 2 per SM; CUDA-core
+        // kernel: two waves of 4 per SM), but no chunk below kMinChunk keys
+        const int target = pl.use_mma ? sm_count() * 2 : sm_count() * 4 * 2;
         splits = (target + units - 1) / units;
         const int by_len = (p->N + kMinChunk - 1) / kMinChunk;
         if (splits > by_len) splits = by_len;
         if (splits < 1) splits = 1;
         if (splits > kMaxSplits) splits = kMaxSplits;
     }
-    pl.splits = splits;
     pl.chunk = p->N > 0 ? (p->N + splits - 1) / splits : 0;
-    pl.in_kernel_merge = (size_t)units * sizeof(unsigned) <= QSDPA_COUNTER_BYTES;
+    if (pl.use_mma && p->N > 0) {
+        // the tensor-core kernel walks whole 64-token tiles of physical keys
+        const int t = mma_tile();
+        pl.chunk = (pl.chunk + t - 1) / t * t;
+        splits = (p->N + pl.chunk - 1) / pl.chunk;
+    }
+    pl.splits = splits;
+    // the last-arriving CTA merges a handful of splits cheaply; beyond that a
+    // separate, fully parallel combine launch (programmatic dependent launch)
+    // is faster than one CTA walking every split record
+    pl.in_kernel_merge = splits <= kMaxTicketSplits && (size_t)units * sizeof(unsigned) <= QSDPA_COUNTER_BYTES;
     if (splits == 1) {
         pl.ws_bytes = 0;
     } else {
@@ -180,18 +191,6 @@ Plan make_plan(const qsdpa_decode_params* p, const DecodeArgs& a) {
 }
 
 }  // namespace
-
-// Defaults until the tensor-core path is linked in (weak so the MMA
-// translation unit can override them).
-__attribute__((weak)) bool mma_supported(const DecodeArgs&) { return false; }
-__attribute__((weak)) int mma_heads_per_block(const DecodeArgs&) { return 16; }
-__attribute__((weak)) int launch_decode_mma(const DecodeArgs&, int, cudaStream_t) {
-    return set_error(QSDPA_ERR_UNSUPPORTED, "tensor-core decode path not built");
-}
-
-int launch_combine_strided(const float* po, const float* pml, int64_t so, int64_t sml, int64_t ro, int64_t rml,
-                           int parts, int rows, int D, void* out, int dtype, float* out_o, float* out_ml,
-                           cudaStream_t st);
 
 }  // namespace qsdpa
 
@@ -238,14 +237,13 @@ extern "C" int qsdpa_decode(const qsdpa_decode_params* p, void* stream) {
     rc = pl.use_mma ? launch_decode_mma(a, p->dtype, st) : launch_decode_simt(a, p->dtype, st);
     if (rc) return rc;
     if (pl.splits > 1 && !pl.in_kernel_merge) {
-        // too many (unit, head block) pairs for the counter region: merge with
-        // a second launch over the (row, split, D) workspace layout
+        // merge the (row, split, D) workspace records with a second launch
         const int rows = a.B * a.Hq;
         return launch_combine_strided(a.ws_o, a.ws_ml, a.D, 2, (int64_t)pl.splits * a.D, (int64_t)pl.splits * 2,
                                       pl.splits, rows, a.D,
                                       p->out_mode == QSDPA_OUT_FINAL ? p->out : nullptr, p->dtype,
                                       p->out_mode == QSDPA_OUT_PARTIAL ? p->part_o : nullptr,
-                                      p->out_mode == QSDPA_OUT_PARTIAL ? p->part_ml : nullptr, st);
+                                      p->out_mode == QSDPA_OUT_PARTIAL ? p->part_ml : nullptr, true, st);
     }
     return QSDPA_OK;
 }

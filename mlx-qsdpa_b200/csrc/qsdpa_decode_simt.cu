@@ -166,9 +166,11 @@ __global__ void __launch_bounds__(kNW * 32) decode_simt_kernel(const DecodeArgs 
     }
     __syncthreads();
 
-    const int rows_per_cta = nh;
-    const int nsplit = a.splits;
-    for (int idx = threadIdx.x; idx < rows_per_cta * D; idx += blockDim.x) {
+    // merged record of this CTA's heads: [kHPW][D] + m + l, after the per-warp area
+    float* mo = s_l + kNW * kHPW;
+    float* mm = mo + kHPW * D;
+    float* ml = mm + kHPW;
+    for (int idx = threadIdx.x; idx < nh * D; idx += blockDim.x) {
         const int h = idx / D, d = idx - h * D;
         float mt = -INFINITY;
 #pragma unroll
@@ -180,69 +182,20 @@ __global__ void __launch_bounds__(kNW * 32) decode_simt_kernel(const DecodeArgs 
             lt += wt * s_l[w * kHPW + h];
             ot += wt * s_o[(w * kHPW + h) * D + d];
         }
-        const int row = b * a.Hq + kvh * a.gqa + h0 + h;
-        if (nsplit == 1) {
-            if (a.out_mode == QSDPA_OUT_FINAL) {
-                static_cast<T*>(a.out)[(int64_t)row * D + d] = Dt<T>::from_f(lt > 0.f ? ot / lt : 0.f);
-            } else {
-                a.out_o[(int64_t)row * D + d] = ot;
-                if (d == 0) {
-                    a.out_ml[2 * row] = mt;
-                    a.out_ml[2 * row + 1] = lt;
-                }
-            }
-        } else {
-            a.ws_o[((int64_t)row * nsplit + split) * D + d] = ot;
-            if (d == 0) {
-                a.ws_ml[((int64_t)row * nsplit + split) * 2] = mt;
-                a.ws_ml[((int64_t)row * nsplit + split) * 2 + 1] = lt;
-            }
+        mo[idx] = ot;
+        if (d == 0) {
+            mm[h] = mt;
+            ml[h] = lt;
         }
-    }
-    if (nsplit == 1 || a.counters == nullptr) return;
-
-    // ---- last CTA of this (unit, head block) merges the splits ----
-    __shared__ int s_last;
-    __threadfence();
-    __syncthreads();
-    if (threadIdx.x == 0) {
-        unsigned* ctr = a.counters + (unit * a.head_blocks + hblk);
-        const unsigned ticket = atomicAdd(ctr, 1u);
-        s_last = (ticket == (unsigned)nsplit - 1u);
-        if (s_last) *ctr = 0u;  // leave the counter zero for the next call
     }
     __syncthreads();
-    if (!s_last) return;
-    __threadfence();
-    for (int idx = threadIdx.x; idx < rows_per_cta * D; idx += blockDim.x) {
-        const int h = idx / D, d = idx - h * D;
-        const int row = b * a.Hq + kvh * a.gqa + h0 + h;
-        const float* rml = a.ws_ml + (int64_t)row * nsplit * 2;
-        const float* ro = a.ws_o + (int64_t)row * nsplit * D + d;
-        float mt = -INFINITY;
-        for (int sp = 0; sp < nsplit; ++sp) mt = fmaxf(mt, __ldcg(rml + 2 * sp));
-        float lt = 0.f, ot = 0.f;
-        for (int sp = 0; sp < nsplit; ++sp) {
-            const float wt = merge_weight(__ldcg(rml + 2 * sp), mt);
-            lt += wt * __ldcg(rml + 2 * sp + 1);
-            ot += wt * __ldcg(ro + (int64_t)sp * D);
-        }
-        if (a.out_mode == QSDPA_OUT_FINAL) {
-            static_cast<T*>(a.out)[(int64_t)row * D + d] = Dt<T>::from_f(lt > 0.f ? ot / lt : 0.f);
-        } else {
-            a.out_o[(int64_t)row * D + d] = ot;
-            if (d == 0) {
-                a.out_ml[2 * row] = mt;
-                a.out_ml[2 * row + 1] = lt;
-            }
-        }
-    }
+    finish_cta<T>(a, b, kvh, h0, nh, unit, hblk, split, mo, mm, ml);
 }
 
 template <typename T, int BITS, int DPL>
 int launch3(const DecodeArgs& a, cudaStream_t st) {
     dim3 grid(a.splits, a.B * a.Hkv, a.head_blocks);
-    const size_t smem = (size_t)kNW * kHPW * (a.D + 2) * sizeof(float);
+    const size_t smem = ((size_t)kNW * kHPW * (a.D + 2) + (size_t)kHPW * (a.D + 2)) * sizeof(float);
     auto kern = decode_simt_kernel<T, BITS, DPL>;
     if (smem > 48 * 1024) {
         cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);

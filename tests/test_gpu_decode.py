@@ -34,10 +34,19 @@ def run(qs, c: Case, **kw):
 
 
 def check(qs, c: Case, mask=None, **kw):
+    """Gate: the exact oracle within 2e-3 / 1e-2.  Diagnostic: the emulation
+    of the MLX fallback's intermediate roundings (q*scale, scores and
+    probabilities rounded to the dtype) drifts from the exact answer by itself
+    -- by more than 2e-3 for bf16 or large scores -- so the kernel must sit no
+    farther from it than that drift (plus the tolerance)."""
     out = run(qs, c, mask=mask, **kw)
-    e1 = assert_close(out, c.reference(mask=mask), what="vs exact")
-    e2 = assert_close(out, c.reference(mask=mask, mode="mlx"), what="vs mlx-rounded")
-    return out, max(e1, e2)
+    exact = c.reference(mask=mask)
+    e1 = assert_close(out, exact, what="vs exact")
+    mlx = c.reference(mask=mask, mode="mlx")
+    drift = float(np.abs(mlx - exact).max())
+    e2 = float(np.abs(out - mlx).max())
+    assert e2 <= drift + 2e-3, f"vs mlx-rounded: {e2:.3e} > drift {drift:.3e} + 2e-3"
+    return out, e1
 
 
 # ---- reference test shapes (B, Hq, Hkv, N, D) ----
@@ -260,3 +269,24 @@ def test_validation_errors(qs):
     q3 = to_torch(np.zeros((1, 3, 1, 128), np.float32), O.F16)
     with pytest.raises(ValueError, match="divisible"):
         qs.quantized_sdpa(q3, pk, pv, ks, vs)
+
+
+@pytest.mark.parametrize("dtype,bits,gs", [(O.F16, 4, 32), (O.BF16, 8, 64), (O.F16, 8, 128), (O.BF16, 4, 32)])
+def test_tensor_core_and_cuda_core_paths_agree(qs, dtype, bits, gs):
+    """Scales viewed from a buffer with an odd head stride are not 16-byte
+    aligned, which routes the call to the CUDA-core kernel; both kernels must
+    match the oracle and each other."""
+    c = Case(2, 32, 2, 777, 256, bits=bits, gs=gs, dtype=dtype, seed=61)
+    q, pk, pv, ks, vs, kb, vb = c.torch_args()
+
+    def odd(t):
+        big = torch.zeros((t.shape[0], t.shape[1], t.shape[2] + 1, t.shape[3]), dtype=t.dtype, device=t.device)
+        big[:, :, : t.shape[2]] = t
+        return big[:, :, : t.shape[2]]
+
+    fast = from_torch(qs.quantized_sdpa(q, pk, pv, ks, vs, kb, vb, bits=bits, group_size=gs, threshold=0))
+    slow = from_torch(qs.quantized_sdpa(q, pk, pv, odd(ks), odd(vs), odd(kb), odd(vb), bits=bits,
+                                        group_size=gs, threshold=0))
+    ref = c.reference()
+    assert_close(fast, ref, what="tensor-core path")
+    assert_close(slow, ref, what="cuda-core path")
