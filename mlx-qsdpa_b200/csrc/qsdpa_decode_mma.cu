@@ -59,12 +59,13 @@ __device__ __forceinline__ uint32_t smem_u32(const void* p) {
 
 __device__ __forceinline__ void cp_async16(void* smem, const void* gmem, int src_bytes) {
     asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(smem_u32(smem)), "l"(gmem),
-                 "r"(src_bytes));
+                 "r"(src_bytes)
+                 : "memory");
 }
-__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::); }
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
 template <int N>
 __device__ __forceinline__ void cp_async_wait() {
-    asm volatile("cp.async.wait_group %0;\n" ::"n"(N));
+    asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory");
 }
 
 __device__ __forceinline__ uint32_t lop3_or_and(uint32_t a, uint32_t b, uint32_t c) {
@@ -74,28 +75,12 @@ __device__ __forceinline__ uint32_t lop3_or_and(uint32_t a, uint32_t b, uint32_t
     return d;
 }
 
-__device__ __forceinline__ uint4 lds128(const void* p) {
-    uint4 v;
-    asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];\n"
-                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
-                 : "r"(smem_u32(p)));
-    return v;
-}
-__device__ __forceinline__ uint2 lds64(const void* p) {
-    uint2 v;
-    asm volatile("ld.shared.v2.u32 {%0, %1}, [%2];\n" : "=r"(v.x), "=r"(v.y) : "r"(smem_u32(p)));
-    return v;
-}
-__device__ __forceinline__ uint32_t lds32(const void* p) {
-    uint32_t v;
-    asm volatile("ld.shared.u32 %0, [%1];\n" : "=r"(v) : "r"(smem_u32(p)));
-    return v;
-}
-__device__ __forceinline__ uint16_t lds16(const void* p) {
-    uint16_t v;
-    asm volatile("ld.shared.u16 %0, [%1];\n" : "=h"(v) : "r"(smem_u32(p)));
-    return v;
-}
+// Plain C++ shared-memory loads: the compiler may schedule and combine them
+// (they are ordered against the cp.async waits by __syncthreads()).
+__device__ __forceinline__ uint4 lds128(const void* p) { return *reinterpret_cast<const uint4*>(p); }
+__device__ __forceinline__ uint2 lds64(const void* p) { return *reinterpret_cast<const uint2*>(p); }
+__device__ __forceinline__ uint32_t lds32(const void* p) { return *reinterpret_cast<const uint32_t*>(p); }
+__device__ __forceinline__ uint32_t lds16(const void* p) { return *reinterpret_cast<const uint16_t*>(p); }
 
 // --------------------------------------------- per-dtype register math --
 template <typename T>
@@ -103,6 +88,7 @@ struct Ops;
 
 template <>
 struct Ops<__half> {
+    static constexpr bool kSplitP = false;
     static __device__ __forceinline__ uint32_t fma2(uint32_t a, uint32_t b, uint32_t c) {
         uint32_t d;
         asm("fma.rn.f16x2 %0, %1, %2, %3;\n" : "=r"(d) : "r"(a), "r"(b), "r"(c));
@@ -132,7 +118,7 @@ struct Ops<__half> {
         c[1] = sub2(__byte_perm(w, 0x64646464u, 0x4342), 0x64006400u);
     }
     static __device__ __forceinline__ void mma(float d[4], const uint32_t a[4], uint32_t b0, uint32_t b1) {
-        asm volatile(
+        asm(
             "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
             "{%0,%1,%2,%3};\n"
             : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
@@ -142,6 +128,9 @@ struct Ops<__half> {
 
 template <>
 struct Ops<__nv_bfloat16> {
+    // bfloat16 probabilities carry 8 significant bits, too few for the 1e-2
+    // relative budget when V is far from zero-mean; P is fed as hi + lo parts
+    static constexpr bool kSplitP = true;
     static __device__ __forceinline__ uint32_t fma2(uint32_t a, uint32_t b, uint32_t c) {
         uint32_t d;
         asm("fma.rn.bf16x2 %0, %1, %2, %3;\n" : "=r"(d) : "r"(a), "r"(b), "r"(c));
@@ -175,7 +164,7 @@ struct Ops<__nv_bfloat16> {
         c[1] = pack(f2, f3);
     }
     static __device__ __forceinline__ void mma(float d[4], const uint32_t a[4], uint32_t b0, uint32_t b1) {
-        asm volatile(
+        asm(
             "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
             "{%0,%1,%2,%3};\n"
             : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
@@ -386,6 +375,23 @@ __global__ void __launch_bounds__(kThreads, 2) decode_mma_kernel(const DecodeArg
         float s[2][4];
 #pragma unroll
         for (int j = 0; j < 2; ++j) s[j][0] = s[j][1] = s[j][2] = s[j][3] = 0.f;
+        // scale/bias (dtype pairs {x, x}) of the groups in this thread's quarter
+        constexpr int QG = (D / 4 >= GS) ? (D / 4) / GS : 1;
+        uint32_t ksc[2][QG], kbi[2][QG];
+        {
+            const int gbase = (t4 * (D / 4)) / GS;
+#pragma unroll
+            for (int j = 0; j < 2; ++j) {
+                const int r = warp * 16 + j * 8 + g;
+#pragma unroll
+                for (int lg = 0; lg < QG; ++lg) {
+                    const uint32_t sv = lds16(s_ks + r * C::SROWB + (gbase + lg) * 2);
+                    const uint32_t bv = has_bias ? lds16(s_kb + r * C::SROWB + (gbase + lg) * 2) : 0u;
+                    ksc[j][lg] = sv | (sv << 16);
+                    kbi[j][lg] = bv | (bv << 16);
+                }
+            }
+        }
         constexpr int KWQ = C::KW >= 4 ? 4 : C::KW;  // words per shared load
 #pragma unroll
         for (int w0 = 0; w0 < C::KW; w0 += KWQ) {
@@ -393,8 +399,7 @@ __global__ void __launch_bounds__(kThreads, 2) decode_mma_kernel(const DecodeArg
 #pragma unroll
             for (int j = 0; j < 2; ++j) {
                 const int r = warp * 16 + j * 8 + g;
-                const int wi = t4 * C::KW + w0;  // word index in the row
-                const int byte = wi * 4;
+                const int byte = (t4 * C::KW + w0) * 4;  // word offset in the row
                 const char* p = s_kp + swz<C::CPR>(r, byte >> 4) * 16 + (byte & 15);
                 if constexpr (KWQ == 4) {
                     const uint4 v = lds128(p);
@@ -407,23 +412,14 @@ __global__ void __launch_bounds__(kThreads, 2) decode_mma_kernel(const DecodeArg
 #pragma unroll
             for (int u = 0; u < KWQ; ++u) {
                 const int wi = w0 + u;
-                const int grp = ((t4 * C::KW + wi) * C::EPW) / GS;
-                uint32_t sc2[2], bi2[2];
-#pragma unroll
-                for (int j = 0; j < 2; ++j) {
-                    const int r = warp * 16 + j * 8 + g;
-                    const uint32_t sv = lds16(s_ks + r * C::SROWB + grp * 2);
-                    const uint32_t bv = has_bias ? lds16(s_kb + r * C::SROWB + grp * 2) : 0u;
-                    sc2[j] = sv | (sv << 16);
-                    bi2[j] = bv | (bv << 16);
-                }
+                const int lg = (D / 4 >= GS) ? (wi * C::EPW) / GS : 0;
                 if constexpr (BITS == 4) {
                     uint32_t c[2][4];
 #pragma unroll
                     for (int j = 0; j < 2; ++j) {
                         Ops<T>::nib4(kw[j][u], c[j]);
 #pragma unroll
-                        for (int e = 0; e < 4; ++e) c[j][e] = Ops<T>::fma2(c[j][e], sc2[j], bi2[j]);
+                        for (int e = 0; e < 4; ++e) c[j][e] = Ops<T>::fma2(c[j][e], ksc[j][lg], kbi[j][lg]);
                     }
 #pragma unroll
                     for (int hs = 0; hs < 2; ++hs) {
@@ -439,7 +435,7 @@ __global__ void __launch_bounds__(kThreads, 2) decode_mma_kernel(const DecodeArg
                     for (int j = 0; j < 2; ++j) {
                         Ops<T>::byte2(kw[j][u], c[j]);
 #pragma unroll
-                        for (int e = 0; e < 2; ++e) c[j][e] = Ops<T>::fma2(c[j][e], sc2[j], bi2[j]);
+                        for (int e = 0; e < 2; ++e) c[j][e] = Ops<T>::fma2(c[j][e], ksc[j][lg], kbi[j][lg]);
                     }
                     const int kstep = wi;
                     const uint4 qa = lds128(sQ + (kstep * 32 + lane) * 16);
@@ -502,11 +498,40 @@ __global__ void __launch_bounds__(kThreads, 2) decode_mma_kernel(const DecodeArg
             l0 += p[j][0] + p[j][1];
             l1 += p[j][2] + p[j][3];
         }
-        const uint32_t pa[4] = {Ops<T>::pack(p[0][0], p[0][1]), Ops<T>::pack(p[0][2], p[0][3]),
-                                Ops<T>::pack(p[1][0], p[1][1]), Ops<T>::pack(p[1][2], p[1][3])};
+        uint32_t pa[4] = {Ops<T>::pack(p[0][0], p[0][1]), Ops<T>::pack(p[0][2], p[0][3]),
+                          Ops<T>::pack(p[1][0], p[1][1]), Ops<T>::pack(p[1][2], p[1][3])};
+        uint32_t pl[4] = {0u, 0u, 0u, 0u};
+        if constexpr (Ops<T>::kSplitP) {
+            // residual p - bf16(p), itself rounded to bf16
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const float lo_v = p[i >> 1][2 * (i & 1)] - __uint_as_float(pa[i] << 16);
+                const float hi_v = p[i >> 1][2 * (i & 1) + 1] - __uint_as_float(pa[i] & 0xffff0000u);
+                pl[i] = Ops<T>::pack(lo_v, hi_v);
+            }
+        }
 
         // ---------------- O += P V over the 16 tokens ---------------------
-        // B fragment rows (tokens): 2t4, 2t4+1 (b0b1) and 2t4+8, 2t4+9 (b2b3)
+        // B fragment rows (tokens): 2t4, 2t4+1 (b0b1) and 2t4+8, 2t4+9 (b2b3);
+        // scale/bias of the groups in this thread's eighth of the head dim,
+        // paired (token a, token b)
+        constexpr int VG = (D / 8 >= GS) ? (D / 8) / GS : 1;
+        uint32_t vsc[2][VG], vbi[2][VG];
+        {
+            const int gbase = (g * (D / 8)) / GS;
+#pragma unroll
+            for (int pr = 0; pr < 2; ++pr) {
+                const int ra = warp * 16 + 2 * t4 + pr * 8;
+#pragma unroll
+                for (int lg = 0; lg < VG; ++lg) {
+                    const int go = (gbase + lg) * 2;
+                    vsc[pr][lg] = lds16(s_vs + ra * C::SROWB + go) | (lds16(s_vs + (ra + 1) * C::SROWB + go) << 16);
+                    vbi[pr][lg] = has_bias ? (lds16(s_vb + ra * C::SROWB + go) |
+                                              (lds16(s_vb + (ra + 1) * C::SROWB + go) << 16))
+                                           : 0u;
+                }
+            }
+        }
         constexpr int VWQ = C::VW >= 4 ? 4 : C::VW;
 #pragma unroll
         for (int w0 = 0; w0 < C::VW; w0 += VWQ) {
@@ -529,22 +554,7 @@ __global__ void __launch_bounds__(kThreads, 2) decode_mma_kernel(const DecodeArg
 #pragma unroll
             for (int u = 0; u < VWQ; ++u) {
                 const int wi = w0 + u;
-                const int grp = ((g * C::VW + wi) * C::EPW) / GS;
-                uint32_t sc2[2], bi2[2];  // (token a, token b) pairs for rows (0,1) and (2,3)
-#pragma unroll
-                for (int pr = 0; pr < 2; ++pr) {
-                    const int ra = warp * 16 + 2 * t4 + pr * 8;
-                    const uint32_t sa = lds16(s_vs + ra * C::SROWB + grp * 2);
-                    const uint32_t sb = lds16(s_vs + (ra + 1) * C::SROWB + grp * 2);
-                    sc2[pr] = sa | (sb << 16);
-                    if (has_bias) {
-                        const uint32_t ba = lds16(s_vb + ra * C::SROWB + grp * 2);
-                        const uint32_t bb = lds16(s_vb + (ra + 1) * C::SROWB + grp * 2);
-                        bi2[pr] = ba | (bb << 16);
-                    } else {
-                        bi2[pr] = 0u;
-                    }
-                }
+                const int lg = (D / 8 >= GS) ? (wi * C::EPW) / GS : 0;
                 if constexpr (BITS == 4) {
                     uint32_t c[2][8];
 #pragma unroll
@@ -553,10 +563,13 @@ __global__ void __launch_bounds__(kThreads, 2) decode_mma_kernel(const DecodeArg
                         Ops<T>::nib4(__byte_perm(wa, wb, 0x5410), &c[pr][0]);
                         Ops<T>::nib4(__byte_perm(wa, wb, 0x7632), &c[pr][4]);
 #pragma unroll
-                        for (int e = 0; e < 8; ++e) c[pr][e] = Ops<T>::fma2(c[pr][e], sc2[pr], bi2[pr]);
+                        for (int e = 0; e < 8; ++e) c[pr][e] = Ops<T>::fma2(c[pr][e], vsc[pr][lg], vbi[pr][lg]);
                     }
 #pragma unroll
-                    for (int e = 0; e < 8; ++e) Ops<T>::mma(o[8 * wi + e], pa, c[0][e], c[1][e]);
+                    for (int e = 0; e < 8; ++e) {
+                        Ops<T>::mma(o[8 * wi + e], pa, c[0][e], c[1][e]);
+                        if constexpr (Ops<T>::kSplitP) Ops<T>::mma(o[8 * wi + e], pl, c[0][e], c[1][e]);
+                    }
                 } else {
                     uint32_t c[2][4];
 #pragma unroll
@@ -565,10 +578,13 @@ __global__ void __launch_bounds__(kThreads, 2) decode_mma_kernel(const DecodeArg
                         Ops<T>::byte2(__byte_perm(wa, wb, 0x5140), &c[pr][0]);
                         Ops<T>::byte2(__byte_perm(wa, wb, 0x7362), &c[pr][2]);
 #pragma unroll
-                        for (int e = 0; e < 4; ++e) c[pr][e] = Ops<T>::fma2(c[pr][e], sc2[pr], bi2[pr]);
+                        for (int e = 0; e < 4; ++e) c[pr][e] = Ops<T>::fma2(c[pr][e], vsc[pr][lg], vbi[pr][lg]);
                     }
 #pragma unroll
-                    for (int e = 0; e < 4; ++e) Ops<T>::mma(o[4 * wi + e], pa, c[0][e], c[1][e]);
+                    for (int e = 0; e < 4; ++e) {
+                        Ops<T>::mma(o[4 * wi + e], pa, c[0][e], c[1][e]);
+                        if constexpr (Ops<T>::kSplitP) Ops<T>::mma(o[4 * wi + e], pl, c[0][e], c[1][e]);
+                    }
                 }
             }
         }
