@@ -32,8 +32,6 @@ extern "C" {
 
 #define QSDPA_ABI_VERSION 1
 
-/* size of the counter region at the start of a decode workspace */
-#define QSDPA_COUNTER_BYTES 65536
 
 /* element types */
 enum { QSDPA_F16 = 0, QSDPA_BF16 = 1 };
@@ -80,7 +78,8 @@ enum {
  * mlx_qsdpa/kernels.py:42-161, 224-319, 342-419).  One launch: each CTA
  * handles one KV head of one batch row and a contiguous chunk of its keys for
  * all the query heads of that GQA group; when the keys are split over several
- * CTAs the last CTA of each group merges the partials (no second launch).
+ * CTAs a second kernel, launched as a programmatic dependent on the same
+ * stream, merges the partial records.
  */
 typedef struct qsdpa_decode_params {
     /* query (B, H_q, 1, D), dtype `dtype`, element strides for b and h */
@@ -118,10 +117,10 @@ typedef struct qsdpa_decode_params {
     void* out;
     float* part_o;
     float* part_ml;
-    /* scratch of qsdpa_decode_workspace_size() bytes, 256-byte aligned.  Its
-     * first QSDPA_COUNTER_BYTES bytes are split-K arrival counters: zero them
-     * once when the workspace is created; every call leaves them zero again.
-     * Calls that run concurrently must use different workspaces. */
+    /* scratch for the split-K partial records: qsdpa_decode_workspace_size()
+     * bytes, 256-byte aligned, no initialisation needed (0 bytes when the
+     * keys are not split).  Calls that run concurrently must use different
+     * workspaces. */
     void* workspace;
     size_t workspace_bytes;
     int32_t B, Hq, Hkv, N, D;

@@ -23,7 +23,6 @@ std::atomic<int> g_sm_count[64];
 constexpr size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
 constexpr int kMaxSplits = 1024;
 constexpr int kMinChunk = 256;  // keys per CTA below which splitting stops paying
-constexpr int kMaxTicketSplits = 16;
 }  // namespace
 
 int set_error(int code, const char* fmt, ...) {
@@ -64,7 +63,6 @@ struct Plan {
     int head_blocks;
     int splits;
     int chunk;
-    bool in_kernel_merge;
     size_t ws_bytes;
 };
 
@@ -136,7 +134,6 @@ void fill_args(const qsdpa_decode_params* p, DecodeArgs& a) {
     a.out_ml = p->part_ml;
     a.ws_o = nullptr;
     a.ws_ml = nullptr;
-    a.counters = nullptr;
     a.B = p->B;
     a.Hq = p->Hq;
     a.Hkv = p->Hkv;
@@ -159,9 +156,9 @@ Plan make_plan(const qsdpa_decode_params* p, const DecodeArgs& a) {
     const int units = a.B * a.Hkv * pl.head_blocks;
     int splits = p->splits;
     if (splits == 0) {
-        // one full wave of resident CTAs (tensor-core kernel: 2 per SM; CUDA-core
+        // one full wave of resident CTAs (tensor-core kernel: 3 per SM; CUDA-core
         // kernel: two waves of 4 per SM), but no chunk below kMinChunk keys
-        const int target = pl.use_mma ? sm_count() * 2 : sm_count() * 4 * 2;
+        const int target = pl.use_mma ? sm_count() * 3 : sm_count() * 4 * 2;
         splits = (target + units - 1) / units;
         const int by_len = (p->N + kMinChunk - 1) / kMinChunk;
         if (splits > by_len) splits = by_len;
@@ -176,16 +173,11 @@ Plan make_plan(const qsdpa_decode_params* p, const DecodeArgs& a) {
         splits = (p->N + pl.chunk - 1) / pl.chunk;
     }
     pl.splits = splits;
-    // the last-arriving CTA merges a handful of splits cheaply; beyond that a
-    // separate, fully parallel combine launch (programmatic dependent launch)
-    // is faster than one CTA walking every split record
-    pl.in_kernel_merge = splits <= kMaxTicketSplits && (size_t)units * sizeof(unsigned) <= QSDPA_COUNTER_BYTES;
     if (splits == 1) {
         pl.ws_bytes = 0;
     } else {
         const size_t rows = (size_t)a.B * a.Hq;
-        pl.ws_bytes = QSDPA_COUNTER_BYTES + align256(rows * splits * a.D * sizeof(float)) +
-                      align256(rows * splits * 2 * sizeof(float));
+        pl.ws_bytes = align256(rows * splits * a.D * sizeof(float)) + align256(rows * splits * 2 * sizeof(float));
     }
     return pl;
 }
@@ -229,14 +221,13 @@ extern "C" int qsdpa_decode(const qsdpa_decode_params* p, void* stream) {
             return set_error(QSDPA_ERR_WORKSPACE, "workspace must be 256-byte aligned");
         char* ws = static_cast<char*>(p->workspace);
         const size_t rows = (size_t)a.B * a.Hq;
-        a.counters = pl.in_kernel_merge ? reinterpret_cast<unsigned*>(ws) : nullptr;
-        a.ws_o = reinterpret_cast<float*>(ws + QSDPA_COUNTER_BYTES);
-        a.ws_ml = reinterpret_cast<float*>(ws + QSDPA_COUNTER_BYTES + align256(rows * pl.splits * a.D * sizeof(float)));
+        a.ws_o = reinterpret_cast<float*>(ws);
+        a.ws_ml = reinterpret_cast<float*>(ws + align256(rows * pl.splits * a.D * sizeof(float)));
     }
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     rc = pl.use_mma ? launch_decode_mma(a, p->dtype, st) : launch_decode_simt(a, p->dtype, st);
     if (rc) return rc;
-    if (pl.splits > 1 && !pl.in_kernel_merge) {
+    if (pl.splits > 1) {
         // merge the (row, split, D) workspace records with a second launch
         const int rows = a.B * a.Hq;
         return launch_combine_strided(a.ws_o, a.ws_ml, a.D, 2, (int64_t)pl.splits * a.D, (int64_t)pl.splits * 2,

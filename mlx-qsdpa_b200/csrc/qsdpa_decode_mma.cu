@@ -48,6 +48,7 @@ namespace qsdpa {
 namespace {
 
 constexpr int kWarps = 4;
+constexpr int kPairs = kWarps / 2;
 constexpr int kThreads = kWarps * 32;
 constexpr int kTile = 64;  // tokens per stage
 constexpr int kRescaleLog2 = 8;
@@ -66,6 +67,19 @@ __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commi
 template <int N>
 __device__ __forceinline__ void cp_async_wait() {
     asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory");
+}
+
+// Barrier among `count` threads (a warp pair) on hardware barrier `id` (>= 1).
+__device__ __forceinline__ void named_barrier(int id, int count) {
+    asm volatile("bar.sync %0, %1;\n" ::"r"(id), "r"(count) : "memory");
+}
+
+// 2^x on the MUFU unit (flushes results below 2^-126 to zero, which only
+// touches probabilities far below the fp16/bf16 resolution of P)
+__device__ __forceinline__ float ex2(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;\n" : "=f"(y) : "f"(x));
+    return y;
 }
 
 __device__ __forceinline__ uint32_t lop3_or_and(uint32_t a, uint32_t b, uint32_t c) {
@@ -189,15 +203,21 @@ struct Cfg {
     static constexpr int SC_BYTES = kTile * SROWB;
     static constexpr int STAGE_BYTES = 2 * PACK_BYTES + 4 * SC_BYTES;
     static constexpr int Q_BYTES = KSTEPS * 32 * 16;
-    // deepest ring (2..4 stages) that keeps a CTA within ~100 KB so two CTAs
+    static constexpr int XP_BYTES = kPairs * 2 * 2 * 32 * 16;  // P fragments (hi, lo) per warp
+    static constexpr int X_BYTES = XP_BYTES + kPairs * 2 * 16 * 4;
+    // end-of-chunk merge area: per-pair O (16 x D fp32) + m, l; then merged
+    static constexpr int MERGE_BYTES = kPairs * 16 * D * 4 + kPairs * 3 * 16 * 4 + 16 * (D + 2) * 4;
+    // deepest ring (2..4 stages) that keeps a CTA within ~74 KB so three CTAs
     // share an SM
-    static constexpr int STAGES_FIT = (100 * 1024 - Q_BYTES) / STAGE_BYTES;
+    static constexpr int STAGES_FIT = (74 * 1024 - Q_BYTES - X_BYTES) / STAGE_BYTES;
     static constexpr int STAGES = STAGES_FIT > 4 ? 4 : (STAGES_FIT < 2 ? 2 : STAGES_FIT);
-    static constexpr int RING_BYTES = STAGES * STAGE_BYTES;
-    // end-of-chunk merge area: per-warp O (16 x D fp32) + m, l; then merged
-    static constexpr int MERGE_BYTES = kWarps * 16 * (D + 2) * 4 + 16 * (D + 2) * 4;
-    static constexpr int SMEM = (RING_BYTES > MERGE_BYTES ? RING_BYTES : MERGE_BYTES) + Q_BYTES;
+    static constexpr int RING_RAW = STAGES * STAGE_BYTES;
+    static constexpr int RING_BYTES = RING_RAW > MERGE_BYTES ? RING_RAW : MERGE_BYTES;
+    static constexpr int SMEM = RING_BYTES + Q_BYTES + X_BYTES;
+    static constexpr int MIN_BLOCKS = SMEM <= 75 * 1024 ? 3 : 2;
     static_assert(CPR >= 2, "packed rows must span at least two 16-byte chunks");
+    static_assert(STAGE_BYTES >= 16 * D * 2, "the Q staging area must fit in one stage");
+    static_assert(PD % 2 == 0 && VW % 2 == 0, "the head dim must split into two halves of whole words");
 };
 
 // XOR-128B swizzle of 16-byte chunk (row r, chunk c) inside a stage's packed
@@ -246,11 +266,12 @@ struct Window {
 };
 
 template <typename T, int BITS, int D, int GS>
-__global__ void __launch_bounds__(kThreads, 2) decode_mma_kernel(const DecodeArgs a) {
+__global__ void __launch_bounds__(kThreads, (Cfg<BITS, D, GS>::MIN_BLOCKS)) decode_mma_kernel(const DecodeArgs a) {
     using C = Cfg<BITS, D, GS>;
     extern __shared__ __align__(128) char smem[];
     char* ring = smem;
-    char* sQ = smem + (C::RING_BYTES > C::MERGE_BYTES ? C::RING_BYTES : C::MERGE_BYTES);
+    char* sQ = smem + C::RING_BYTES;   // Q fragments
+    char* sX = sQ + C::Q_BYTES;        // pair exchange: P fragments + row maxima
 
     const int split = blockIdx.x;
     const int unit = blockIdx.y;
@@ -264,6 +285,8 @@ __global__ void __launch_bounds__(kThreads, 2) decode_mma_kernel(const DecodeArg
     const int lane = tid & 31;
     const int g = lane >> 2;
     const int t4 = lane & 3;
+    const int pair = warp >> 1;  // warps 2p, 2p+1 share 32 tokens of each tile
+    const int role = warp & 1;   // QK on tokens [16*role, +16) of the pair; PV on head-dim half `role`
 
     Window win;
     key_window(a, b, win.start, win.len);
@@ -284,20 +307,34 @@ __global__ void __launch_bounds__(kThreads, 2) decode_mma_kernel(const DecodeArg
     const char* vb = has_bias ? static_cast<const char*>(a.vb) + ((int64_t)b * a.vb_sb + (int64_t)kvh * a.vb_sh) * 2
                               : nullptr;
 
-    // ---- stage loader: tile starting at physical token p0 ----
+    // Per-thread copy plan, fixed for the whole chunk: thread tid copies
+    // packed chunks i = tid + k*kThreads (row i / CPR, chunk i % CPR) of every
+    // tile; only the tile's base token changes between tiles.
+    constexpr int KCP = (kTile * C::CPR + kThreads - 1) / kThreads;
+    int cp_row[KCP], cp_dst[KCP], cp_src[KCP];
+#pragma unroll
+    for (int k = 0; k < KCP; ++k) {
+        const int i = tid + k * kThreads;
+        const int r = i / C::CPR, c = i - r * C::CPR;
+        cp_row[k] = i < kTile * C::CPR ? r : kTile;  // kTile: no copy
+        cp_dst[k] = swz<C::CPR>(r, c) * 16;
+        cp_src[k] = r * C::ROWB + c * 16;
+    }
+    const char* kp_b = reinterpret_cast<const char*>(kp);
+    const char* vp_b = reinterpret_cast<const char*>(vp);
     auto load_tile = [&](int tile, int stage) {
         const int p0 = p_lo + tile * kTile;
         if (!win.overlaps(p0, min(p0 + kTile, p_hi))) return;  // skipped tile: nothing to load
         char* st = ring + stage * C::STAGE_BYTES;
         const int rows_valid = min(kTile, a.N - p0);
+        const int64_t tile_off = (int64_t)p0 * C::ROWB;
 #pragma unroll
-        for (int i = tid; i < kTile * C::CPR; i += kThreads) {
-            const int r = i / C::CPR, c = i - r * C::CPR;
-            const bool ok = r < rows_valid;
-            const int64_t off = (int64_t)(ok ? p0 + r : 0) * C::PD + c * 4;
-            const int dst = swz<C::CPR>(r, c) * 16;
-            cp_async16(st + dst, kp + off, ok ? 16 : 0);
-            cp_async16(st + C::PACK_BYTES + dst, vp + off, ok ? 16 : 0);
+        for (int k = 0; k < KCP; ++k) {
+            if (cp_row[k] >= kTile) continue;
+            const bool ok = cp_row[k] < rows_valid;
+            const int64_t off = ok ? tile_off + cp_src[k] : 0;
+            cp_async16(st + cp_dst[k], kp_b + off, ok ? 16 : 0);
+            cp_async16(st + C::PACK_BYTES + cp_dst[k], vp_b + off, ok ? 16 : 0);
         }
         const int sbytes = rows_valid * C::SROWB;
         char* s_ks = st + 2 * C::PACK_BYTES;
@@ -321,36 +358,53 @@ __global__ void __launch_bounds__(kThreads, 2) decode_mma_kernel(const DecodeArg
         cp_async_commit();
     }
 
-    // ---- Q fragments (A operand of S = Q K^T), permuted like K, in smem ----
-    for (int idx = tid; idx < C::KSTEPS * 32; idx += kThreads) {
-        const int kstep = idx >> 5, ln = idx & 31;
-        const int qg = ln >> 2, qt = ln & 3;
+    // ---- Q fragments (A operand of S = Q K^T), permuted like K ----
+    // The 16 query rows are first staged (coalesced) in the ring's last stage,
+    // which the prologue leaves untouched, then gathered into per-lane
+    // fragment order.
+    {
+        T* qst = reinterpret_cast<T*>(ring + (C::STAGES - 1) * C::STAGE_BYTES);
         const T* q = static_cast<const T*>(a.q) + (int64_t)b * a.q_sb;
-        const int hq0 = kvh * a.gqa + h0 + qg, hq1 = hq0 + 8;
-        uint16_t v[2][4];
-#pragma unroll
-        for (int s = 0; s < 4; ++s) {
-            const int dim = k_dim<BITS, D>(kstep, qt, s);
-            T x0 = qg < nh ? q[(int64_t)hq0 * a.q_sh + dim] : Dt<T>::from_f(0.f);
-            T x1 = qg + 8 < nh ? q[(int64_t)hq1 * a.q_sh + dim] : Dt<T>::from_f(0.f);
-            memcpy(&v[0][s], &x0, 2);
-            memcpy(&v[1][s], &x1, 2);
+        for (int i = tid; i < 16 * D; i += kThreads) {
+            const int h = i / D, d = i - h * D;
+            qst[i] = h < nh ? q[(int64_t)(kvh * a.gqa + h0 + h) * a.q_sh + d] : Dt<T>::from_f(0.f);
         }
-        uint4 f;
-        f.x = v[0][0] | ((uint32_t)v[0][1] << 16);  // row g,   slots 2t4, 2t4+1
-        f.y = v[1][0] | ((uint32_t)v[1][1] << 16);  // row g+8, slots 2t4, 2t4+1
-        f.z = v[0][2] | ((uint32_t)v[0][3] << 16);  // row g,   slots 2t4+8, 2t4+9
-        f.w = v[1][2] | ((uint32_t)v[1][3] << 16);  // row g+8, slots 2t4+8, 2t4+9
-        *reinterpret_cast<uint4*>(sQ + idx * 16) = f;
+        __syncthreads();
+        const uint16_t* q16 = reinterpret_cast<const uint16_t*>(qst);
+        for (int idx = tid; idx < C::KSTEPS * 32; idx += kThreads) {
+            const int kstep = idx >> 5, ln = idx & 31;
+            const int qg = ln >> 2, qt = ln & 3;
+            uint32_t v[2][4];
+#pragma unroll
+            for (int s = 0; s < 4; ++s) {
+                const int dim = k_dim<BITS, D>(kstep, qt, s);
+                v[0][s] = q16[qg * D + dim];
+                v[1][s] = q16[(qg + 8) * D + dim];
+            }
+            uint4 f;
+            f.x = v[0][0] | (v[0][1] << 16);  // row g,   slots 2t4, 2t4+1
+            f.y = v[1][0] | (v[1][1] << 16);  // row g+8, slots 2t4, 2t4+1
+            f.z = v[0][2] | (v[0][3] << 16);  // row g,   slots 2t4+8, 2t4+9
+            f.w = v[1][2] | (v[1][3] << 16);  // row g+8, slots 2t4+8, 2t4+9
+            *reinterpret_cast<uint4*>(sQ + idx * 16) = f;
+        }
+        // the first loop iteration's __syncthreads orders these writes (and the
+        // reads of the staging area) before anything reuses the last stage
     }
 
-    float o[C::NT][4];
+    constexpr int NTH = C::NT / 2;  // n8 tiles of this warp's head-dim half
+    float o[NTH][4];
 #pragma unroll
-    for (int j = 0; j < C::NT; ++j) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.f;
-    float m0 = -INFINITY, m1 = -INFINITY;  // rows g and g+8 (log2 domain)
-    float l0 = 0.f, l1 = 0.f;              // this thread's partial sums
+    for (int j = 0; j < NTH; ++j) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.f;
+    float m0 = -INFINITY, m1 = -INFINITY;  // rows g and g+8 (log2 domain), shared by the pair
+    float l0 = 0.f, l1 = 0.f;              // partial sums over this warp's QK tokens
     const int hq_g = kvh * a.gqa + h0 + g;
     const int64_t mrow = a.mask ? (int64_t)b * a.m_sb : 0;
+
+    // pair exchange area: P fragments [pair][role][hi/lo][lane] (16 B each) + row maxima
+    uint4* xP = reinterpret_cast<uint4*>(sX);
+    float* xM = reinterpret_cast<float*>(sX + C::XP_BYTES);  // [pair][role][16]
+    const int bar_id = 1 + pair;
 
     for (int tile = 0; tile < ntiles; ++tile) {
         cp_async_wait<C::STAGES - 2>();
@@ -361,8 +415,9 @@ __global__ void __launch_bounds__(kThreads, 2) decode_mma_kernel(const DecodeArg
             cp_async_commit();
         }
         const int p0 = p_lo + tile * kTile;
-        const int wp0 = p0 + warp * 16;  // this warp's 16 tokens
-        if (!win.overlaps(wp0, min(wp0 + 16, p_hi))) continue;
+        const int pp0 = p0 + pair * 32;       // the pair's 32 tokens
+        const int wp0 = pp0 + role * 16;      // this warp's 16 QK tokens
+        if (!win.overlaps(pp0, min(pp0 + 32, p_hi))) continue;  // uniform across the pair
         const char* st = ring + (tile % C::STAGES) * C::STAGE_BYTES;
         const char* s_kp = st;
         const char* s_vp = st + C::PACK_BYTES;
@@ -370,19 +425,22 @@ __global__ void __launch_bounds__(kThreads, 2) decode_mma_kernel(const DecodeArg
         const char* s_kb = s_ks + C::SC_BYTES;
         const char* s_vs = s_ks + 2 * C::SC_BYTES;
         const char* s_vb = s_ks + 3 * C::SC_BYTES;
+        const int r0 = pair * 32 + role * 16;  // this warp's QK rows in the stage
 
         // ---------------- S = Q K^T for 16 tokens (two n8 tiles) ----------
-        float s[2][4];
+        // four accumulator chains (token tile j x word parity) for MMA ILP
+        float sacc[2][2][4];
 #pragma unroll
-        for (int j = 0; j < 2; ++j) s[j][0] = s[j][1] = s[j][2] = s[j][3] = 0.f;
-        // scale/bias (dtype pairs {x, x}) of the groups in this thread's quarter
+        for (int c2 = 0; c2 < 2; ++c2)
+#pragma unroll
+            for (int j = 0; j < 2; ++j) sacc[c2][j][0] = sacc[c2][j][1] = sacc[c2][j][2] = sacc[c2][j][3] = 0.f;
         constexpr int QG = (D / 4 >= GS) ? (D / 4) / GS : 1;
         uint32_t ksc[2][QG], kbi[2][QG];
         {
             const int gbase = (t4 * (D / 4)) / GS;
 #pragma unroll
             for (int j = 0; j < 2; ++j) {
-                const int r = warp * 16 + j * 8 + g;
+                const int r = r0 + j * 8 + g;
 #pragma unroll
                 for (int lg = 0; lg < QG; ++lg) {
                     const uint32_t sv = lds16(s_ks + r * C::SROWB + (gbase + lg) * 2);
@@ -398,8 +456,8 @@ __global__ void __launch_bounds__(kThreads, 2) decode_mma_kernel(const DecodeArg
             uint32_t kw[2][KWQ];
 #pragma unroll
             for (int j = 0; j < 2; ++j) {
-                const int r = warp * 16 + j * 8 + g;
-                const int byte = (t4 * C::KW + w0) * 4;  // word offset in the row
+                const int r = r0 + j * 8 + g;
+                const int byte = (t4 * C::KW + w0) * 4;
                 const char* p = s_kp + swz<C::CPR>(r, byte >> 4) * 16 + (byte & 15);
                 if constexpr (KWQ == 4) {
                     const uint4 v = lds128(p);
@@ -413,6 +471,7 @@ __global__ void __launch_bounds__(kThreads, 2) decode_mma_kernel(const DecodeArg
             for (int u = 0; u < KWQ; ++u) {
                 const int wi = w0 + u;
                 const int lg = (D / 4 >= GS) ? (wi * C::EPW) / GS : 0;
+                const int ch = wi & 1;
                 if constexpr (BITS == 4) {
                     uint32_t c[2][4];
 #pragma unroll
@@ -427,7 +486,7 @@ __global__ void __launch_bounds__(kThreads, 2) decode_mma_kernel(const DecodeArg
                         const uint4 qa = lds128(sQ + (kstep * 32 + lane) * 16);
                         const uint32_t af[4] = {qa.x, qa.y, qa.z, qa.w};
 #pragma unroll
-                        for (int j = 0; j < 2; ++j) Ops<T>::mma(s[j], af, c[j][2 * hs], c[j][2 * hs + 1]);
+                        for (int j = 0; j < 2; ++j) Ops<T>::mma(sacc[ch][j], af, c[j][2 * hs], c[j][2 * hs + 1]);
                     }
                 } else {
                     uint32_t c[2][2];
@@ -437,49 +496,67 @@ __global__ void __launch_bounds__(kThreads, 2) decode_mma_kernel(const DecodeArg
 #pragma unroll
                         for (int e = 0; e < 2; ++e) c[j][e] = Ops<T>::fma2(c[j][e], ksc[j][lg], kbi[j][lg]);
                     }
-                    const int kstep = wi;
-                    const uint4 qa = lds128(sQ + (kstep * 32 + lane) * 16);
+                    const uint4 qa = lds128(sQ + (wi * 32 + lane) * 16);
                     const uint32_t af[4] = {qa.x, qa.y, qa.z, qa.w};
 #pragma unroll
-                    for (int j = 0; j < 2; ++j) Ops<T>::mma(s[j], af, c[j][0], c[j][1]);
+                    for (int j = 0; j < 2; ++j) Ops<T>::mma(sacc[ch][j], af, c[j][0], c[j][1]);
+                }
+            }
+        }
+        float s[2][4];
+#pragma unroll
+        for (int j = 0; j < 2; ++j)
+#pragma unroll
+            for (int e = 0; e < 4; ++e) s[j][e] = (sacc[0][j][e] + sacc[1][j][e]) * a.scale_log2;
+
+        // ---------------- masking (s[j][e]: token wp0 + 8j + 2t4 + (e&1), row g + 8*(e>>1))
+        const bool all_valid = a.mask == nullptr && wp0 + 16 <= p_hi &&
+                               (win.full || (win.len >= 16 && win.contains(wp0) && win.contains(wp0 + 15) &&
+                                             ((wp0 - win.start + win.N) % win.N) + 15 < win.len));
+        if (!all_valid) {
+#pragma unroll
+            for (int j = 0; j < 2; ++j) {
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    const int t = wp0 + 8 * j + 2 * t4 + (e & 1);
+                    float v = s[j][e];
+                    if (!(t < p_hi && win.contains(t))) v = -INFINITY;
+                    if (a.mask) {
+                        const int hq = hq_g + (e >> 1) * 8;
+                        if (g + (e >> 1) * 8 < nh && v != -INFINITY)
+                            v += mask_offset(a.mask, a.mask_kind, mrow + (int64_t)hq * a.m_sh + t);
+                    }
+                    s[j][e] = v;
                 }
             }
         }
 
-        // ---------------- online softmax (log2 domain) --------------------
-        // s[j][e]: e=0,1 -> head g, tokens wp0 + 8j + 2t4 + e; e=2,3 -> head g+8
-#pragma unroll
-        for (int j = 0; j < 2; ++j) {
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-                const int t = wp0 + 8 * j + 2 * t4 + (e & 1);
-                float v = s[j][e] * a.scale_log2;
-                if (!(t < p_hi && win.contains(t))) v = -INFINITY;
-                if (a.mask) {
-                    const int hq = hq_g + (e >> 1) * 8;
-                    if (h0 + g + (e >> 1) * 8 < h0 + nh && v != -INFINITY)
-                        v += mask_offset(a.mask, a.mask_kind, mrow + (int64_t)hq * a.m_sh + t);
-                }
-                s[j][e] = v;
-            }
-        }
+        // ---------------- pair-wide row maxima ----------------------------
         float mx0 = fmaxf(fmaxf(s[0][0], s[0][1]), fmaxf(s[1][0], s[1][1]));
         float mx1 = fmaxf(fmaxf(s[0][2], s[0][3]), fmaxf(s[1][2], s[1][3]));
         mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 1));
         mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2));
         mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
         mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
+        if (t4 == 0) {
+            xM[(pair * 2 + role) * 16 + g] = mx0;
+            xM[(pair * 2 + role) * 16 + g + 8] = mx1;
+        }
+        named_barrier(bar_id, 64);
+        mx0 = fmaxf(mx0, xM[(pair * 2 + (role ^ 1)) * 16 + g]);
+        mx1 = fmaxf(mx1, xM[(pair * 2 + (role ^ 1)) * 16 + g + 8]);
+        // both warps of the pair see the same maxima and history: same decisions
         const bool up0 = mx0 > m0 + (float)kRescaleLog2;
         const bool up1 = mx1 > m1 + (float)kRescaleLog2;
         if (__any_sync(0xffffffffu, up0 || up1)) {
-            const float a0 = up0 ? exp2f(m0 - mx0) : 1.f;
-            const float a1 = up1 ? exp2f(m1 - mx1) : 1.f;
+            const float a0 = up0 ? ex2(m0 - mx0) : 1.f;
+            const float a1 = up1 ? ex2(m1 - mx1) : 1.f;
             if (up0) m0 = mx0;
             if (up1) m1 = mx1;
             l0 *= a0;
             l1 *= a1;
 #pragma unroll
-            for (int j = 0; j < C::NT; ++j) {
+            for (int j = 0; j < NTH; ++j) {
                 o[j][0] *= a0;
                 o[j][1] *= a0;
                 o[j][2] *= a1;
@@ -491,60 +568,80 @@ __global__ void __launch_bounds__(kThreads, 2) decode_mma_kernel(const DecodeArg
         float p[2][4];
 #pragma unroll
         for (int j = 0; j < 2; ++j) {
-            p[j][0] = exp2f(s[j][0] - mu0);
-            p[j][1] = exp2f(s[j][1] - mu0);
-            p[j][2] = exp2f(s[j][2] - mu1);
-            p[j][3] = exp2f(s[j][3] - mu1);
+            p[j][0] = ex2(s[j][0] - mu0);
+            p[j][1] = ex2(s[j][1] - mu0);
+            p[j][2] = ex2(s[j][2] - mu1);
+            p[j][3] = ex2(s[j][3] - mu1);
             l0 += p[j][0] + p[j][1];
             l1 += p[j][2] + p[j][3];
         }
-        uint32_t pa[4] = {Ops<T>::pack(p[0][0], p[0][1]), Ops<T>::pack(p[0][2], p[0][3]),
-                          Ops<T>::pack(p[1][0], p[1][1]), Ops<T>::pack(p[1][2], p[1][3])};
-        uint32_t pl[4] = {0u, 0u, 0u, 0u};
+        // P as the A fragment of k-step `role` (tokens 16*role.. of the pair)
+        uint4 pa_own;
+        pa_own.x = Ops<T>::pack(p[0][0], p[0][1]);
+        pa_own.y = Ops<T>::pack(p[0][2], p[0][3]);
+        pa_own.z = Ops<T>::pack(p[1][0], p[1][1]);
+        pa_own.w = Ops<T>::pack(p[1][2], p[1][3]);
+        uint4 pl_own = make_uint4(0u, 0u, 0u, 0u);
         if constexpr (Ops<T>::kSplitP) {
             // residual p - bf16(p), itself rounded to bf16
+            const uint32_t hi[4] = {pa_own.x, pa_own.y, pa_own.z, pa_own.w};
+            uint32_t lo[4];
 #pragma unroll
             for (int i = 0; i < 4; ++i) {
-                const float lo_v = p[i >> 1][2 * (i & 1)] - __uint_as_float(pa[i] << 16);
-                const float hi_v = p[i >> 1][2 * (i & 1) + 1] - __uint_as_float(pa[i] & 0xffff0000u);
-                pl[i] = Ops<T>::pack(lo_v, hi_v);
+                const float lo_v = p[i >> 1][2 * (i & 1)] - __uint_as_float(hi[i] << 16);
+                const float hi_v = p[i >> 1][2 * (i & 1) + 1] - __uint_as_float(hi[i] & 0xffff0000u);
+                lo[i] = Ops<T>::pack(lo_v, hi_v);
             }
+            pl_own = make_uint4(lo[0], lo[1], lo[2], lo[3]);
         }
+        xP[((pair * 2 + role) * 2 + 0) * 32 + lane] = pa_own;
+        if constexpr (Ops<T>::kSplitP) xP[((pair * 2 + role) * 2 + 1) * 32 + lane] = pl_own;
+        named_barrier(bar_id, 64);
+        const uint4 pa_oth = xP[((pair * 2 + (role ^ 1)) * 2 + 0) * 32 + lane];
+        uint4 pl_oth = make_uint4(0u, 0u, 0u, 0u);
+        if constexpr (Ops<T>::kSplitP) pl_oth = xP[((pair * 2 + (role ^ 1)) * 2 + 1) * 32 + lane];
 
-        // ---------------- O += P V over the 16 tokens ---------------------
-        // B fragment rows (tokens): 2t4, 2t4+1 (b0b1) and 2t4+8, 2t4+9 (b2b3);
-        // scale/bias of the groups in this thread's eighth of the head dim,
-        // paired (token a, token b)
-        constexpr int VG = (D / 8 >= GS) ? (D / 8) / GS : 1;
-        uint32_t vsc[2][VG], vbi[2][VG];
-        {
-            const int gbase = (g * (D / 8)) / GS;
+        // ---------------- O[:, half] += P V over the pair's 32 tokens -----
+        // thread g owns head dims role*D/2 + g*D/16 + [0, D/16); B-fragment
+        // rows (tokens of k-step kk): 2t4, 2t4+1 (b0b1) and 2t4+8, 2t4+9 (b2b3)
+        constexpr int VG = (D / 16 >= GS) ? (D / 16) / GS : 1;
+        constexpr int VWH = C::VW / 2;  // V words per thread per token (half head dim)
 #pragma unroll
-            for (int pr = 0; pr < 2; ++pr) {
-                const int ra = warp * 16 + 2 * t4 + pr * 8;
+        for (int kk = 0; kk < 2; ++kk) {
+            const uint4 pf = (kk == role) ? pa_own : pa_oth;
+            const uint32_t pa[4] = {pf.x, pf.y, pf.z, pf.w};
+            uint32_t plo[4] = {0u, 0u, 0u, 0u};
+            if constexpr (Ops<T>::kSplitP) {
+                const uint4 lf = (kk == role) ? pl_own : pl_oth;
+                plo[0] = lf.x, plo[1] = lf.y, plo[2] = lf.z, plo[3] = lf.w;
+            }
+            const int rb = pair * 32 + kk * 16 + 2 * t4;  // stage row of token 2t4 of this k-step
+            uint32_t vsc[2][VG], vbi[2][VG];
+            {
+                const int gbase = (role * (D / 2) + g * (D / 16)) / GS;
 #pragma unroll
-                for (int lg = 0; lg < VG; ++lg) {
-                    const int go = (gbase + lg) * 2;
-                    vsc[pr][lg] = lds16(s_vs + ra * C::SROWB + go) | (lds16(s_vs + (ra + 1) * C::SROWB + go) << 16);
-                    vbi[pr][lg] = has_bias ? (lds16(s_vb + ra * C::SROWB + go) |
-                                              (lds16(s_vb + (ra + 1) * C::SROWB + go) << 16))
-                                           : 0u;
+                for (int pr = 0; pr < 2; ++pr) {
+                    const int ra = rb + pr * 8;
+#pragma unroll
+                    for (int lg = 0; lg < VG; ++lg) {
+                        const int go = (gbase + lg) * 2;
+                        vsc[pr][lg] = lds16(s_vs + ra * C::SROWB + go) | (lds16(s_vs + (ra + 1) * C::SROWB + go) << 16);
+                        vbi[pr][lg] = has_bias ? (lds16(s_vb + ra * C::SROWB + go) |
+                                                  (lds16(s_vb + (ra + 1) * C::SROWB + go) << 16))
+                                               : 0u;
+                    }
                 }
             }
-        }
-        constexpr int VWQ = C::VW >= 4 ? 4 : C::VW;
-#pragma unroll
-        for (int w0 = 0; w0 < C::VW; w0 += VWQ) {
-            uint32_t vw[4][VWQ];
+            uint32_t vw[4][VWH];
 #pragma unroll
             for (int rr = 0; rr < 4; ++rr) {
-                const int r = warp * 16 + 2 * t4 + (rr & 1) + (rr >> 1) * 8;
-                const int byte = (g * C::VW + w0) * 4;
+                const int r = rb + (rr & 1) + (rr >> 1) * 8;
+                const int byte = (role * (C::PD / 2) + g * VWH) * 4;
                 const char* pp = s_vp + swz<C::CPR>(r, byte >> 4) * 16 + (byte & 15);
-                if constexpr (VWQ == 4) {
+                if constexpr (VWH == 4) {
                     const uint4 v = lds128(pp);
                     vw[rr][0] = v.x, vw[rr][1] = v.y, vw[rr][2] = v.z, vw[rr][3] = v.w;
-                } else if constexpr (VWQ == 2) {
+                } else if constexpr (VWH == 2) {
                     const uint2 v = lds64(pp);
                     vw[rr][0] = v.x, vw[rr][1] = v.y;
                 } else {
@@ -552,14 +649,13 @@ __global__ void __launch_bounds__(kThreads, 2) decode_mma_kernel(const DecodeArg
                 }
             }
 #pragma unroll
-            for (int u = 0; u < VWQ; ++u) {
-                const int wi = w0 + u;
-                const int lg = (D / 8 >= GS) ? (wi * C::EPW) / GS : 0;
+            for (int wi = 0; wi < VWH; ++wi) {
+                const int lg = (D / 16 >= GS) ? (wi * C::EPW) / GS : 0;
                 if constexpr (BITS == 4) {
                     uint32_t c[2][8];
 #pragma unroll
                     for (int pr = 0; pr < 2; ++pr) {
-                        const uint32_t wa = vw[2 * pr][u], wb = vw[2 * pr + 1][u];
+                        const uint32_t wa = vw[2 * pr][wi], wb = vw[2 * pr + 1][wi];
                         Ops<T>::nib4(__byte_perm(wa, wb, 0x5410), &c[pr][0]);
                         Ops<T>::nib4(__byte_perm(wa, wb, 0x7632), &c[pr][4]);
 #pragma unroll
@@ -568,13 +664,13 @@ __global__ void __launch_bounds__(kThreads, 2) decode_mma_kernel(const DecodeArg
 #pragma unroll
                     for (int e = 0; e < 8; ++e) {
                         Ops<T>::mma(o[8 * wi + e], pa, c[0][e], c[1][e]);
-                        if constexpr (Ops<T>::kSplitP) Ops<T>::mma(o[8 * wi + e], pl, c[0][e], c[1][e]);
+                        if constexpr (Ops<T>::kSplitP) Ops<T>::mma(o[8 * wi + e], plo, c[0][e], c[1][e]);
                     }
                 } else {
                     uint32_t c[2][4];
 #pragma unroll
                     for (int pr = 0; pr < 2; ++pr) {
-                        const uint32_t wa = vw[2 * pr][u], wb = vw[2 * pr + 1][u];
+                        const uint32_t wa = vw[2 * pr][wi], wb = vw[2 * pr + 1][wi];
                         Ops<T>::byte2(__byte_perm(wa, wb, 0x5140), &c[pr][0]);
                         Ops<T>::byte2(__byte_perm(wa, wb, 0x7362), &c[pr][2]);
 #pragma unroll
@@ -583,7 +679,7 @@ __global__ void __launch_bounds__(kThreads, 2) decode_mma_kernel(const DecodeArg
 #pragma unroll
                     for (int e = 0; e < 4; ++e) {
                         Ops<T>::mma(o[4 * wi + e], pa, c[0][e], c[1][e]);
-                        if constexpr (Ops<T>::kSplitP) Ops<T>::mma(o[4 * wi + e], pl, c[0][e], c[1][e]);
+                        if constexpr (Ops<T>::kSplitP) Ops<T>::mma(o[4 * wi + e], plo, c[0][e], c[1][e]);
                     }
                 }
             }
@@ -592,44 +688,47 @@ __global__ void __launch_bounds__(kThreads, 2) decode_mma_kernel(const DecodeArg
     cp_async_wait<0>();
     __syncthreads();  // ring no longer read: reuse it for the merge
 
-    // ---- merge the 4 warps' records; undo the head-dim permutation ----
+    // ---- merge: each pair's record is [O_role0 | O_role1], common m, l0+l1 ----
     l0 += __shfl_xor_sync(0xffffffffu, l0, 1);
     l0 += __shfl_xor_sync(0xffffffffu, l0, 2);
     l1 += __shfl_xor_sync(0xffffffffu, l1, 1);
     l1 += __shfl_xor_sync(0xffffffffu, l1, 2);
-    float* w_o = reinterpret_cast<float*>(ring);          // [kWarps][16][D]
-    float* w_m = w_o + kWarps * 16 * D;                   // [kWarps][16]
-    float* w_l = w_m + kWarps * 16;                       // [kWarps][16]
-    float* mo = w_l + kWarps * 16;                        // [16][D]
-    float* mm = mo + 16 * D;                              // [16]
-    float* ml = mm + 16;                                  // [16]
+    float* w_o = reinterpret_cast<float*>(ring);  // [kPairs][16][D]
+    float* w_m = w_o + kPairs * 16 * D;           // [kPairs][16]
+    float* w_l = w_m + kPairs * 16;               // [kPairs][2][16]
+    float* mo = w_l + kPairs * 2 * 16;            // [16][D]
+    float* mm = mo + 16 * D;                      // [16]
+    float* ml = mm + 16;                          // [16]
 #pragma unroll
-    for (int j = 0; j < C::NT; ++j) {
-        const int d0 = (2 * t4) * (D / 8) + j;
-        const int d1 = (2 * t4 + 1) * (D / 8) + j;
-        w_o[(warp * 16 + g) * D + d0] = o[j][0];
-        w_o[(warp * 16 + g) * D + d1] = o[j][1];
-        w_o[(warp * 16 + g + 8) * D + d0] = o[j][2];
-        w_o[(warp * 16 + g + 8) * D + d1] = o[j][3];
+    for (int j = 0; j < NTH; ++j) {
+        // n8 tile j, column c -> head dim role*D/2 + c*(D/16) + j
+        const int d0 = role * (D / 2) + (2 * t4) * (D / 16) + j;
+        const int d1 = d0 + D / 16;
+        w_o[(pair * 16 + g) * D + d0] = o[j][0];
+        w_o[(pair * 16 + g) * D + d1] = o[j][1];
+        w_o[(pair * 16 + g + 8) * D + d0] = o[j][2];
+        w_o[(pair * 16 + g + 8) * D + d1] = o[j][3];
     }
     if (t4 == 0) {
-        w_m[warp * 16 + g] = m0;
-        w_m[warp * 16 + g + 8] = m1;
-        w_l[warp * 16 + g] = l0;
-        w_l[warp * 16 + g + 8] = l1;
+        if (role == 0) {
+            w_m[pair * 16 + g] = m0;
+            w_m[pair * 16 + g + 8] = m1;
+        }
+        w_l[(pair * 2 + role) * 16 + g] = l0;
+        w_l[(pair * 2 + role) * 16 + g + 8] = l1;
     }
     __syncthreads();
     for (int idx = tid; idx < nh * D; idx += kThreads) {
         const int h = idx / D, d = idx - h * D;
         float mt = -INFINITY;
 #pragma unroll
-        for (int w = 0; w < kWarps; ++w) mt = fmaxf(mt, w_m[w * 16 + h]);
+        for (int pq = 0; pq < kPairs; ++pq) mt = fmaxf(mt, w_m[pq * 16 + h]);
         float lt = 0.f, ot = 0.f;
 #pragma unroll
-        for (int w = 0; w < kWarps; ++w) {
-            const float wt = merge_weight(w_m[w * 16 + h], mt);
-            lt += wt * w_l[w * 16 + h];
-            ot += wt * w_o[(w * 16 + h) * D + d];
+        for (int pq = 0; pq < kPairs; ++pq) {
+            const float wt = merge_weight(w_m[pq * 16 + h], mt);
+            lt += wt * (w_l[(pq * 2) * 16 + h] + w_l[(pq * 2 + 1) * 16 + h]);
+            ot += wt * w_o[(pq * 16 + h) * D + d];
         }
         mo[idx] = ot;
         if (d == 0) {
@@ -638,7 +737,7 @@ __global__ void __launch_bounds__(kThreads, 2) decode_mma_kernel(const DecodeArg
         }
     }
     __syncthreads();
-    finish_cta<T>(a, b, kvh, h0, nh, unit, hblk, split, mo, mm, ml);
+    finish_cta<T>(a, b, kvh, h0, nh, split, mo, mm, ml);
 }
 
 template <typename T, int BITS, int D, int GS>
@@ -671,11 +770,13 @@ int launch3(const DecodeArgs& a, cudaStream_t st) {
 template <typename T, int BITS>
 int launch2(const DecodeArgs& a, cudaStream_t st) {
     switch (a.D) {
-        case 64: return launch3<T, BITS, 64>(a, st);
+        case 64:
+            if constexpr (BITS == 8) return launch3<T, BITS, 64>(a, st);
+            break;
         case 128: return launch3<T, BITS, 128>(a, st);
         case 256: return launch3<T, BITS, 256>(a, st);
     }
-    return set_error(QSDPA_ERR_UNSUPPORTED, "tensor-core decode: D=%d", a.D);
+    return set_error(QSDPA_ERR_UNSUPPORTED, "tensor-core decode: D=%d bits=%d", a.D, a.bits);
 }
 
 bool aligned16(const void* p, int64_t sb, int64_t sh, int elt) {
@@ -688,7 +789,8 @@ bool aligned16(const void* p, int64_t sb, int64_t sh, int elt) {
 constexpr int kMinGqaMma = 4;
 
 bool mma_supported(const DecodeArgs& a) {
-    if (a.D != 64 && a.D != 128 && a.D != 256) return false;
+    // each warp of a pair owns half the head dim in whole packed words
+    if (a.D != 128 && a.D != 256 && !(a.D == 64 && a.bits == 8)) return false;
     if (a.gqa < kMinGqaMma) return false;
     if (!aligned16(a.kp, a.kp_sb, a.kp_sh, 4) || !aligned16(a.vp, a.vp_sb, a.vp_sh, 4)) return false;
     if (!aligned16(a.ks, a.ks_sb, a.ks_sh, 2) || !aligned16(a.vs, a.vs_sb, a.vs_sh, 2)) return false;

@@ -12,9 +12,8 @@
 // read by the warp as one contiguous, coalesced segment.  Keys are
 // dequantised once per CTA and shared by the HPW heads.  Scores use an online
 // softmax in the log2 domain (exp2f); the warps' (m, l, o) are merged through
-// shared memory, and with several splits the last CTA of a (unit, head
-// block) -- elected with an arrival counter -- merges the splits' records
-// (the reference's separate pass-2 kernel, mlx_qsdpa/kernels.py:342-419).
+// shared memory, and with several splits the combine kernel merges the
+// splits' records (the reference's pass-2 kernel, mlx_qsdpa/kernels.py:342-419).
 //
 // Numerics follow the reference's dequantise-then-attend path
 // (mlx_qsdpa/dispatch.py:68-83): each K/V element is dequantised to the query
@@ -189,7 +188,7 @@ __global__ void __launch_bounds__(kNW * 32) decode_simt_kernel(const DecodeArgs 
         }
     }
     __syncthreads();
-    finish_cta<T>(a, b, kvh, h0, nh, unit, hblk, split, mo, mm, ml);
+    finish_cta<T>(a, b, kvh, h0, nh, split, mo, mm, ml);
 }
 
 template <typename T, int BITS, int DPL>

@@ -85,7 +85,6 @@ struct DecodeArgs {
     float* out_ml;
     float* ws_o;    // split partials: (B*Hq, splits, D)
     float* ws_ml;   // (B*Hq, splits, 2)
-    unsigned* counters;  // one per (unit, head block); NULL = no in-kernel merge
     int B, Hq, Hkv, N, D, bits, gs, G, pd, gqa;
     int head_blocks;  // query-head blocks per GQA group
     int heads_per_block;
@@ -116,20 +115,19 @@ __device__ __forceinline__ float merge_weight(float m_part, float m_tot) {
 // mo[h*D + d] (un-normalised, relative to mm[h]), mm[h], ml[h], all in shared
 // memory.  With one split the CTA writes the output directly (normalised in
 // the query dtype, or as a partial record); otherwise it stores its split
-// record in the workspace and, when arrival counters are provided, the last
-// CTA of the (unit, head block) merges all splits (the reference's pass 2,
-// mlx_qsdpa/kernels.py:342-419, without a second launch).  Without counters
-// the host launches the combine kernel afterwards.
+// record in the workspace and the combine kernel, launched right after as a
+// programmatic dependent, merges the splits (the reference's pass 2,
+// mlx_qsdpa/kernels.py:342-419).
 template <typename T>
-__device__ void finish_cta(const DecodeArgs& a, int b, int kvh, int h0, int nh, int unit, int hblk, int split,
-                           const float* mo, const float* mm, const float* ml) {
+__device__ void finish_cta(const DecodeArgs& a, int b, int kvh, int h0, int nh, int split, const float* mo,
+                           const float* mm, const float* ml) {
     const int D = a.D;
     const int nsplit = a.splits;
     const int row0 = b * a.Hq + kvh * a.gqa + h0;
-    if (nsplit == 1) {
-        for (int idx = threadIdx.x; idx < nh * D; idx += blockDim.x) {
-            const int h = idx / D, d = idx - h * D;
-            const int row = row0 + h;
+    for (int idx = threadIdx.x; idx < nh * D; idx += blockDim.x) {
+        const int h = idx / D, d = idx - h * D;
+        const int row = row0 + h;
+        if (nsplit == 1) {
             if (a.out_mode == QSDPA_OUT_FINAL) {
                 const float lt = ml[h];
                 static_cast<T*>(a.out)[(int64_t)row * D + d] = Dt<T>::from_f(lt > 0.f ? mo[idx] / lt : 0.f);
@@ -140,52 +138,12 @@ __device__ void finish_cta(const DecodeArgs& a, int b, int kvh, int h0, int nh, 
                     a.out_ml[2 * row + 1] = ml[h];
                 }
             }
-        }
-        return;
-    }
-    for (int idx = threadIdx.x; idx < nh * D; idx += blockDim.x) {
-        const int h = idx / D, d = idx - h * D;
-        const int64_t rec = (int64_t)(row0 + h) * nsplit + split;
-        a.ws_o[rec * D + d] = mo[idx];
-        if (d == 0) {
-            a.ws_ml[rec * 2] = mm[h];
-            a.ws_ml[rec * 2 + 1] = ml[h];
-        }
-    }
-    if (a.counters == nullptr) return;
-
-    __shared__ int s_last;
-    __threadfence();
-    __syncthreads();
-    if (threadIdx.x == 0) {
-        unsigned* ctr = a.counters + (unit * a.head_blocks + hblk);
-        const unsigned ticket = atomicAdd(ctr, 1u);
-        s_last = (ticket == (unsigned)nsplit - 1u);
-        if (s_last) *ctr = 0u;  // leave the counter zero for the next call
-    }
-    __syncthreads();
-    if (!s_last) return;
-    __threadfence();
-    for (int idx = threadIdx.x; idx < nh * D; idx += blockDim.x) {
-        const int h = idx / D, d = idx - h * D;
-        const int row = row0 + h;
-        const float* rml = a.ws_ml + (int64_t)row * nsplit * 2;
-        const float* ro = a.ws_o + (int64_t)row * nsplit * D + d;
-        float mt = -INFINITY;
-        for (int sp = 0; sp < nsplit; ++sp) mt = fmaxf(mt, __ldcg(rml + 2 * sp));
-        float lt = 0.f, ot = 0.f;
-        for (int sp = 0; sp < nsplit; ++sp) {
-            const float wt = merge_weight(__ldcg(rml + 2 * sp), mt);
-            lt += wt * __ldcg(rml + 2 * sp + 1);
-            ot += wt * __ldcg(ro + (int64_t)sp * D);
-        }
-        if (a.out_mode == QSDPA_OUT_FINAL) {
-            static_cast<T*>(a.out)[(int64_t)row * D + d] = Dt<T>::from_f(lt > 0.f ? ot / lt : 0.f);
         } else {
-            a.out_o[(int64_t)row * D + d] = ot;
+            const int64_t rec = (int64_t)row * nsplit + split;
+            a.ws_o[rec * D + d] = mo[idx];
             if (d == 0) {
-                a.out_ml[2 * row] = mt;
-                a.out_ml[2 * row + 1] = lt;
+                a.ws_ml[rec * 2] = mm[h];
+                a.ws_ml[rec * 2 + 1] = ml[h];
             }
         }
     }

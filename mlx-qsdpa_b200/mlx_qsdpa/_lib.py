@@ -22,7 +22,6 @@ LIB_PATH = os.environ.get("QSDPA_LIB", os.path.join(_HERE, "libqsdpa.so"))
 QSDPA_F16, QSDPA_BF16 = 0, 1
 MASK_NONE, MASK_BOOL, MASK_ADD_F16, MASK_ADD_BF16, MASK_ADD_F32 = 0, 1, 2, 3, 4
 OUT_FINAL, OUT_PARTIAL = 0, 1
-COUNTER_BYTES = 65536
 
 _c_i32 = ctypes.c_int32
 _c_i64 = ctypes.c_int64
@@ -171,18 +170,18 @@ _ws_lock = threading.Lock()
 
 
 def workspace(device: torch.device, nbytes: int) -> torch.Tensor:
-    """Per-(device, stream) zero-initialised decode workspace of >= nbytes.
+    """Per-(device, stream) decode workspace (split-K partial records) of >= nbytes.
 
-    The kernel leaves the counter region zero after every call, so the buffer
-    is zeroed only when it is (re)allocated.  Calls on one stream are ordered,
-    so sharing one workspace per stream is race-free.
+    Calls on one stream are ordered, so sharing one workspace per stream is
+    race-free; the caching allocator keeps a replaced buffer alive until the
+    work queued on that stream has used it.
     """
     key = (device.index, _stream(device))
     with _ws_lock:
         buf = _ws_cache.get(key)
         if buf is None or buf.numel() < nbytes:
             size = max(nbytes, 2 * (buf.numel() if buf is not None else 0), 1 << 20)
-            buf = torch.zeros(size + 256, dtype=torch.uint8, device=device)
+            buf = torch.empty(size + 256, dtype=torch.uint8, device=device)
             _ws_cache[key] = buf
         return buf
 

@@ -34,19 +34,25 @@ def run(qs, c: Case, **kw):
 
 
 def check(qs, c: Case, mask=None, **kw):
-    """Gate: the exact oracle within 2e-3 / 1e-2.  Diagnostic: the emulation
-    of the MLX fallback's intermediate roundings (q*scale, scores and
-    probabilities rounded to the dtype) drifts from the exact answer by itself
-    -- by more than 2e-3 for bf16 or large scores -- so the kernel must sit no
-    farther from it than that drift (plus the tolerance)."""
+    """The exact oracle (float64 on the dtype-rounded dequantised K/V) within
+    2e-3 / 1e-2 per element."""
     out = run(qs, c, mask=mask, **kw)
-    exact = c.reference(mask=mask)
-    e1 = assert_close(out, exact, what="vs exact")
-    mlx = c.reference(mask=mask, mode="mlx")
-    drift = float(np.abs(mlx - exact).max())
-    e2 = float(np.abs(out - mlx).max())
-    assert e2 <= drift + 2e-3, f"vs mlx-rounded: {e2:.3e} > drift {drift:.3e} + 2e-3"
+    e1 = assert_close(out, c.reference(mask=mask), what="vs exact")
     return out, e1
+
+
+@pytest.mark.parametrize("shape", [(1, 32, 2, 1000, 256), (2, 16, 4, 300, 128)])
+def test_matches_mlx_rounded_fallback(qs, shape):
+    """Against the emulation of the MLX CPU fallback graph (q*scale, scores,
+    probabilities and output rounded to float16): for float16 affine caches
+    its own drift from the exact result is small, and the kernel must sit
+    within the tolerance of it as well.  (For bfloat16 or symmetric caches
+    with large scores that emulation drifts from the exact answer by more
+    than the tolerance itself, so the exact oracle is the gate there.)"""
+    B, Hq, Hkv, N, D = shape
+    c = Case(B, Hq, Hkv, N, D, seed=N)
+    out = run(qs, c, threshold=0)
+    assert_close(out, c.reference(mode="mlx"), what="vs mlx-rounded")
 
 
 # ---- reference test shapes (B, Hq, Hkv, N, D) ----
