@@ -206,7 +206,7 @@ struct Cfg {
     static constexpr int XP_BYTES = kPairs * 2 * 2 * 32 * 16;  // P fragments (hi, lo) per warp
     static constexpr int X_BYTES = XP_BYTES + kPairs * 2 * 16 * 4;
     // end-of-chunk merge area: per-pair O (16 x D fp32) + m, l; then merged
-    static constexpr int MERGE_BYTES = kPairs * 16 * D * 4 + kPairs * 3 * 16 * 4 + 16 * (D + 2) * 4;
+    static constexpr int MERGE_BYTES = kPairs * 16 * D * 4 + kPairs * 3 * 16 * 4 + 16 * (D + 2) * 4 + kPairs * 16 * 4;
     // deepest ring (2..4 stages) that keeps a CTA within ~74 KB so three CTAs
     // share an SM
     static constexpr int STAGES_FIT = (74 * 1024 - Q_BYTES - X_BYTES) / STAGE_BYTES;
@@ -351,7 +351,38 @@ __global__ void __launch_bounds__(kThreads, (Cfg<BITS, D, GS>::MIN_BLOCKS)) deco
         }
     };
 
-    // prologue: start streaming before building the Q fragments
+    // ---- prologue: the 16 query rows, then the first tiles, all asynchronous ----
+    // The query rows land in the ring's last stage, which the prologue's tile
+    // loads leave untouched; 16-byte copies when the rows are 16-byte aligned.
+    T* qst = reinterpret_cast<T*>(ring + (C::STAGES - 1) * C::STAGE_BYTES);
+    {
+        const T* q = static_cast<const T*>(a.q) + (int64_t)b * a.q_sb + (int64_t)(kvh * a.gqa + h0) * a.q_sh;
+        const bool q_vec = ((uintptr_t)q % 16 == 0) && ((a.q_sh * 2) % 16 == 0);
+        if (q_vec) {
+            constexpr int CH = 16 * D * 2 / 16;  // 16-byte chunks of the 16 rows
+#pragma unroll
+            for (int k = 0; k < (CH + kThreads - 1) / kThreads; ++k) {
+                const int i = tid + k * kThreads;
+                if (i < CH) {
+                    const int h = i / (D / 8), c = i - h * (D / 8);
+                    const bool ok = h < nh;
+                    cp_async16(reinterpret_cast<char*>(qst) + i * 16, q + (ok ? (int64_t)h * a.q_sh + c * 8 : 0),
+                               ok ? 16 : 0);
+                }
+            }
+        } else {
+            constexpr int PER = 16 * D / kThreads;
+            T v[PER];
+#pragma unroll
+            for (int k = 0; k < PER; ++k) {
+                const int i = tid + k * kThreads, h = i / D, d = i - h * D;
+                v[k] = h < nh ? q[(int64_t)h * a.q_sh + d] : Dt<T>::from_f(0.f);
+            }
+#pragma unroll
+            for (int k = 0; k < PER; ++k) qst[tid + k * kThreads] = v[k];
+        }
+        cp_async_commit();
+    }
 #pragma unroll
     for (int i = 0; i < C::STAGES - 1; ++i) {
         if (i < ntiles) load_tile(i, i);
@@ -359,19 +390,13 @@ __global__ void __launch_bounds__(kThreads, (Cfg<BITS, D, GS>::MIN_BLOCKS)) deco
     }
 
     // ---- Q fragments (A operand of S = Q K^T), permuted like K ----
-    // The 16 query rows are first staged (coalesced) in the ring's last stage,
-    // which the prologue leaves untouched, then gathered into per-lane
-    // fragment order.
+    cp_async_wait<C::STAGES - 1>();  // the query group (oldest) has landed
+    __syncthreads();
     {
-        T* qst = reinterpret_cast<T*>(ring + (C::STAGES - 1) * C::STAGE_BYTES);
-        const T* q = static_cast<const T*>(a.q) + (int64_t)b * a.q_sb;
-        for (int i = tid; i < 16 * D; i += kThreads) {
-            const int h = i / D, d = i - h * D;
-            qst[i] = h < nh ? q[(int64_t)(kvh * a.gqa + h0 + h) * a.q_sh + d] : Dt<T>::from_f(0.f);
-        }
-        __syncthreads();
         const uint16_t* q16 = reinterpret_cast<const uint16_t*>(qst);
-        for (int idx = tid; idx < C::KSTEPS * 32; idx += kThreads) {
+#pragma unroll
+        for (int k = 0; k < C::KSTEPS * 32 / kThreads; ++k) {
+            const int idx = tid + k * kThreads;
             const int kstep = idx >> 5, ln = idx & 31;
             const int qg = ln >> 2, qt = ln & 3;
             uint32_t v[2][4];
@@ -389,7 +414,7 @@ __global__ void __launch_bounds__(kThreads, (Cfg<BITS, D, GS>::MIN_BLOCKS)) deco
             *reinterpret_cast<uint4*>(sQ + idx * 16) = f;
         }
         // the first loop iteration's __syncthreads orders these writes (and the
-        // reads of the staging area) before anything reuses the last stage
+        // reads of the staging area) before the last stage is refilled
     }
 
     constexpr int NTH = C::NT / 2;  // n8 tiles of this warp's head-dim half
@@ -718,23 +743,37 @@ __global__ void __launch_bounds__(kThreads, (Cfg<BITS, D, GS>::MIN_BLOCKS)) deco
         w_l[(pair * 2 + role) * 16 + g + 8] = l1;
     }
     __syncthreads();
-    for (int idx = tid; idx < nh * D; idx += kThreads) {
-        const int h = idx / D, d = idx - h * D;
+    // per-head weights of the two pair records, then a 4-wide weighted sum
+    float* w_wt = ml + 16;  // [kPairs][16]
+    if (tid < 16) {
+        const int h = tid;
         float mt = -INFINITY;
 #pragma unroll
         for (int pq = 0; pq < kPairs; ++pq) mt = fmaxf(mt, w_m[pq * 16 + h]);
-        float lt = 0.f, ot = 0.f;
+        float lt = 0.f;
 #pragma unroll
         for (int pq = 0; pq < kPairs; ++pq) {
-            const float wt = merge_weight(w_m[pq * 16 + h], mt);
+            const float wt = w_m[pq * 16 + h] == -INFINITY ? 0.f : ex2(w_m[pq * 16 + h] - mt);
+            w_wt[pq * 16 + h] = wt;
             lt += wt * (w_l[(pq * 2) * 16 + h] + w_l[(pq * 2 + 1) * 16 + h]);
-            ot += wt * w_o[(pq * 16 + h) * D + d];
         }
-        mo[idx] = ot;
-        if (d == 0) {
-            mm[h] = mt;
-            ml[h] = lt;
+        mm[h] = mt;
+        ml[h] = lt;
+    }
+    __syncthreads();
+    for (int idx = tid * 4; idx < nh * D; idx += kThreads * 4) {
+        const int h = idx / D;
+        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+        for (int pq = 0; pq < kPairs; ++pq) {
+            const float wt = w_wt[pq * 16 + h];
+            const float4 v = *reinterpret_cast<const float4*>(w_o + pq * 16 * D + idx);
+            acc.x += wt * v.x;
+            acc.y += wt * v.y;
+            acc.z += wt * v.z;
+            acc.w += wt * v.w;
         }
+        *reinterpret_cast<float4*>(mo + idx) = acc;
     }
     __syncthreads();
     finish_cta<T>(a, b, kvh, h0, nh, split, mo, mm, ml);

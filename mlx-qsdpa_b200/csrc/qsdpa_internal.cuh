@@ -121,18 +121,23 @@ __device__ __forceinline__ float merge_weight(float m_part, float m_tot) {
 template <typename T>
 __device__ void finish_cta(const DecodeArgs& a, int b, int kvh, int h0, int nh, int split, const float* mo,
                            const float* mm, const float* ml) {
-    const int D = a.D;
+    const int D = a.D;  // a multiple of 32: four consecutive dims per thread
     const int nsplit = a.splits;
     const int row0 = b * a.Hq + kvh * a.gqa + h0;
-    for (int idx = threadIdx.x; idx < nh * D; idx += blockDim.x) {
+    for (int idx = threadIdx.x * 4; idx < nh * D; idx += blockDim.x * 4) {
         const int h = idx / D, d = idx - h * D;
         const int row = row0 + h;
+        const float4 v = *reinterpret_cast<const float4*>(mo + idx);
         if (nsplit == 1) {
             if (a.out_mode == QSDPA_OUT_FINAL) {
-                const float lt = ml[h];
-                static_cast<T*>(a.out)[(int64_t)row * D + d] = Dt<T>::from_f(lt > 0.f ? mo[idx] / lt : 0.f);
+                const float inv = ml[h] > 0.f ? 1.f / ml[h] : 0.f;
+                T* o = static_cast<T*>(a.out) + (int64_t)row * D + d;
+                o[0] = Dt<T>::from_f(v.x * inv);
+                o[1] = Dt<T>::from_f(v.y * inv);
+                o[2] = Dt<T>::from_f(v.z * inv);
+                o[3] = Dt<T>::from_f(v.w * inv);
             } else {
-                a.out_o[(int64_t)row * D + d] = mo[idx];
+                *reinterpret_cast<float4*>(a.out_o + (int64_t)row * D + d) = v;
                 if (d == 0) {
                     a.out_ml[2 * row] = mm[h];
                     a.out_ml[2 * row + 1] = ml[h];
@@ -140,7 +145,7 @@ __device__ void finish_cta(const DecodeArgs& a, int b, int kvh, int h0, int nh, 
             }
         } else {
             const int64_t rec = (int64_t)row * nsplit + split;
-            a.ws_o[rec * D + d] = mo[idx];
+            *reinterpret_cast<float4*>(a.ws_o + rec * D + d) = v;
             if (d == 0) {
                 a.ws_ml[rec * 2] = mm[h];
                 a.ws_ml[rec * 2 + 1] = ml[h];
