@@ -22,7 +22,7 @@ std::atomic<int> g_sm_count[64];
 
 constexpr size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
 constexpr int kMaxSplits = 1024;
-constexpr int kMinChunk = 256;  // keys per CTA below which splitting stops paying
+constexpr int kMinChunk = 64;  // keys per CTA below which splitting stops paying
 }  // namespace
 
 int set_error(int code, const char* fmt, ...) {
@@ -156,9 +156,10 @@ Plan make_plan(const qsdpa_decode_params* p, const DecodeArgs& a) {
     const int units = a.B * a.Hkv * pl.head_blocks;
     int splits = p->splits;
     if (splits == 0) {
-        // one full wave of resident CTAs (tensor-core kernel: 3 per SM; CUDA-core
-        // kernel: two waves of 4 per SM), but no chunk below kMinChunk keys
-        const int target = pl.use_mma ? sm_count() * 3 : sm_count() * 4 * 2;
+        // tensor-core kernel: two CTAs per SM, one wave, every SM equally
+        // loaded (a third resident CTA on some SMs only adds imbalance);
+        // CUDA-core kernel: two waves of 4 per SM.  No chunk below kMinChunk.
+        const int target = pl.use_mma ? sm_count() * 2 : sm_count() * 4 * 2;
         splits = (target + units - 1) / units;
         const int by_len = (p->N + kMinChunk - 1) / kMinChunk;
         if (splits > by_len) splits = by_len;
