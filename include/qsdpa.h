@@ -142,6 +142,27 @@ int qsdpa_decode_splits(const qsdpa_decode_params* p);
 size_t qsdpa_decode_workspace_size(const qsdpa_decode_params* p);
 
 /*
+ * qsdpa_decode for callers that cannot allocate device memory -- a host that
+ * owns every allocation and hands its plugins only the call's tensors, code
+ * running while someone else captures the stream into a CUDA graph (where
+ * cudaMalloc is not allowed), or a loop that must never pay cudaMalloc's
+ * implicit device synchronisation.  No counterpart in the reference.
+ *
+ * Same parameters as qsdpa_decode except that `workspace` is ignored: the
+ * split records go to a fixed array of QSDPA_NOALLOC_SCRATCH_BYTES compiled
+ * into the library, which every GPU that loads the library holds until the
+ * process exits.  With splits == 0 the split count is capped so the records fit
+ * (down to one CTA per KV head, which needs no scratch); an explicit split
+ * count whose records do not fit is rejected with QSDPA_ERR_WORKSPACE.  The
+ * function allocates nothing.  The first call on a device looks up the array's
+ * device address -- make it before any stream capture.  All calls on a device
+ * share the array: calls that overlap on the GPU (other streams or threads at
+ * the same time) race and must be serialised by the caller.
+ */
+#define QSDPA_NOALLOC_SCRATCH_BYTES (4u << 20)
+int qsdpa_decode_noalloc(const qsdpa_decode_params* p, void* stream);
+
+/*
  * Merge `parts` partial records per query row into the attention output.
  * Replaces the reference's pass-2 reduction (mlx_qsdpa/kernels.py:342-419,
  * launched from dispatch.py:245-267) and serves as the cross-GPU merge after

@@ -79,7 +79,7 @@ class DequantizeParams(ctypes.Structure):
 
 # Every function the C header declares (checked by the CPU test suite).
 EXPORTS = (
-    "qsdpa_decode", "qsdpa_decode_splits", "qsdpa_decode_workspace_size",
+    "qsdpa_decode", "qsdpa_decode_noalloc", "qsdpa_decode_splits", "qsdpa_decode_workspace_size",
     "qsdpa_combine", "qsdpa_quantize", "qsdpa_dequantize", "qsdpa_last_error",
     "qsdpa_abi_version",
 )
@@ -104,6 +104,8 @@ def load() -> ctypes.CDLL:
         P = ctypes.POINTER
         lib.qsdpa_decode.argtypes = [P(DecodeParams), _c_vp]
         lib.qsdpa_decode.restype = ctypes.c_int
+        lib.qsdpa_decode_noalloc.argtypes = [P(DecodeParams), _c_vp]
+        lib.qsdpa_decode_noalloc.restype = ctypes.c_int
         lib.qsdpa_decode_splits.argtypes = [P(DecodeParams)]
         lib.qsdpa_decode_splits.restype = ctypes.c_int
         lib.qsdpa_decode_workspace_size.argtypes = [P(DecodeParams)]
