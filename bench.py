@@ -44,8 +44,8 @@ METRIC = "decode-attn us/step (GQA-16, D=256, 4-bit gs32, 128K ctx per GPU)"
 def parse():
     ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=240)
-    ap.add_argument("--warmup", type=int, default=24)
+    ap.add_argument("--steps", type=int, default=2000)
+    ap.add_argument("--warmup", type=int, default=50)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--ctx", type=int, default=CTX_PER_GPU, help="context tokens per GPU")
     ap.add_argument("--layers", type=int, default=LAYERS)
@@ -122,7 +122,7 @@ def cpu_decode_timer(ctx: int, calls: int, seed: int = 0):
 class ClockSampler:
     """nvidia-smi clock / throttle-reason sampling during the timed region."""
 
-    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+    FIELDS = ("timestamp,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
@@ -137,7 +137,7 @@ class ClockSampler:
             os.close(fd)
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                 "-lms", "100"], stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+                 "-lms", "20"], stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
             time.sleep(0.25)
         except Exception:
             self.proc = None
@@ -151,9 +151,11 @@ class ClockSampler:
             except Exception:
                 self.proc.kill()
 
-    def summary(self):
+    def summary(self, t0: float, t1: float):
+        """Samples whose timestamp falls in the timed window [t0, t1] (host clock)."""
         if self.proc is None or not self.path or not os.path.exists(self.path):
             return None
+        import datetime
         sm, mx, reasons = [], None, set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
         with open(self.path) as f:
@@ -162,16 +164,21 @@ class ClockSampler:
                 if len(parts) < 9:
                     continue
                 try:
-                    sm.append(float(parts[1]))
-                    mx = float(parts[2])
+                    ts = datetime.datetime.strptime(parts[0], "%Y/%m/%d %H:%M:%S.%f").timestamp()
+                    clk, cmax = float(parts[1]), float(parts[2])
                 except ValueError:
                     continue
+                if not (t0 - 0.03 <= ts <= t1 + 0.03):
+                    continue
+                sm.append(clk)
+                mx = cmax
                 for n, v in zip(names, parts[5:9]):
                     if v.lower().startswith("active"):
                         reasons.add(n)
         os.unlink(self.path)
         if not sm:
-            return None
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0,
+                    "note": "timed region shorter than the sampling interval"}
         return {"sm_mhz": float(np.median(sm)), "sm_max_mhz": mx, "reasons": sorted(reasons),
                 "samples": len(sm)}
 
@@ -220,6 +227,7 @@ def main():
 
     import mlx_qsdpa
     from mlx_qsdpa import _lib
+    from mlx_qsdpa.sharded import sharded_quantized_sdpa
 
     ctx = args.ctx
     L = args.layers
@@ -291,13 +299,15 @@ def main():
     with ClockSampler(local) as clk:
         e0 = torch.cuda.Event(enable_timing=True)
         e1 = torch.cuda.Event(enable_timing=True)
+        t_host0 = time.time()
         e0.record(stream)
         for i in range(K):
             run(i)
         e1.record(stream)
         barrier()
+        t_host1 = time.time()
     elapsed_ms = e0.elapsed_time(e1)
-    clocks = clk.summary()
+    clocks = clk.summary(t_host0, t_host1)
 
     # ---- device duration of one decode-kernel launch (for the roofline) ----
     # the local decode alone (no collective), captured per layer and replayed
@@ -351,13 +361,7 @@ def main():
         if world == 1:
             o = mlx_qsdpa.quantized_sdpa(qd, pk, pv, ks, vs, kb, vb, scale=scale, bits=BITS, group_size=GS)
         else:
-            po, pml = _lib.decode(qd, pk, pv, ks, vs, kb, vb, scale=scale, bits=BITS, group_size=GS,
-                                  out_mode=_lib.OUT_PARTIAL)
-            go = torch.empty((world,) + po.shape, dtype=po.dtype, device=dev)
-            gm = torch.empty((world,) + pml.shape, dtype=pml.dtype, device=dev)
-            dist.all_gather_into_tensor(go, po)
-            dist.all_gather_into_tensor(gm, pml)
-            o = _lib.combine(go, gm, torch.float16).view(B, HQ, 1, D)
+            o = sharded_quantized_sdpa(qd, (pk, ks, kb), (pv, vs, vb), bits=BITS, group_size=GS, scale=scale)
         out_host.copy_(o, non_blocking=True)
 
     for i in range(3):
@@ -387,7 +391,9 @@ def main():
         peak, peak_kind = measured_peaks()
         bytes_local = algorithmic_bytes(ctx)
         achieved = bytes_local / (per_launch_ms * 1e-3) / 1e9
-        splits = _lib.decode_splits((B, HQ), HKV, ctx, D, BITS, GS)
+        (pk0, ks0, kb0), (pv0, vs0, vb0) = layers[0]
+        splits = _lib.plan_splits(q, pk0, pv0, ks0, vs0, kb0, vb0, BITS, GS)
+        launches_per_step = (1 if splits == 1 else 2) + (1 if world > 1 else 0)
         line = {
             "metric": METRIC,
             "value": round(ms_per_step * 1e3, 3),
@@ -420,7 +426,7 @@ def main():
             },
             "e2e": {"value": round(e2e_ms * 1e3, 3), "unit": "us/step",
                     "h2d_bytes_per_step": B * HQ * D * 2, "d2h_bytes_per_step": B * HQ * D * 2},
-            "gpu_launches": K * (1 if world == 1 else 2),  # decode (+ combine) per step
+            "gpu_launches": K * launches_per_step,  # decode, split merge, (cross-GPU merge) per step
             "clocks": clocks,
             "split_check_max_abs": check,
         }

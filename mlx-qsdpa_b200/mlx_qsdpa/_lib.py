@@ -250,6 +250,28 @@ def decode(q: torch.Tensor, kp, vp, ks, vs, kb, vb, *, scale: float, bits: int, 
     return out if out_mode == OUT_FINAL else part
 
 
+def plan_splits(q, kp, vp, ks, vs, kb, vb, bits: int, group_size: int, splits: int = 0) -> int:
+    """Split count qsdpa_decode will use for these tensors (host-only query)."""
+    lib = load()
+    B, Hq, _, D = q.shape
+    p = DecodeParams()
+    p.q, p.q_sb, p.q_sh = q.data_ptr(), q.stride(0), q.stride(1)
+    p.k_packed, p.kp_sb, p.kp_sh = kp.data_ptr(), kp.stride(0), kp.stride(1)
+    p.v_packed, p.vp_sb, p.vp_sh = vp.data_ptr(), vp.stride(0), vp.stride(1)
+    p.k_scales, p.ks_sb, p.ks_sh = ks.data_ptr(), ks.stride(0), ks.stride(1)
+    p.v_scales, p.vs_sb, p.vs_sh = vs.data_ptr(), vs.stride(0), vs.stride(1)
+    if kb is not None:
+        p.k_biases, p.kb_sb, p.kb_sh = kb.data_ptr(), kb.stride(0), kb.stride(1)
+        p.v_biases, p.vb_sb, p.vb_sh = vb.data_ptr(), vb.stride(0), vb.stride(1)
+    p.out = 1
+    p.B, p.Hq, p.Hkv, p.N, p.D = B, Hq, kp.shape[1], kp.shape[2], D
+    p.bits, p.group_size, p.dtype, p.splits = bits, group_size, dtype_code(q.dtype), splits
+    p.scale = 1.0
+    rc = lib.qsdpa_decode_splits(ctypes.byref(p))
+    _check(rc if rc < 0 else 0, "qsdpa_decode_splits")
+    return rc
+
+
 def decode_splits(q_shape, Hkv: int, N: int, D: int, bits: int, group_size: int, splits: int = 0) -> int:
     """Split count the library would use (host-only query)."""
     lib = load()

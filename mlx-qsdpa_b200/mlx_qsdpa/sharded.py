@@ -1,0 +1,152 @@
+"""Sequence-sharded decode across the GPUs of one node.
+
+A long context is split into contiguous token ranges, one per rank (the
+reference has no multi-device code; this is the long-context scaling layer of
+the B200 build).  Each rank runs the fused decode over its own shard with
+partial output -- for every query row the un-normalised ``o``, the running
+maximum ``m`` and the sum ``l`` (log2 domain) -- the ranks all-gather these
+small records (``B*H_q*(D+2)*4`` bytes per rank) and every rank merges them
+with the combine kernel, so the attention output ends up replicated, as the
+next layer needs it.
+
+Appends go to the rank that owns the tail of the sequence
+(:class:`SequenceShardedCache`).  Batches shard by sequence instead and need no
+collective at all (each rank runs the unsharded decode on its own rows).
+"""
+
+from __future__ import annotations
+
+from typing import Callable, Optional
+
+import torch
+import torch.distributed as dist
+
+from . import _lib
+from .cache import QuantizedSDPACache
+
+__all__ = ["sharded_quantized_sdpa", "merge_partials", "SequenceShardedCache"]
+
+
+def _gather(t: torch.Tensor, group) -> torch.Tensor:
+    world = dist.get_world_size(group)
+    out = torch.empty((world,) + tuple(t.shape), dtype=t.dtype, device=t.device)
+    if dist.get_backend(group) == "nccl":
+        dist.all_gather_into_tensor(out, t.contiguous(), group=group)
+    else:
+        dist.all_gather(list(out.unbind(0)), t.contiguous(), group=group)
+    return out
+
+
+def merge_partials(gath_o: torch.Tensor, gath_ml: torch.Tensor, dtype: torch.dtype,
+                   combine_fn: Optional[Callable] = None) -> torch.Tensor:
+    """Merge gathered records (P, rows, D) / (P, rows, 2) into (rows, D)."""
+    fn = combine_fn or _lib.combine
+    return fn(gath_o, gath_ml, dtype)
+
+
+def sharded_quantized_sdpa(q, k_quant, v_quant, *, bits=4, group_size=32, scale=None, mask=None,
+                           group=None, partial_fn: Optional[Callable] = None,
+                           combine_fn: Optional[Callable] = None):
+    """Decode attention over a sequence sharded across the ranks of ``group``.
+
+    Args:
+        q:        (B, H_q, 1, D) query, identical on every rank
+        k_quant:  (packed, scales, biases) of this rank's key shard (B, H_kv, N_r, .)
+        v_quant:  (packed, scales, biases) of this rank's value shard
+        mask:     None, or a bool / additive mask over this rank's N_r keys,
+                  or a KVRanges window in shard coordinates
+    Returns the (B, H_q, 1, D) attention output over the whole sequence.
+
+    ``partial_fn(q, k_quant, v_quant, scale, bits, group_size, mask)`` and
+    ``combine_fn(gath_o, gath_ml, dtype)`` default to the CUDA kernels; the
+    CPU tests substitute the oracle to exercise the collective logic.
+    """
+    B, Hq, qL, D = q.shape
+    if qL != 1:
+        raise ValueError("sharded decode expects qL == 1")
+    if scale is None:
+        scale = D ** -0.5
+    if partial_fn is None:
+        part_o, part_ml = _partial_cuda(q, k_quant, v_quant, scale, bits, group_size, mask)
+    else:
+        part_o, part_ml = partial_fn(q, k_quant, v_quant, scale, bits, group_size, mask)
+    gath_o = _gather(part_o, group)
+    gath_ml = _gather(part_ml, group)
+    out = merge_partials(gath_o, gath_ml, q.dtype, combine_fn)
+    return out.view(B, Hq, 1, D)
+
+
+def _partial_cuda(q, k_quant, v_quant, scale, bits, group_size, mask):
+    from .dispatch import _fused_mask, _mask_kind  # local: shared validation helpers
+    pk, ks, kb = k_quant
+    pv, vs, vb = v_quant
+    B, Hq, _, D = q.shape
+    m, ranges = _fused_mask(mask, B, Hq, pk.shape[2], q.device)
+    return _lib.decode(
+        q.contiguous(), _lib.rows_contiguous(pk), _lib.rows_contiguous(pv), _lib.rows_contiguous(ks),
+        _lib.rows_contiguous(vs), _lib.rows_contiguous(kb) if kb is not None else None,
+        _lib.rows_contiguous(vb) if vb is not None else None, scale=scale, bits=bits, group_size=group_size,
+        mask=m, mask_kind=_mask_kind(m) if m is not None else _lib.MASK_NONE,
+        kv_start=ranges.start if ranges is not None else None,
+        kv_len=ranges.length if ranges is not None else None, out_mode=_lib.OUT_PARTIAL)
+
+
+class SequenceShardedCache:
+    """A quantized KV cache whose token range is split across ranks.
+
+    Rank ``r`` owns global token positions ``[r*shard_tokens, (r+1)*shard_tokens)``
+    and keeps them in a local :class:`QuantizedSDPACache`; ``update_and_fetch``
+    is called with the same new tokens on every rank, and each rank stores only
+    the ones it owns.  ``offset`` is the global length.
+    """
+
+    _use_fused_sdpa = True
+
+    def __init__(self, shard_tokens: int, bits: int = 4, group_size: int = 32, group=None):
+        self.shard_tokens = int(shard_tokens)
+        self.bits = bits
+        self.group_size = group_size
+        self.group = group
+        self.rank = dist.get_rank(group)
+        self.world = dist.get_world_size(group)
+        self.offset = 0
+        self.local = QuantizedSDPACache(bits=bits, group_size=group_size,
+                                        step=min(256, max(1, self.shard_tokens)))
+        self._quantize_hook = None  # tests: oracle quantization on CPU tensors
+
+    def owned_range(self):
+        lo = self.rank * self.shard_tokens
+        return lo, lo + self.shard_tokens
+
+    def update_and_fetch(self, keys, values):
+        """Append (B, H_kv, S, D) tokens at the global tail; returns this rank's shard views."""
+        S = keys.shape[2]
+        lo, hi = self.owned_range()
+        a, b = max(self.offset, lo), min(self.offset + S, hi)
+        if self.offset + S > self.world * self.shard_tokens:
+            raise ValueError("sequence exceeds the sharded capacity")
+        if b > a:
+            ks = keys[:, :, a - self.offset:b - self.offset]
+            vs = values[:, :, a - self.offset:b - self.offset]
+            if self._quantize_hook is not None:
+                self._quantize_hook(self.local, ks, vs)
+            else:
+                self.local.update_and_fetch(ks, vs)
+        self.offset += S
+        if self.local.empty():
+            return None, None
+        return self.local.state
+
+    def attend(self, q, scale=None, partial_fn=None, combine_fn=None):
+        """Decode attention of q over the whole (sharded) sequence."""
+        kq, vq = self.local.state
+        if kq is None:
+            # a rank without tokens still joins the collective with an empty shard
+            D = q.shape[-1]
+            dev = q.device
+            z = lambda w: torch.zeros((q.shape[0], 1, 0, w), dtype=torch.uint32, device=dev)
+            s = lambda: torch.zeros((q.shape[0], 1, 0, D // self.group_size), dtype=q.dtype, device=dev)
+            kq = (z(D * self.bits // 32), s(), s())
+            vq = (z(D * self.bits // 32), s(), s())
+        return sharded_quantized_sdpa(q, kq, vq, bits=self.bits, group_size=self.group_size, scale=scale,
+                                      group=self.group, partial_fn=partial_fn, combine_fn=combine_fn)
