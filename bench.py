@@ -239,11 +239,11 @@ def main():
     stream = torch.cuda.current_stream(dev)
 
     if world > 1:
+        # one packed record per rank, [o (rows x D) | m, l (rows x 2)]: one all-gather per step
         rows = B * HQ
-        part_o = torch.empty((rows, D), dtype=torch.float32, device=dev)
-        part_ml = torch.empty((rows, 2), dtype=torch.float32, device=dev)
-        gath_o = torch.empty((world, rows, D), dtype=torch.float32, device=dev)
-        gath_ml = torch.empty((world, rows, 2), dtype=torch.float32, device=dev)
+        rec = torch.empty(rows * (D + 2), dtype=torch.float32, device=dev)
+        part = (rec[: rows * D].view(rows, D), rec[rows * D:].view(rows, 2))
+        gath = torch.empty((world, rows * (D + 2)), dtype=torch.float32, device=dev)
 
     outs = [torch.empty((B, HQ, 1, D), dtype=torch.float16, device=dev) for _ in range(L)]
 
@@ -253,37 +253,35 @@ def main():
             _lib.decode(q, pk, pv, ks, vs, kb, vb, scale=scale, bits=BITS, group_size=GS, out=outs[i % L])
         else:
             _lib.decode(q, pk, pv, ks, vs, kb, vb, scale=scale, bits=BITS, group_size=GS,
-                        out_mode=_lib.OUT_PARTIAL, part=(part_o, part_ml))
-            dist.all_gather_into_tensor(gath_o, part_o)
-            dist.all_gather_into_tensor(gath_ml, part_ml)
-            outs[i % L].copy_(_lib.combine(gath_o, gath_ml, torch.float16).view(B, HQ, 1, D))
+                        out_mode=_lib.OUT_PARTIAL, part=part)
+            dist.all_gather_into_tensor(gath, rec)
+            _lib.combine_packed(gath, rows, D, out=outs[i % L].view(rows, D))
 
     # warm-up (also allocates the decode workspace outside any capture)
     for i in range(max(args.warmup, 3)):
         step(i)
     torch.cuda.synchronize(dev)
 
-    graphs = None
+    # every CUDA graph lives only in these lists (no loop variable keeps one):
+    # graphs that hold NCCL work must all be gone before destroy_process_group
+    graphs = []
     graph_note = "eager"
     if not args.no_graph:
         try:
-            graphs = []
             for l in range(L):
-                g = torch.cuda.CUDAGraph()
-                with torch.cuda.graph(g):
+                graphs.append(torch.cuda.CUDAGraph())
+                with torch.cuda.graph(graphs[l]):
                     step(l)
-                graphs.append(g)
-            del g
-            for g in graphs:
-                g.replay()
+            for l in range(L):
+                graphs[l].replay()
             torch.cuda.synchronize(dev)
             graph_note = "cuda-graph per layer"
         except Exception as e:  # noqa: BLE001
-            graphs = None
+            graphs.clear()
             graph_note = f"eager (graph capture failed: {type(e).__name__})"
 
     def run(i):
-        if graphs is not None:
+        if graphs:
             graphs[i % L].replay()
         else:
             step(i)
@@ -320,13 +318,11 @@ def main():
         kern = run
     else:
         kgraphs = []
-        if graphs is not None:
+        if graphs:
             for l in range(L):
-                gk = torch.cuda.CUDAGraph()
-                with torch.cuda.graph(gk):
+                kgraphs.append(torch.cuda.CUDAGraph())
+                with torch.cuda.graph(kgraphs[l]):
                     local_decode(l)
-                kgraphs.append(gk)
-            del gk
 
         def kern(i):
             if kgraphs:
@@ -441,12 +437,12 @@ def main():
 
     if world > 1:
         # graphs holding NCCL work must be released before the process group
-        graphs = None
-        kgraphs = None
-        kern = run = None
         torch.cuda.synchronize(dev)
+        graphs.clear()
+        kgraphs.clear()
         import gc
         gc.collect()
+        torch.cuda.synchronize(dev)
         dist.destroy_process_group()
 
 

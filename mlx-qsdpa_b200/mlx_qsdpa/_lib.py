@@ -339,6 +339,23 @@ def dequantize(packed: torch.Tensor, scales: torch.Tensor, biases: Optional[torc
     return out
 
 
+def combine_packed(gath: torch.Tensor, rows: int, D: int, out: Optional[torch.Tensor] = None,
+                   dtype: torch.dtype = torch.float16) -> torch.Tensor:
+    """Merge gathered packed records: gath (P, rows*(D+2)) fp32, each part laid
+    out as [o (rows x D) | (m, l) (rows x 2)]."""
+    lib = load()
+    P = gath.shape[0]
+    gath = gath.contiguous()
+    if out is None:
+        out = torch.empty((rows, D), dtype=dtype, device=gath.device)
+    base = gath.data_ptr()
+    stride = rows * (D + 2)
+    rc = lib.qsdpa_combine(base, base + rows * D * 4, stride, stride, P, rows, D, out.data_ptr(),
+                           dtype_code(out.dtype), _stream(gath.device))
+    _check(rc, "qsdpa_combine")
+    return out
+
+
 def combine(part_o: torch.Tensor, part_ml: torch.Tensor, dtype: torch.dtype) -> torch.Tensor:
     """Merge gathered partial records: part_o (P, rows, D), part_ml (P, rows, 2)."""
     lib = load()

@@ -66,17 +66,25 @@ def sharded_quantized_sdpa(q, k_quant, v_quant, *, bits=4, group_size=32, scale=
         raise ValueError("sharded decode expects qL == 1")
     if scale is None:
         scale = D ** -0.5
+    rows = B * Hq
+    # one packed record per rank, [o (rows x D) | m, l (rows x 2)]: one all-gather
+    rec = torch.empty(rows * (D + 2), dtype=torch.float32, device=q.device)
+    part = (rec[: rows * D].view(rows, D), rec[rows * D:].view(rows, 2))
     if partial_fn is None:
-        part_o, part_ml = _partial_cuda(q, k_quant, v_quant, scale, bits, group_size, mask)
+        _partial_cuda(q, k_quant, v_quant, scale, bits, group_size, mask, part)
     else:
-        part_o, part_ml = partial_fn(q, k_quant, v_quant, scale, bits, group_size, mask)
-    gath_o = _gather(part_o, group)
-    gath_ml = _gather(part_ml, group)
-    out = merge_partials(gath_o, gath_ml, q.dtype, combine_fn)
+        po, pml = partial_fn(q, k_quant, v_quant, scale, bits, group_size, mask)
+        part[0].copy_(po)
+        part[1].copy_(pml)
+    gath = _gather(rec, group)
+    if combine_fn is None:
+        out = _lib.combine_packed(gath, rows, D, dtype=q.dtype)
+    else:
+        out = combine_fn(gath[:, : rows * D].view(-1, rows, D), gath[:, rows * D:].view(-1, rows, 2), q.dtype)
     return out.view(B, Hq, 1, D)
 
 
-def _partial_cuda(q, k_quant, v_quant, scale, bits, group_size, mask):
+def _partial_cuda(q, k_quant, v_quant, scale, bits, group_size, mask, part):
     from .dispatch import _fused_mask, _mask_kind  # local: shared validation helpers
     pk, ks, kb = k_quant
     pv, vs, vb = v_quant
@@ -88,7 +96,7 @@ def _partial_cuda(q, k_quant, v_quant, scale, bits, group_size, mask):
         _lib.rows_contiguous(vb) if vb is not None else None, scale=scale, bits=bits, group_size=group_size,
         mask=m, mask_kind=_mask_kind(m) if m is not None else _lib.MASK_NONE,
         kv_start=ranges.start if ranges is not None else None,
-        kv_len=ranges.length if ranges is not None else None, out_mode=_lib.OUT_PARTIAL)
+        kv_len=ranges.length if ranges is not None else None, out_mode=_lib.OUT_PARTIAL, part=part)
 
 
 class SequenceShardedCache:
