@@ -23,6 +23,7 @@ std::atomic<int> g_sm_count[64];
 constexpr size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
 constexpr int kMaxSplits = 1024;
 constexpr int kMinChunk = 64;  // keys per CTA below which splitting stops paying
+constexpr int kLongChunk = 256;  // keys per CTA from which a second CTA per SM pays off
 }  // namespace
 
 int set_error(int code, const char* fmt, ...) {
@@ -156,11 +157,17 @@ Plan make_plan(const qsdpa_decode_params* p, const DecodeArgs& a) {
     const int units = a.B * a.Hkv * pl.head_blocks;
     int splits = p->splits;
     if (splits == 0) {
-        // tensor-core kernel: two CTAs per SM, one wave, every SM equally
-        // loaded (a third resident CTA on some SMs only adds imbalance);
-        // CUDA-core kernel: two waves of 4 per SM.  No chunk below kMinChunk.
-        const int target = pl.use_mma ? sm_count() * 2 : sm_count() * 4 * 2;
-        splits = (target + units - 1) / units;
+        // tensor-core kernel: one wave, one CTA per SM while chunks are short
+        // (a CTA's fixed cost dominates), growing to two per SM once every
+        // chunk holds kLongChunk keys; CUDA-core kernel: two waves of 4 per SM.
+        // No chunk below kMinChunk.
+        if (pl.use_mma) {
+            const int lo = (sm_count() + units - 1) / units, hi = (2 * sm_count() + units - 1) / units;
+            const int by_long = (p->N + kLongChunk - 1) / kLongChunk;
+            splits = by_long < lo ? lo : (by_long > hi ? hi : by_long);
+        } else {
+            splits = (sm_count() * 4 * 2 + units - 1) / units;
+        }
         const int by_len = (p->N + kMinChunk - 1) / kMinChunk;
         if (splits > by_len) splits = by_len;
         if (splits < 1) splits = 1;
@@ -168,7 +175,7 @@ Plan make_plan(const qsdpa_decode_params* p, const DecodeArgs& a) {
     }
     pl.chunk = p->N > 0 ? (p->N + splits - 1) / splits : 0;
     if (pl.use_mma && p->N > 0) {
-        // the tensor-core kernel walks whole 64-token tiles of physical keys
+        // the tensor-core kernel's chunks start on mma_tile()-token boundaries
         const int t = mma_tile();
         pl.chunk = (pl.chunk + t - 1) / t * t;
         splits = (p->N + pl.chunk - 1) / pl.chunk;

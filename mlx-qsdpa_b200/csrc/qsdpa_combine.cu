@@ -1,10 +1,8 @@
 // Merge of partial (o, m, l) records: the split-K second pass
 // (mlx_qsdpa/kernels.py:342-419) and the cross-GPU merge after an all-gather.
 //
-// Grid (rows, ceil(D/64)); a CTA of 64 x kLanes threads owns 64 output
-// dimensions of one query row, and its kLanes part-lanes walk the parts in
-// parallel before a shared-memory reduction, so hundreds of split records
-// merge in a few microseconds.  Weights are 2^(m_p - max m) in the log2
+// Grid (rows, ceil(D/64)); a CTA owns 64 output dimensions of one query row
+// (D is a multiple of 32, so float4 loads stay inside a row).  Weights are 2^(m_p - max m) in the log2
 // domain the decode kernels use; rows whose parts saw no key produce 0 (the
 // reference's global_sum == 0 guard, kernels.py:408).
 //
@@ -17,62 +15,105 @@
 namespace qsdpa {
 namespace {
 
-constexpr int kDims = 64;
-constexpr int kLanes = 4;
+constexpr int kThreadsC = 256;
+constexpr int kDimQuads = 16;                       // 4-dim groups per CTA: 64 dims
+constexpr int kSplitLanes = kThreadsC / kDimQuads;  // 16 lanes walk the parts
+constexpr int kMaxPartsSmem = 2048;
 
+__device__ __forceinline__ float block_reduce(float v, float* scratch, bool is_max) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        const float w = __shfl_xor_sync(0xffffffffu, v, o);
+        v = is_max ? fmaxf(v, w) : v + w;
+    }
+    if ((threadIdx.x & 31) == 0) scratch[threadIdx.x >> 5] = v;
+    __syncthreads();
+    v = is_max ? -INFINITY : 0.f;
+#pragma unroll
+    for (int i = 0; i < kThreadsC / 32; ++i) v = is_max ? fmaxf(v, scratch[i]) : v + scratch[i];
+    __syncthreads();
+    return v;
+}
+
+// CTA (row, 64-dim slice).  Phase 1: the parts' maxima and weights
+// w_p = 2^(m_p - max) into shared memory, and l = sum w_p l_p.  Phase 2: 16
+// lanes each walk every 16th part with float4 loads (unrolled, so several
+// records are in flight per thread), then a shared-memory reduction.
 template <typename T>
-__global__ void __launch_bounds__(kDims* kLanes)
+__global__ void __launch_bounds__(kThreadsC)
     combine_kernel(const float* __restrict__ po, const float* __restrict__ pml, int64_t so, int64_t sml, int64_t ro,
                    int64_t rml, int parts, int D, T* __restrict__ out, float* __restrict__ out_o,
                    float* __restrict__ out_ml) {
 #if defined(__CUDA_ARCH__) && __CUDA_ARCH__ >= 900
     cudaGridDependencySynchronize();
 #endif
-    __shared__ float s_red[kLanes][kDims];
-    __shared__ float s_l[kLanes];
-    __shared__ float s_m[kDims * kLanes / 32];
+    __shared__ float s_w[kMaxPartsSmem];
+    __shared__ float s_red[kSplitLanes][kDimQuads * 4 + 4];
+    __shared__ float s_scr[kThreadsC / 32];
     const int row = blockIdx.x;
-    const int dl = threadIdx.x % kDims;
-    const int pl = threadIdx.x / kDims;
-    const int d = blockIdx.y * kDims + dl;
     const float* ml = pml + (int64_t)row * rml;
+    const int tid = threadIdx.x;
 
-    // max over the parts' maxima
     float mt = -INFINITY;
-    for (int p = threadIdx.x; p < parts; p += blockDim.x) mt = fmaxf(mt, __ldcg(ml + (int64_t)p * sml));
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, o));
-    if ((threadIdx.x & 31) == 0) s_m[threadIdx.x / 32] = mt;
-    __syncthreads();
-    mt = -INFINITY;
-#pragma unroll
-    for (int w = 0; w < kDims * kLanes / 32; ++w) mt = fmaxf(mt, s_m[w]);
-
-    float lt = 0.f, ot = 0.f;
-    const float* o = po + (int64_t)row * ro + (d < D ? d : 0);
-    for (int p = pl; p < parts; p += kLanes) {
-        const float w = merge_weight(__ldcg(ml + (int64_t)p * sml), mt);
+    for (int p = tid; p < parts; p += kThreadsC) mt = fmaxf(mt, __ldcg(ml + (int64_t)p * sml));
+    mt = block_reduce(mt, s_scr, true);
+    float lt = 0.f;
+    for (int p = tid; p < parts; p += kThreadsC) {
+        const float m = __ldcg(ml + (int64_t)p * sml);
+        const float w = m == -INFINITY ? 0.f : exp2f(m - mt);
+        s_w[p] = w;
         lt += w * __ldcg(ml + (int64_t)p * sml + 1);
-        if (d < D) ot += w * __ldcg(o + (int64_t)p * so);
     }
-    s_red[pl][dl] = ot;
-    if (dl == 0) s_l[pl] = lt;
-    __syncthreads();
-    if (pl != 0 || d >= D) return;
-    ot = 0.f;
-    lt = 0.f;
+    lt = block_reduce(lt, s_scr, false);  // its __syncthreads also publishes s_w
+
+    const int dq = tid % kDimQuads, sl = tid / kDimQuads;
+    const int d = blockIdx.y * (kDimQuads * 4) + dq * 4;
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (d < D) {
+        const float* o = po + (int64_t)row * ro + d;
+        int p = sl;
+        for (; p + 3 * kSplitLanes < parts; p += 4 * kSplitLanes) {
+            float4 v[4];
 #pragma unroll
-    for (int i = 0; i < kLanes; ++i) {
-        ot += s_red[i][dl];
-        lt += s_l[i];
+            for (int u = 0; u < 4; ++u) v[u] = __ldcg(reinterpret_cast<const float4*>(o + (int64_t)(p + u * kSplitLanes) * so));
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                const float w = s_w[p + u * kSplitLanes];
+                acc.x += w * v[u].x;
+                acc.y += w * v[u].y;
+                acc.z += w * v[u].z;
+                acc.w += w * v[u].w;
+            }
+        }
+        for (; p < parts; p += kSplitLanes) {
+            const float4 v = __ldcg(reinterpret_cast<const float4*>(o + (int64_t)p * so));
+            const float w = s_w[p];
+            acc.x += w * v.x;
+            acc.y += w * v.y;
+            acc.z += w * v.z;
+            acc.w += w * v.w;
+        }
     }
-    if (out) {
-        out[(int64_t)row * D + d] = Dt<T>::from_f(lt > 0.f ? ot / lt : 0.f);
-    } else {
-        out_o[(int64_t)row * D + d] = ot;
-        if (d == 0) {
-            out_ml[2 * row] = mt;
-            out_ml[2 * row + 1] = lt;
+    s_red[sl][dq * 4 + 0] = acc.x;
+    s_red[sl][dq * 4 + 1] = acc.y;
+    s_red[sl][dq * 4 + 2] = acc.z;
+    s_red[sl][dq * 4 + 3] = acc.w;
+    __syncthreads();
+    if (tid < kDimQuads * 4) {
+        const int dd = blockIdx.y * (kDimQuads * 4) + tid;
+        if (dd < D) {
+            float ot = 0.f;
+#pragma unroll
+            for (int i = 0; i < kSplitLanes; ++i) ot += s_red[i][tid];
+            if (out) {
+                out[(int64_t)row * D + dd] = Dt<T>::from_f(lt > 0.f ? ot / lt : 0.f);
+            } else {
+                out_o[(int64_t)row * D + dd] = ot;
+                if (dd == 0) {
+                    out_ml[2 * row] = mt;
+                    out_ml[2 * row + 1] = lt;
+                }
+            }
         }
     }
 }
@@ -81,8 +122,8 @@ template <typename T>
 int launch_t(const float* po, const float* pml, int64_t so, int64_t sml, int64_t ro, int64_t rml, int parts,
              int rows, int D, void* out, float* out_o, float* out_ml, bool pdl, cudaStream_t st) {
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(rows, (D + kDims - 1) / kDims);
-    cfg.blockDim = dim3(kDims * kLanes);
+    cfg.gridDim = dim3(rows, (D + kDimQuads * 4 - 1) / (kDimQuads * 4));
+    cfg.blockDim = dim3(kThreadsC);
     cfg.dynamicSmemBytes = 0;
     cfg.stream = st;
     cudaLaunchAttribute attr[1];
@@ -116,7 +157,8 @@ extern "C" int qsdpa_combine(const float* part_o, const float* part_ml, int64_t 
                              void* stream) {
     if (parts <= 0 || rows < 0 || D <= 0 || D > 4096)
         return set_error(QSDPA_ERR_INVALID, "qsdpa_combine: bad sizes parts=%d rows=%d D=%d", parts, rows, D);
-    if (rows > 65535) return set_error(QSDPA_ERR_INVALID, "qsdpa_combine: rows=%d exceeds 65535", rows);
+    if (parts > kMaxPartsSmem)
+        return set_error(QSDPA_ERR_INVALID, "qsdpa_combine: at most %d parts, got %d", kMaxPartsSmem, parts);
     if (dtype != QSDPA_F16 && dtype != QSDPA_BF16)
         return set_error(QSDPA_ERR_INVALID, "qsdpa_combine: dtype must be QSDPA_F16 or QSDPA_BF16");
     if (rows > 0 && (!part_o || !part_ml || !out))

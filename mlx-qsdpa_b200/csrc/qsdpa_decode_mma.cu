@@ -39,7 +39,7 @@
 // removes almost every rescale of the 16 x D accumulator.
 //
 // Work decomposition: CTA = 4 warps over one (b, kv-head, 16-head block) and a
-// contiguous physical chunk of keys (a multiple of 64 tokens); each warp takes
+// contiguous physical chunk of keys (starting on an 8-token boundary); each warp takes
 // 16 tokens of every tile.  A key window (ring interval) and masks apply per
 // token; tiles entirely outside the window are skipped without loading.
 #include "qsdpa_internal.cuh"
@@ -326,7 +326,7 @@ __global__ void __launch_bounds__(kThreads, (Cfg<BITS, D, GS>::MIN_BLOCKS)) deco
         const int p0 = p_lo + tile * kTile;
         if (!win.overlaps(p0, min(p0 + kTile, p_hi))) return;  // skipped tile: nothing to load
         char* st = ring + stage * C::STAGE_BYTES;
-        const int rows_valid = min(kTile, a.N - p0);
+        const int rows_valid = min(kTile, p_hi - p0);  // rows past the chunk are zero-filled
         const int64_t tile_off = (int64_t)p0 * C::ROWB;
 #pragma unroll
         for (int k = 0; k < KCP; ++k) {
@@ -839,7 +839,10 @@ bool mma_supported(const DecodeArgs& a) {
 
 int mma_heads_per_block(const DecodeArgs&) { return 16; }
 
-int mma_tile() { return kTile; }
+// Chunk granularity of the tensor-core kernel: chunks start on 8-token
+// boundaries, which keeps every tile's scale/bias copy 16-byte aligned for any
+// group count (8 tokens x D/gs scales x 2 bytes is a multiple of 16).
+int mma_tile() { return 8; }
 
 int launch_decode_mma(const DecodeArgs& a, int dtype, cudaStream_t st) {
     if (dtype == QSDPA_F16) return a.bits == 4 ? launch2<__half, 4>(a, st) : launch2<__half, 8>(a, st);
