@@ -263,28 +263,44 @@ def main():
     torch.cuda.synchronize(dev)
 
     # every CUDA graph lives only in these lists (no loop variable keeps one):
-    # graphs that hold NCCL work must all be gone before destroy_process_group
+    # graphs that hold NCCL work must all be gone before destroy_process_group.
+    # A model captures a decode step's layers in one graph; so does the bench:
+    # graphs[0] runs the L layers' steps back to back, graphs[1 + l] layer l
+    # alone (for step counts that are not a multiple of L).
     graphs = []
     graph_note = "eager"
+
+    def capture(fn, into):
+        into.append(torch.cuda.CUDAGraph())
+        with torch.cuda.graph(into[-1]):
+            for l in range(L):
+                fn(l)
+        for l in range(L):
+            into.append(torch.cuda.CUDAGraph())
+            with torch.cuda.graph(into[-1]):
+                fn(l)
+        for g in into:
+            g.replay()
+        torch.cuda.synchronize(dev)
+
     if not args.no_graph:
         try:
-            for l in range(L):
-                graphs.append(torch.cuda.CUDAGraph())
-                with torch.cuda.graph(graphs[l]):
-                    step(l)
-            for l in range(L):
-                graphs[l].replay()
-            torch.cuda.synchronize(dev)
-            graph_note = "cuda-graph per layer"
+            capture(step, graphs)
+            graph_note = f"one cuda graph over the {L} layers' decode steps"
         except Exception as e:  # noqa: BLE001
             graphs.clear()
             graph_note = f"eager (graph capture failed: {type(e).__name__})"
 
-    def run(i):
-        if graphs:
-            graphs[i % L].replay()
-        else:
-            step(i)
+    def replay(gl, fn, K):
+        """K steps: whole L-layer graphs, then single layers for the remainder."""
+        if not gl:
+            for i in range(K):
+                fn(i)
+            return
+        for _ in range(K // L):
+            gl[0].replay()
+        for i in range(K % L):
+            gl[1 + i].replay()
 
     def barrier():
         if world > 1:
@@ -299,8 +315,7 @@ def main():
         e1 = torch.cuda.Event(enable_timing=True)
         t_host0 = time.time()
         e0.record(stream)
-        for i in range(K):
-            run(i)
+        replay(graphs, step, K)
         e1.record(stream)
         barrier()
         t_host1 = time.time()
@@ -308,33 +323,22 @@ def main():
     clocks = clk.summary(t_host0, t_host1)
 
     # ---- device duration of one decode-kernel launch (for the roofline) ----
-    # the local decode alone (no collective), captured per layer and replayed
-    # back to back between one pair of events on the launching stream
+    # the local decode alone (no collective), captured like the step and
+    # replayed back to back between one pair of events on the launching stream
     def local_decode(i):
         (pk, ks, kb), (pv, vs, vb) = layers[i % L]
         _lib.decode(q, pk, pv, ks, vs, kb, vb, scale=scale, bits=BITS, group_size=GS, out=outs[i % L])
 
+    kgraphs = []
     if world == 1:
-        kern = run
-    else:
-        kgraphs = []
-        if graphs:
-            for l in range(L):
-                kgraphs.append(torch.cuda.CUDAGraph())
-                with torch.cuda.graph(kgraphs[l]):
-                    local_decode(l)
-
-        def kern(i):
-            if kgraphs:
-                kgraphs[i % L].replay()
-            else:
-                local_decode(i)
+        kgraphs = graphs
+    elif graphs:
+        capture(local_decode, kgraphs)
     barrier()
     k0 = torch.cuda.Event(enable_timing=True)
     k1 = torch.cuda.Event(enable_timing=True)
     k0.record(stream)
-    for i in range(K):
-        kern(i)
+    replay(kgraphs, local_decode, K)
     k1.record(stream)
     barrier()
     per_launch_ms = k0.elapsed_time(k1) / K
@@ -438,8 +442,8 @@ def main():
     if world > 1:
         # graphs holding NCCL work must be released before the process group
         torch.cuda.synchronize(dev)
+        kgraphs = None
         graphs.clear()
-        kgraphs.clear()
         import gc
         gc.collect()
         torch.cuda.synchronize(dev)

@@ -30,7 +30,7 @@
 extern "C" {
 #endif
 
-#define QSDPA_ABI_VERSION 1
+#define QSDPA_ABI_VERSION 2
 
 
 /* element types */
@@ -49,6 +49,14 @@ enum {
 enum {
     QSDPA_OUT_FINAL = 0,   /* normalised attention output in the query dtype */
     QSDPA_OUT_PARTIAL = 1  /* fp32 partial record (o, m, l) for a later merge */
+};
+
+/* decode kernel selection (qsdpa_decode_params.kernel) */
+enum {
+    QSDPA_KERNEL_AUTO = 0,    /* the fastest kernel that supports the call */
+    QSDPA_KERNEL_TCGEN05 = 1, /* tcgen05 / tensor-memory kernel (GQA >= 4, D 128 or 256) */
+    QSDPA_KERNEL_MMA = 2,     /* warp-level mma.sync kernel (GQA >= 4) */
+    QSDPA_KERNEL_SIMT = 3     /* CUDA-core kernel (every supported shape) */
 };
 
 /* return codes */
@@ -130,6 +138,8 @@ typedef struct qsdpa_decode_params {
     float scale;        /* attention scale, e.g. D^-0.5 */
     int32_t splits;     /* CTAs per KV head over the keys; 0 = automatic */
     int32_t out_mode;   /* QSDPA_OUT_* */
+    int32_t kernel;     /* QSDPA_KERNEL_*; a kernel that cannot run the call
+                         * is an error (QSDPA_ERR_UNSUPPORTED), not a fallback */
 } qsdpa_decode_params;
 
 int qsdpa_decode(const qsdpa_decode_params* p, void* stream);
@@ -222,6 +232,14 @@ typedef struct qsdpa_dequantize_params {
 } qsdpa_dequantize_params;
 
 int qsdpa_dequantize(const qsdpa_dequantize_params* p, void* stream);
+
+/*
+ * Device-side faults recorded by the decode kernels since the last reset:
+ * bit 0 = a wait on a tensor-core completion barrier ran out of time (the
+ * kernel gave up after ~1 s, left its output undefined and returned instead of
+ * hanging).  Synchronises the device.  0 when healthy; `reset` != 0 clears it.
+ */
+int qsdpa_device_status(int reset);
 
 /* Message of the last failed call on this thread ("" if none). */
 const char* qsdpa_last_error(void);

@@ -24,6 +24,9 @@ constexpr size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
 constexpr int kMaxSplits = 1024;
 constexpr int kMinChunk = 64;  // keys per CTA below which splitting stops paying
 constexpr int kLongChunk = 256;  // keys per CTA from which a second CTA per SM pays off
+constexpr int kMinChunkTc = 128;  // one tile of the tcgen05 kernel
+// QSDPA_KERNEL_AUTO prefers the tcgen05 kernel where it applies
+constexpr bool kAutoTc = false;
 }  // namespace
 
 int set_error(int code, const char* fmt, ...) {
@@ -58,8 +61,11 @@ int mma_tile();
 
 namespace {
 
+enum class Kern { Tc, Mma, Simt };
+
 struct Plan {
-    bool use_mma;
+    Kern kern;
+    bool use_mma;  // a 16-head tensor-core kernel (tcgen05 or mma.sync)
     int heads_per_block;
     int head_blocks;
     int splits;
@@ -97,6 +103,8 @@ int validate(const qsdpa_decode_params* p) {
     if (p->kv_start && !p->kv_len) return set_error(QSDPA_ERR_INVALID, "kv_start given without kv_len");
     if (p->splits < 0 || p->splits > kMaxSplits)
         return set_error(QSDPA_ERR_INVALID, "splits must be in [0, %d], got %d", kMaxSplits, p->splits);
+    if (p->kernel < QSDPA_KERNEL_AUTO || p->kernel > QSDPA_KERNEL_SIMT)
+        return set_error(QSDPA_ERR_INVALID, "unknown kernel selector %d", p->kernel);
     if (p->D != 32 && p->D != 64 && p->D != 128 && p->D != 256)
         return set_error(QSDPA_ERR_UNSUPPORTED, "fused decode supports D in {32, 64, 128, 256}, got %d", p->D);
     return QSDPA_OK;
@@ -149,9 +157,27 @@ void fill_args(const qsdpa_decode_params* p, DecodeArgs& a) {
     a.scale_log2 = p->scale * kLog2e;
 }
 
-Plan make_plan(const qsdpa_decode_params* p, const DecodeArgs& a) {
-    Plan pl;
-    pl.use_mma = mma_supported(a);
+// Picks the kernel (QSDPA_KERNEL_AUTO: the fastest that supports the call)
+// and the split plan; a kernel named explicitly that cannot run the call is an
+// error.
+int make_plan(const qsdpa_decode_params* p, const DecodeArgs& a, Plan& pl) {
+    const bool tc_ok = tc_supported(a), mma_ok = mma_supported(a);
+    switch (p->kernel) {
+        case QSDPA_KERNEL_TCGEN05:
+            if (!tc_ok) return set_error(QSDPA_ERR_UNSUPPORTED, "tcgen05 kernel: needs D 128/256, GQA >= 4, 16-byte aligned K/V");
+            pl.kern = Kern::Tc;
+            break;
+        case QSDPA_KERNEL_MMA:
+            if (!mma_ok) return set_error(QSDPA_ERR_UNSUPPORTED, "mma kernel: needs D 128/256 (64 at 8 bits), GQA >= 4, 16-byte aligned K/V");
+            pl.kern = Kern::Mma;
+            break;
+        case QSDPA_KERNEL_SIMT:
+            pl.kern = Kern::Simt;
+            break;
+        default:
+            pl.kern = kAutoTc && tc_ok ? Kern::Tc : (mma_ok ? Kern::Mma : Kern::Simt);
+    }
+    pl.use_mma = pl.kern != Kern::Simt;
     pl.heads_per_block = pl.use_mma ? mma_heads_per_block(a) : simt_heads_per_block();
     pl.head_blocks = (a.gqa + pl.heads_per_block - 1) / pl.heads_per_block;
     const int units = a.B * a.Hkv * pl.head_blocks;
@@ -161,14 +187,18 @@ Plan make_plan(const qsdpa_decode_params* p, const DecodeArgs& a) {
         // (a CTA's fixed cost dominates), growing to two per SM once every
         // chunk holds kLongChunk keys; CUDA-core kernel: two waves of 4 per SM.
         // No chunk below kMinChunk.
-        if (pl.use_mma) {
+        if (pl.kern == Kern::Tc) {
+            // one CTA per SM (its shared memory fills the SM), one wave
+            splits = (sm_count() + units - 1) / units;
+        } else if (pl.use_mma) {
             const int lo = (sm_count() + units - 1) / units, hi = (2 * sm_count() + units - 1) / units;
             const int by_long = (p->N + kLongChunk - 1) / kLongChunk;
             splits = by_long < lo ? lo : (by_long > hi ? hi : by_long);
         } else {
             splits = (sm_count() * 4 * 2 + units - 1) / units;
         }
-        const int by_len = (p->N + kMinChunk - 1) / kMinChunk;
+        const int min_chunk = pl.kern == Kern::Tc ? kMinChunkTc : kMinChunk;
+        const int by_len = (p->N + min_chunk - 1) / min_chunk;
         if (splits > by_len) splits = by_len;
         if (splits < 1) splits = 1;
         if (splits > kMaxSplits) splits = kMaxSplits;
@@ -187,7 +217,7 @@ Plan make_plan(const qsdpa_decode_params* p, const DecodeArgs& a) {
         const size_t rows = (size_t)a.B * a.Hq;
         pl.ws_bytes = align256(rows * splits * a.D * sizeof(float)) + align256(rows * splits * 2 * sizeof(float));
     }
-    return pl;
+    return QSDPA_OK;
 }
 
 }  // namespace
@@ -201,14 +231,18 @@ extern "C" int qsdpa_decode_splits(const qsdpa_decode_params* p) {
     if (rc) return rc;
     DecodeArgs a;
     fill_args(p, a);
-    return make_plan(p, a).splits;
+    Plan pl;
+    rc = make_plan(p, a, pl);
+    return rc ? rc : pl.splits;
 }
 
 extern "C" size_t qsdpa_decode_workspace_size(const qsdpa_decode_params* p) {
     if (validate(p)) return 0;
     DecodeArgs a;
     fill_args(p, a);
-    return make_plan(p, a).ws_bytes;
+    Plan pl;
+    if (make_plan(p, a, pl)) return 0;
+    return pl.ws_bytes;
 }
 
 extern "C" int qsdpa_decode(const qsdpa_decode_params* p, void* stream) {
@@ -216,7 +250,9 @@ extern "C" int qsdpa_decode(const qsdpa_decode_params* p, void* stream) {
     if (rc) return rc;
     DecodeArgs a;
     fill_args(p, a);
-    const Plan pl = make_plan(p, a);
+    Plan pl;
+    rc = make_plan(p, a, pl);
+    if (rc) return rc;
     a.heads_per_block = pl.heads_per_block;
     a.head_blocks = pl.head_blocks;
     a.splits = pl.splits;
@@ -233,7 +269,9 @@ extern "C" int qsdpa_decode(const qsdpa_decode_params* p, void* stream) {
         a.ws_ml = reinterpret_cast<float*>(ws + align256(rows * pl.splits * a.D * sizeof(float)));
     }
     cudaStream_t st = static_cast<cudaStream_t>(stream);
-    rc = pl.use_mma ? launch_decode_mma(a, p->dtype, st) : launch_decode_simt(a, p->dtype, st);
+    rc = pl.kern == Kern::Tc    ? launch_decode_tc(a, p->dtype, st)
+         : pl.kern == Kern::Mma ? launch_decode_mma(a, p->dtype, st)
+                                : launch_decode_simt(a, p->dtype, st);
     if (rc) return rc;
     if (pl.splits > 1) {
         // merge the (row, split, D) workspace records with a second launch

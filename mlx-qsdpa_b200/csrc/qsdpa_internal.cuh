@@ -157,6 +157,8 @@ __device__ void finish_cta(const DecodeArgs& a, int b, int kvh, int h0, int nh, 
 // Launchers (defined in the .cu files).
 int launch_decode_simt(const DecodeArgs& a, int dtype, cudaStream_t s);
 int launch_decode_mma(const DecodeArgs& a, int dtype, cudaStream_t s);
+int launch_decode_tc(const DecodeArgs& a, int dtype, cudaStream_t s);
+bool tc_supported(const DecodeArgs& a);
 bool mma_supported(const DecodeArgs& a);
 int mma_heads_per_block(const DecodeArgs& a);
 // Merge parts of partial records (part p of row r: o at po + p*so + r*ro,

@@ -22,6 +22,8 @@ LIB_PATH = os.environ.get("QSDPA_LIB", os.path.join(_HERE, "libqsdpa.so"))
 QSDPA_F16, QSDPA_BF16 = 0, 1
 MASK_NONE, MASK_BOOL, MASK_ADD_F16, MASK_ADD_BF16, MASK_ADD_F32 = 0, 1, 2, 3, 4
 OUT_FINAL, OUT_PARTIAL = 0, 1
+KERNEL_AUTO, KERNEL_TCGEN05, KERNEL_MMA, KERNEL_SIMT = 0, 1, 2, 3
+ABI_VERSION = 2
 
 _c_i32 = ctypes.c_int32
 _c_i64 = ctypes.c_int64
@@ -46,6 +48,7 @@ class DecodeParams(ctypes.Structure):
         ("B", _c_i32), ("Hq", _c_i32), ("Hkv", _c_i32), ("N", _c_i32), ("D", _c_i32),
         ("bits", _c_i32), ("group_size", _c_i32), ("dtype", _c_i32),
         ("scale", ctypes.c_float), ("splits", _c_i32), ("out_mode", _c_i32),
+        ("kernel", _c_i32),
     ]
 
 
@@ -80,7 +83,7 @@ class DequantizeParams(ctypes.Structure):
 # Every function the C header declares (checked by the CPU test suite).
 EXPORTS = (
     "qsdpa_decode", "qsdpa_decode_noalloc", "qsdpa_decode_splits", "qsdpa_decode_workspace_size",
-    "qsdpa_combine", "qsdpa_quantize", "qsdpa_dequantize", "qsdpa_last_error",
+    "qsdpa_combine", "qsdpa_quantize", "qsdpa_dequantize", "qsdpa_device_status", "qsdpa_last_error",
     "qsdpa_abi_version",
 )
 
@@ -117,11 +120,13 @@ def load() -> ctypes.CDLL:
         lib.qsdpa_quantize.restype = ctypes.c_int
         lib.qsdpa_dequantize.argtypes = [P(DequantizeParams), _c_vp]
         lib.qsdpa_dequantize.restype = ctypes.c_int
+        lib.qsdpa_device_status.argtypes = [ctypes.c_int]
+        lib.qsdpa_device_status.restype = ctypes.c_int
         lib.qsdpa_last_error.argtypes = []
         lib.qsdpa_last_error.restype = ctypes.c_char_p
         lib.qsdpa_abi_version.argtypes = []
         lib.qsdpa_abi_version.restype = ctypes.c_int
-        if lib.qsdpa_abi_version() != 1:
+        if lib.qsdpa_abi_version() != ABI_VERSION:
             raise RuntimeError("libqsdpa.so ABI version mismatch")
         _lib = lib
         return lib
@@ -199,7 +204,8 @@ def decode(q: torch.Tensor, kp, vp, ks, vs, kb, vb, *, scale: float, bits: int, 
            mask: Optional[torch.Tensor] = None, mask_kind: int = MASK_NONE,
            kv_start: Optional[torch.Tensor] = None, kv_len: Optional[torch.Tensor] = None,
            splits: int = 0, out_mode: int = OUT_FINAL,
-           out: Optional[torch.Tensor] = None, part: Optional[Tuple[torch.Tensor, torch.Tensor]] = None):
+           out: Optional[torch.Tensor] = None, part: Optional[Tuple[torch.Tensor, torch.Tensor]] = None,
+           kernel: int = KERNEL_AUTO):
     """Fused decode through ``qsdpa_decode``.
 
     q: (B, Hq, 1, D); kp/vp: (B, Hkv, N, pd) uint32; ks/vs/kb/vb: (B, Hkv, N, G).
@@ -231,6 +237,7 @@ def decode(q: torch.Tensor, kp, vp, ks, vs, kb, vb, *, scale: float, bits: int, 
     p.scale = float(scale)
     p.splits = int(splits)
     p.out_mode = out_mode
+    p.kernel = int(kernel)
     if out_mode == OUT_FINAL:
         if out is None:
             out = torch.empty((B, Hq, 1, D), dtype=q.dtype, device=dev)
@@ -250,7 +257,8 @@ def decode(q: torch.Tensor, kp, vp, ks, vs, kb, vb, *, scale: float, bits: int, 
     return out if out_mode == OUT_FINAL else part
 
 
-def plan_splits(q, kp, vp, ks, vs, kb, vb, bits: int, group_size: int, splits: int = 0) -> int:
+def plan_splits(q, kp, vp, ks, vs, kb, vb, bits: int, group_size: int, splits: int = 0,
+                kernel: int = KERNEL_AUTO) -> int:
     """Split count qsdpa_decode will use for these tensors (host-only query)."""
     lib = load()
     B, Hq, _, D = q.shape
@@ -266,10 +274,16 @@ def plan_splits(q, kp, vp, ks, vs, kb, vb, bits: int, group_size: int, splits: i
     p.out = 1
     p.B, p.Hq, p.Hkv, p.N, p.D = B, Hq, kp.shape[1], kp.shape[2], D
     p.bits, p.group_size, p.dtype, p.splits = bits, group_size, dtype_code(q.dtype), splits
+    p.kernel = int(kernel)
     p.scale = 1.0
     rc = lib.qsdpa_decode_splits(ctypes.byref(p))
     _check(rc if rc < 0 else 0, "qsdpa_decode_splits")
     return rc
+
+
+def device_status(reset: bool = False) -> int:
+    """Device-side fault bits recorded by the decode kernels (0 = healthy)."""
+    return int(load().qsdpa_device_status(1 if reset else 0))
 
 
 def decode_splits(q_shape, Hkv: int, N: int, D: int, bits: int, group_size: int, splits: int = 0) -> int:
