@@ -14,7 +14,8 @@
 // k, q.k, online softmax, dequantise v, accumulate) done for a 128-token tile
 // at a time.
 //
-// Roles (8 warps, one CTA per SM):
+// Roles (10 warps, one CTA per SM), handing work to each other through
+// mbarriers only -- no CTA-wide barrier inside the key loop:
 //   * warps 0-3 ("key warps"): thread t owns token t of the tile.  It
 //     dequantises the token's packed key row (scale * code + bias, one
 //     rounding) straight into its TMEM lane, then, once the S MMA is done,
@@ -23,11 +24,17 @@
 //     than 2^8) and writes the token's 16 probabilities as one row of P^T.
 //   * warps 4-7 ("value warps"): thread t dequantises token t's value row into
 //     the V^T operand (128-byte swizzled, head dims contiguous).
-//   * thread 0 issues the MMAs (tcgen05.mma, completion via tcgen05.commit on
-//     an mbarrier).
-// Packed rows, scales and biases of the next tiles stream into a ring of
-// shared-memory stages with 16-byte cp.async, rows stored with the XOR-128B
-// swizzle so a thread reading its own row is bank-conflict free.
+//   * warp 8 ("producer"): streams packed rows, scales and biases of the next
+//     tiles into a ring of shared-memory stages with 16-byte cp.async (rows
+//     stored with the XOR-128B swizzle, so a thread reading its own row is
+//     bank-conflict free); completion is signalled on the stage's "full"
+//     mbarrier by cp.async.mbarrier.arrive, consumers release it on "empty".
+//   * warp 9: owns the tensor memory and issues the MMAs from one thread
+//     (tcgen05.mma; completion via tcgen05.commit on mbarriers).  It issues
+//     the S MMA of tile j+1 before the P V MMA of tile j, so the key warps
+//     dequantise tile j+1 while the scores of tile j are computed.
+// Buffers: two K operands and two S^T accumulators in TMEM, one P^T operand,
+// two V^T operands in shared memory when they fit (values run a tile ahead).
 //
 // Dimension order: the exact nibble -> half conversion yields the pairs
 // (d, d+4) of each 8-dim word, so K columns and V^T rows hold the head dims of
@@ -49,15 +56,23 @@ namespace {
 
 using namespace dev;
 
-constexpr int kTcThreads = 256;
-constexpr int kTcTile = 128;   // tokens per tile = M of the S MMA
-constexpr int kTcHeads = 16;   // query heads per CTA = N of both MMAs
-constexpr int kTmemCols = 256;
-constexpr int kTmemS = 0;      // S^T: 16 columns
-constexpr int kTmemO = 16;     // O^T: 16 columns per 128 head dims
-constexpr int kTmemK = 64;     // K operand: D/2 columns
+constexpr int kKeyWarps = 4;    // warps 0-3: keys -> TMEM, softmax
+constexpr int kValWarps = 4;    // warps 4-7: values -> V^T operand
+constexpr int kProdWarp = 8;    // ring producer (cp.async)
+constexpr int kMmaWarp = 9;     // TMEM owner and MMA issuer
+constexpr int kTcThreads = 320;
+constexpr int kTcTile = 128;    // tokens per tile = M of the S MMA
+constexpr int kTcHeads = 16;    // query heads per CTA = N of both MMAs
+constexpr int kTmemCols = 512;  // the whole SM's tensor memory: one CTA per SM
+constexpr int kTmemS = 0;       // S^T: two buffers of 16 columns
+constexpr int kTmemO = 32;      // O^T: 16 columns per 128 head dims
+constexpr int kTmemK = 64;      // K operand: two buffers of D/2 columns
 constexpr float kRescaleTc = 8.f;
 constexpr unsigned long long kWaitNs = 1000000000ull;
+constexpr int kSmemLimit = 227 * 1024;
+// tiles the producer asks L2 for ahead of its cp.async stream (0 = none;
+// measured: the extra L2 traffic costs more than the latency it hides)
+constexpr int kPrefetchTiles = 0;
 
 template <int BITS, int D, int GS>
 struct TcCfg {
@@ -71,20 +86,24 @@ struct TcCfg {
     static constexpr int SC_BYTES = kTcTile * SROWB;
     static constexpr int SC_CHUNKS = SC_BYTES / 16;
     static constexpr int STAGE_BYTES = 2 * PACK_BYTES + 4 * SC_BYTES;
-    static constexpr int V_BYTES = kTcTile * D * 2;       // V^T operand
+    static constexpr int V_BYTES = kTcTile * D * 2;       // one V^T operand
     static constexpr int V_LBO = (kTcTile / 8) * 1024;    // between 64-dim blocks
     static constexpr int Q_BYTES = kTcHeads * D * 2;      // Q operand
-    static constexpr int P_BYTES = kTcTile * kTcHeads * 2;  // one P^T operand
+    static constexpr int P_BYTES = kTcTile * kTcHeads * 2;  // one P^T operand (hi; lo follows)
     static constexpr int MISC_BYTES = 1024;
-    static constexpr int FIXED = 1024 + V_BYTES + Q_BYTES + 2 * P_BYTES + MISC_BYTES;
-    static constexpr int STAGES_FIT = (227 * 1024 - FIXED) / STAGE_BYTES;
-    static constexpr int STAGES = STAGES_FIT > 3 ? 3 : STAGES_FIT;
-    static constexpr int SMEM = FIXED + STAGES * STAGE_BYTES;
+    static constexpr int FIXED = 1024 + Q_BYTES + 2 * P_BYTES + MISC_BYTES;
+    // two V^T buffers (values run a tile ahead) when two ring stages still fit
+    static constexpr int VBUFS = FIXED + 2 * V_BYTES + 2 * STAGE_BYTES <= kSmemLimit ? 2 : 1;
+    static constexpr int STAGES_FIT = (kSmemLimit - FIXED - VBUFS * V_BYTES) / STAGE_BYTES;
+    static constexpr int STAGES = STAGES_FIT > 4 ? 4 : STAGES_FIT;
+    // at least 116 KB so no second CTA shares the SM (and its tensor memory)
+    static constexpr int SMEM_RAW = FIXED + VBUFS * V_BYTES + STAGES * STAGE_BYTES;
+    static constexpr int SMEM = SMEM_RAW > 116 * 1024 ? SMEM_RAW : 116 * 1024;
     static constexpr int MB = D / 128;  // 128-dim blocks of O^T
     static_assert(STAGES >= 2, "two ring stages must fit");
     static_assert(STAGES * STAGE_BYTES >= kTcHeads * D * 4 + 2 * kTcHeads * 4, "merge area must fit in the ring");
-    static_assert(SC_BYTES % 16 == 0 && CPR >= 2 && (CPR % 2) == 0, "copy plan");
-    static_assert(kTmemK + D / 2 <= kTmemCols && kTmemO + 16 * MB <= kTmemK, "TMEM budget");
+    static_assert(SC_BYTES % 16 == 0 && CPR >= 2, "copy plan");
+    static_assert(kTmemK + D <= kTmemCols && kTmemO + 16 * MB <= kTmemK, "TMEM budget");
 };
 
 // ----------------------------------------------------------- tcgen05 PTX --
@@ -184,6 +203,17 @@ __host__ __device__ constexpr uint32_t make_idesc(bool bf16, bool a_mn, bool b_m
 __device__ __forceinline__ void mbar_init(uint32_t addr, int count) {
     asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;\n" ::"r"(addr), "r"(count) : "memory");
 }
+__device__ __forceinline__ void mbar_arrive(uint32_t addr) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];\n" ::"r"(addr) : "memory");
+}
+// bulk prefetch of [p, p + bytes) into L2 (16-byte aligned address and size)
+__device__ __forceinline__ void prefetch_l2(const void* p, uint32_t bytes) {
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;\n" ::"l"(p), "r"(bytes) : "memory");
+}
+// arrive once every cp.async this thread issued so far has landed
+__device__ __forceinline__ void cp_async_mbar_arrive(uint32_t addr) {
+    asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];\n" ::"r"(addr) : "memory");
+}
 __device__ __forceinline__ bool mbar_try(uint32_t addr, uint32_t parity) {
     uint32_t ok;
     asm volatile(
@@ -199,14 +229,10 @@ __device__ __forceinline__ uint64_t global_ns() {
     return t;
 }
 // Wait for completion of the phase with the given parity, for at most about a
-// second.  A thread whose wait ran out (or that sees a fault already recorded)
-// stops waiting from then on, so the kernel still finishes.
+// second.  A thread whose wait ran out stops waiting from then on, so the
+// kernel still finishes.
 __device__ __forceinline__ void mbar_wait(uint32_t addr, uint32_t parity, bool& dead) {
     if (dead || mbar_try(addr, parity)) return;
-    if (*reinterpret_cast<volatile unsigned int*>(&g_device_status) != 0u) {
-        dead = true;
-        return;
-    }
     const uint64_t t0 = global_ns();
     while (!mbar_try(addr, parity)) {
         if (global_ns() - t0 > kWaitNs) {
@@ -229,31 +255,10 @@ __device__ __forceinline__ int tc_dim(int m) {
     }
 }
 
-// One broadcast (x, x) pair per group of a scale / bias row of G halves.
-template <int G>
-__device__ __forceinline__ void load_pairs(const char* row, uint32_t out[G]) {
-    if constexpr (G == 8) {
-        const uint4 v = lds128(row);
-        const uint32_t w[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-            out[2 * i] = __byte_perm(w[i], 0u, 0x1010);
-            out[2 * i + 1] = __byte_perm(w[i], 0u, 0x3232);
-        }
-    } else if constexpr (G == 4) {
-        const uint2 v = lds64(row);
-        out[0] = __byte_perm(v.x, 0u, 0x1010);
-        out[1] = __byte_perm(v.x, 0u, 0x3232);
-        out[2] = __byte_perm(v.y, 0u, 0x1010);
-        out[3] = __byte_perm(v.y, 0u, 0x3232);
-    } else if constexpr (G == 2) {
-        const uint32_t v = lds32(row);
-        out[0] = __byte_perm(v, 0u, 0x1010);
-        out[1] = __byte_perm(v, 0u, 0x3232);
-    } else {
-        const uint32_t v = lds16(row);
-        out[0] = v | (v << 16);
-    }
+// (x, x) pair of the half at p
+__device__ __forceinline__ uint32_t pair_at(const char* p) {
+    const uint32_t v = lds16(p);
+    return v | (v << 16);
 }
 
 // Dequantise one 16-byte chunk (4 packed words) of a row: 4-bit -> 16 pairs,
@@ -283,21 +288,31 @@ __global__ void __launch_bounds__(kTcThreads, 1) decode_tc_kernel(const DecodeAr
     constexpr uint32_t IDESC_PV = make_idesc(kBf16, true, true, 128, kTcHeads);
     constexpr int EPC = 16 * 8 / BITS;  // codes per 16-byte chunk
     constexpr int PPC = EPC / 2;        // half2 pairs per chunk
+    constexpr int ST = C::STAGES;
+    constexpr int VB = C::VBUFS;
 
     extern __shared__ __align__(1024) char smem_raw[];
     // 1024-byte alignment of the swizzled operands (in the shared window)
     const uint32_t raw_u32 = smem_u32(smem_raw);
     char* smem = smem_raw + (((raw_u32 + 1023u) & ~1023u) - raw_u32);
-    char* sV = smem;
-    char* sQ = sV + C::V_BYTES;
-    char* sP = sQ + C::Q_BYTES;
-    char* ring = sP + 2 * C::P_BYTES;
-    char* misc = ring + C::STAGES * C::STAGE_BYTES;
-    const uint32_t mbar_s = smem_u32(misc);
-    const uint32_t mbar_o = smem_u32(misc + 8);
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(misc + 16);
-    int* flags = reinterpret_cast<int*>(misc + 32);     // [4]
-    float* red = reinterpret_cast<float*>(misc + 64);   // [4][16]
+    char* sV = smem;                        // VB x V^T operand
+    char* sQ = sV + VB * C::V_BYTES;        // Q operand
+    char* sP = sQ + C::Q_BYTES;             // P^T operand: hi, lo
+    char* ring = sP + 2 * C::P_BYTES;       // ST stages of packed rows + scales
+    char* misc = ring + ST * C::STAGE_BYTES;
+    // mbarriers (8 bytes each)
+    const uint32_t mb0 = smem_u32(misc);
+    auto full_bar = [&](int s) { return mb0 + 8u * s; };                // count 32 (producer lanes)
+    auto empty_bar = [&](int s) { return mb0 + 8u * (4 + s); };         // count 8 (consumer warps)
+    auto kready_bar = [&](int k) { return mb0 + 8u * (8 + k); };        // count 4 (key warps)
+    auto sready_bar = [&](int k) { return mb0 + 8u * (10 + k); };       // count 1 (commit)
+    const uint32_t pready_bar = mb0 + 8u * 12;                          // count 4 (key warps)
+    const uint32_t pfree_bar = mb0 + 8u * 13;                           // count 1 (commit)
+    auto vready_bar = [&](int v) { return mb0 + 8u * (14 + v); };       // count 4 (value warps)
+    auto vfree_bar = [&](int v) { return mb0 + 8u * (16 + v); };        // count 1 (commit)
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(misc + 160);
+    int* flags = reinterpret_cast<int*>(misc + 192);    // [4]
+    float* red = reinterpret_cast<float*>(misc + 256);  // [4][16]
     const uint32_t sV_u = smem_u32(sV), sQ_u = smem_u32(sQ), sP_u = smem_u32(sP);
 
     const int split = blockIdx.x;
@@ -310,8 +325,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) decode_tc_kernel(const DecodeAr
     const int tid = threadIdx.x;
     const int warp = tid >> 5;
     const int lane = tid & 31;
-    const bool key_warp = warp < 4;
-    const int t = tid & (kTcTile - 1);  // token of the tile owned by this thread
+    const int t = tid & (kTcTile - 1);  // key / value warps: token of the tile owned by this thread
 
     Window win;
     key_window(a, b, win.start, win.len);
@@ -320,6 +334,11 @@ __global__ void __launch_bounds__(kTcThreads, 1) decode_tc_kernel(const DecodeAr
     const int p_lo = split * a.chunk;
     const int p_hi = min(a.N, p_lo + a.chunk);
     const int ntiles = p_hi > p_lo ? (p_hi - p_lo + kTcTile - 1) / kTcTile : 0;
+    // next tile at or after i that holds a key of the window (every role walks the same list)
+    auto advance = [&](int i) {
+        while (i < ntiles && !win.overlaps(p_lo + i * kTcTile, min(p_lo + (i + 1) * kTcTile, p_hi))) ++i;
+        return i;
+    };
 
     const char* kp_b = reinterpret_cast<const char*>(a.kp + (int64_t)b * a.kp_sb + (int64_t)kvh * a.kp_sh);
     const char* vp_b = reinterpret_cast<const char*>(a.vp + (int64_t)b * a.vp_sb + (int64_t)kvh * a.vp_sh);
@@ -331,52 +350,30 @@ __global__ void __launch_bounds__(kTcThreads, 1) decode_tc_kernel(const DecodeAr
     const char* vb = has_bias ? static_cast<const char*>(a.vb) + ((int64_t)b * a.vb_sb + (int64_t)kvh * a.vb_sh) * 2
                               : nullptr;
 
-    // ---- copy plan: every thread copies CPR/2 chunks of each packed array ----
-    auto load_tile = [&](int tile, int stage) {
-        const int p0 = p_lo + tile * kTcTile;
-        if (!win.overlaps(p0, min(p0 + kTcTile, p_hi))) return;
-        char* st = ring + stage * C::STAGE_BYTES;
-        const int rows_valid = min(kTcTile, p_hi - p0);
-        const int64_t tile_off = (int64_t)p0 * C::ROWB;
-#pragma unroll
-        for (int k = 0; k < C::CPR / 2; ++k) {
-            const int i = tid + k * kTcThreads;
-            const int r = i / C::CPR, c = i - r * C::CPR;
-            const bool ok = r < rows_valid;
-            const int dst = swz<C::CPR>(r, c) * 16;
-            const int64_t off = ok ? tile_off + r * C::ROWB + c * 16 : 0;
-            cp_async16(st + dst, kp_b + off, ok ? 16 : 0);
-            cp_async16(st + C::PACK_BYTES + dst, vp_b + off, ok ? 16 : 0);
-        }
-        const int sbytes = rows_valid * C::SROWB;
-        char* s0 = st + 2 * C::PACK_BYTES;
-        for (int i = tid; i < C::SC_CHUNKS; i += kTcThreads) {
-            const int off = i * 16;
-            const int n = max(0, min(16, sbytes - off));
-            const int64_t goff = (int64_t)p0 * C::SROWB + (n > 0 ? off : 0);
-            cp_async16(s0 + off, ks + goff, n);
-            cp_async16(s0 + 2 * C::SC_BYTES + off, vs + goff, n);
-            if (has_bias) {
-                cp_async16(s0 + C::SC_BYTES + off, kb + goff, n);
-                cp_async16(s0 + 3 * C::SC_BYTES + off, vb + goff, n);
-            }
-        }
-    };
-
-    // ---- prologue: TMEM, barriers, Q operand, first tiles ----
-    if (warp == 0) {
+    // ---- prologue: TMEM, barriers, Q operand ----
+    if (warp == kMmaWarp) {
         tmem_alloc(smem_u32(tmem_slot), kTmemCols);
         tmem_relinquish();
     }
     if (tid == 0) {
-        mbar_init(mbar_s, 1);
-        mbar_init(mbar_o, 1);
-        asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
-    }
 #pragma unroll
-    for (int i = 0; i < C::STAGES - 1; ++i) {
-        if (i < ntiles) load_tile(i, i);
-        cp_async_commit();
+        for (int s = 0; s < ST; ++s) {
+            mbar_init(full_bar(s), 32);
+            mbar_init(empty_bar(s), kKeyWarps + kValWarps);
+        }
+#pragma unroll
+        for (int k = 0; k < 2; ++k) {
+            mbar_init(kready_bar(k), kKeyWarps);
+            mbar_init(sready_bar(k), 1);
+        }
+        mbar_init(pready_bar, kKeyWarps);
+        mbar_init(pfree_bar, 1);
+#pragma unroll
+        for (int v = 0; v < VB; ++v) {
+            mbar_init(vready_bar(v), kValWarps);
+            mbar_init(vfree_bar(v), 1);
+        }
+        asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
     }
     {
         // Q rows h0.. of this KV head, K-major with the 128-byte swizzle:
@@ -416,82 +413,174 @@ __global__ void __launch_bounds__(kTcThreads, 1) decode_tc_kernel(const DecodeAr
     __syncthreads();
     tc_fence_after();
     const uint32_t tbase = *tmem_slot;
-    const uint32_t lane_off = (uint32_t)((warp & 3) * 32) << 16;
+    bool dead = false;
 
     float m_run[kTcHeads], l_run[kTcHeads];
 #pragma unroll
     for (int h = 0; h < kTcHeads; ++h) m_run[h] = -INFINITY, l_run[h] = 0.f;
-    bool o_used = false;     // a P V MMA has written O^T
-    bool o_pending = false;  // ... and this thread has not yet waited for it
-    uint32_t ph_s = 0, ph_o = 0;
-    bool dead = false;
-    const int64_t mrow = a.mask ? (int64_t)b * a.m_sb : 0;
-    const int hq0 = kvh * a.gqa + h0;
+    int n_active = 0;
 
-    for (int tile = 0; tile < ntiles; ++tile) {
-        cp_async_wait<C::STAGES - 2>();
-        __syncthreads();
-        {
-            const int nxt = tile + C::STAGES - 1;
-            if (nxt < ntiles) load_tile(nxt, nxt % C::STAGES);
-            cp_async_commit();
-        }
-        const int p0 = p_lo + tile * kTcTile;
-        if (!win.overlaps(p0, min(p0 + kTcTile, p_hi))) continue;  // uniform
-        const char* st = ring + (tile % C::STAGES) * C::STAGE_BYTES;
-        const char* s_sc = st + 2 * C::PACK_BYTES + t * C::SROWB;  // this token's key scale row
-
-        if (key_warp) {
-            // ---------------- K row -> TMEM lane t ----------------
-            {
-                uint32_t sc[C::G], bi[C::G];
-                load_pairs<C::G>(s_sc, sc);
+    if (warp == kProdWarp) {
+        // ================= producer: ring stages with 16-byte cp.async =================
+        // lane 0 keeps bulk L2 prefetches kPrefetchTiles active tiles ahead
+        auto prefetch = [&](int i) {
+            const int p0 = p_lo + i * kTcTile;
+            const int rows = min(kTcTile, p_hi - p0);
+            const uint32_t pb = (uint32_t)(rows * C::ROWB);
+            const uint32_t sb = (uint32_t)(rows * C::SROWB) & ~15u;
+            prefetch_l2(kp_b + (int64_t)p0 * C::ROWB, pb);
+            prefetch_l2(vp_b + (int64_t)p0 * C::ROWB, pb);
+            if (sb) {
+                prefetch_l2(ks + (int64_t)p0 * C::SROWB, sb);
+                prefetch_l2(vs + (int64_t)p0 * C::SROWB, sb);
                 if (has_bias) {
-                    load_pairs<C::G>(s_sc + C::SC_BYTES, bi);
-                } else {
-#pragma unroll
-                    for (int g = 0; g < C::G; ++g) bi[g] = 0u;
-                }
-                constexpr int CPS = 32 / PPC;  // chunks per 32-column store
-#pragma unroll
-                for (int c0 = 0; c0 < C::CPR; c0 += CPS) {
-                    uint32_t cols[32];
-#pragma unroll
-                    for (int u = 0; u < CPS; ++u) {
-                        const int c = c0 + u;
-                        const uint4 w4 = lds128(st + swz<C::CPR>(t, c) * 16);
-                        const int g = (c * EPC) / GS;
-                        dequant_chunk<T, BITS>(w4, sc[g], bi[g], &cols[u * PPC]);
-                    }
-                    tmem_st32(tbase + lane_off + kTmemK + c0 * PPC, cols);
+                    prefetch_l2(kb + (int64_t)p0 * C::SROWB, sb);
+                    prefetch_l2(vb + (int64_t)p0 * C::SROWB, sb);
                 }
             }
-            tmem_wait_st();
-            tc_fence_before();
-            named_barrier(1, 128);
-            if (tid == 0) {
+        };
+        int ipf = advance(0);
+        if (kPrefetchTiles > 0 && lane == 0) {
+            for (int k = 0; k < kPrefetchTiles && ipf < ntiles; ++k, ipf = advance(ipf + 1)) prefetch(ipf);
+        }
+        int j = 0;
+        for (int i = advance(0); i < ntiles; i = advance(i + 1), ++j) {
+            if (kPrefetchTiles > 0 && lane == 0 && ipf < ntiles) {
+                prefetch(ipf);
+                ipf = advance(ipf + 1);
+            }
+            const int s = j % ST;
+            if (j >= ST) mbar_wait(empty_bar(s), ((j / ST) - 1) & 1, dead);
+            const int p0 = p_lo + i * kTcTile;
+            char* st = ring + s * C::STAGE_BYTES;
+            const int rows_valid = min(kTcTile, p_hi - p0);
+            const int64_t tile_off = (int64_t)p0 * C::ROWB;
+            for (int k = lane; k < kTcTile * C::CPR; k += 32) {
+                const int r = k / C::CPR, c = k - r * C::CPR;
+                const bool ok = r < rows_valid;
+                const int dst = swz<C::CPR>(r, c) * 16;
+                const int64_t off = ok ? tile_off + r * C::ROWB + c * 16 : 0;
+                cp_async16(st + dst, kp_b + off, ok ? 16 : 0);
+                cp_async16(st + C::PACK_BYTES + dst, vp_b + off, ok ? 16 : 0);
+            }
+            const int sbytes = rows_valid * C::SROWB;
+            char* s0 = st + 2 * C::PACK_BYTES;
+            for (int k = lane; k < C::SC_CHUNKS; k += 32) {
+                const int off = k * 16;
+                const int n = max(0, min(16, sbytes - off));
+                const int64_t goff = (int64_t)p0 * C::SROWB + (n > 0 ? off : 0);
+                cp_async16(s0 + off, ks + goff, n);
+                cp_async16(s0 + 2 * C::SC_BYTES + off, vs + goff, n);
+                if (has_bias) {
+                    cp_async16(s0 + C::SC_BYTES + off, kb + goff, n);
+                    cp_async16(s0 + 3 * C::SC_BYTES + off, vb + goff, n);
+                }
+            }
+            cp_async_mbar_arrive(full_bar(s));
+        }
+        cp_async_wait<0>();
+    } else if (warp == kMmaWarp) {
+        // ================= MMA issuer (one thread) =================
+        if (lane == 0) {
+            auto issue_qk = [&](int j) {
+                const int kbuf = j & 1;
+                mbar_wait(kready_bar(kbuf), (j >> 1) & 1, dead);
                 tc_fence_after();
 #pragma unroll
                 for (int ks_ = 0; ks_ < D / 16; ++ks_) {
                     const uint64_t qd = smem_desc(sQ_u + (ks_ >> 2) * 2048 + (ks_ & 3) * 32, 16, 1024, kSw128);
-                    mma_ts(tbase + kTmemS, tbase + kTmemK + ks_ * 8, qd, IDESC_QK, ks_ > 0 ? 1u : 0u);
+                    mma_ts(tbase + kTmemS + 16 * kbuf, tbase + kTmemK + kbuf * (D / 2) + ks_ * 8, qd, IDESC_QK,
+                           ks_ > 0 ? 1u : 0u);
                 }
-                mma_commit(mbar_s);
+                mma_commit(sready_bar(kbuf));
+            };
+            int n = 0;
+            for (int i = advance(0); i < ntiles; i = advance(i + 1)) ++n;
+            if (n > 0) issue_qk(0);
+            for (int j = 0; j < n; ++j) {
+                if (j + 1 < n) issue_qk(j + 1);
+                const int vbuf = j % VB;
+                mbar_wait(pready_bar, j & 1, dead);
+                mbar_wait(vready_bar(vbuf), (j / VB) & 1, dead);
+                tc_fence_after();
+#pragma unroll
+                for (int mb = 0; mb < C::MB; ++mb) {
+#pragma unroll
+                    for (int ks_ = 0; ks_ < kTcTile / 16; ++ks_) {
+                        const uint64_t vd = smem_desc(sV_u + vbuf * C::V_BYTES + (2 * mb) * C::V_LBO + (2 * ks_) * 1024,
+                                                      C::V_LBO, 1024, kSw128);
+                        const uint64_t pd = smem_desc(sP_u + ks_ * 512, C::P_BYTES, 256, kSw32);
+                        mma_ss(tbase + kTmemO + mb * 16, vd, pd, IDESC_PV, (j > 0 || ks_ > 0) ? 1u : 0u);
+                        if constexpr (Ops<T>::kSplitP) {
+                            const uint64_t pl = smem_desc(sP_u + C::P_BYTES + ks_ * 512, C::P_BYTES, 256, kSw32);
+                            mma_ss(tbase + kTmemO + mb * 16, vd, pl, IDESC_PV, 1u);
+                        }
+                    }
+                }
+                mma_commit(pfree_bar);
+                mma_commit(vfree_bar(vbuf));
             }
-            mbar_wait(mbar_s, ph_s, dead);
-            ph_s ^= 1u;
+        }
+        __syncwarp();
+    } else if (warp < kKeyWarps) {
+        // ================= key warps: K -> TMEM, softmax, P^T =================
+        const uint32_t lane_off = (uint32_t)(warp * 32) << 16;
+        const int64_t mrow = a.mask ? (int64_t)b * a.m_sb : 0;
+        const int hq0 = kvh * a.gqa + h0;
+        // dequantise the j-th active tile into K buffer j & 1 of TMEM lane t
+        auto load_keys = [&](int j) {
+            const int s = j % ST;
+            mbar_wait(full_bar(s), (j / ST) & 1, dead);
+            const char* st = ring + s * C::STAGE_BYTES;
+            const char* s_sc = st + 2 * C::PACK_BYTES + t * C::SROWB;
+            constexpr int CPS = 32 / PPC;  // chunks per 32-column store
+            const uint32_t kcol = tbase + lane_off + kTmemK + (j & 1) * (D / 2);
+#pragma unroll 1
+            for (int c0 = 0; c0 < C::CPR; c0 += CPS) {
+                uint32_t cols[32];
+#pragma unroll
+                for (int u = 0; u < CPS; ++u) {
+                    const int c = c0 + u;
+                    const int g = (c * EPC) / GS;
+                    const uint32_t s2 = pair_at(s_sc + g * 2);
+                    const uint32_t b2 = has_bias ? pair_at(s_sc + C::SC_BYTES + g * 2) : 0u;
+                    dequant_chunk<T, BITS>(lds128(st + swz<C::CPR>(t, c) * 16), s2, b2, &cols[u * PPC]);
+                }
+                tmem_st32(kcol + c0 * PPC, cols);
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(empty_bar(s));
+            tmem_wait_st();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(kready_bar(j & 1));
+        };
+
+        // step j: keys of active tile j into TMEM, then the softmax of tile j - 1
+        // (whose S MMA ran meanwhile)
+        int i_cur = advance(0), i_prev = -1, j = 0;
+        for (;; ++j) {
+            if (i_cur < ntiles) load_keys(j);
+            if (j == 0) {
+                if (i_cur >= ntiles) break;
+                i_prev = i_cur;
+                i_cur = advance(i_cur + 1);
+                continue;
+            }
+            const int js = j - 1;  // the tile whose scores are ready
+            const int i = i_prev;
+            mbar_wait(sready_bar(js & 1), (js >> 1) & 1, dead);
             tc_fence_after();
             float s[kTcHeads];
-            tmem_ld16(tbase + lane_off + kTmemS, s);
+            tmem_ld16(tbase + lane_off + kTmemS + 16 * (js & 1), s);
             tmem_wait_ld();
-            if (o_pending) {  // the previous tile's P V product has read P^T
-                mbar_wait(mbar_o, ph_o, dead);
-                ph_o ^= 1u;
-                o_pending = false;
+            if (js > 0) {  // the previous P V product is done: P^T free, O^T current
+                mbar_wait(pfree_bar, (js - 1) & 1, dead);
                 tc_fence_after();
             }
 
             // ---------------- online softmax for token p0 + t ----------------
+            const int p0 = p_lo + i * kTcTile;
             const int tok = p0 + t;
             const bool valid = tok < p_hi && win.contains(tok);
 #pragma unroll
@@ -506,8 +595,10 @@ __global__ void __launch_bounds__(kTcThreads, 1) decode_tc_kernel(const DecodeAr
             for (int h = 0; h < kTcHeads; ++h) up |= s[h] > m_run[h] + kRescaleTc;
             const bool wup = __any_sync(0xffffffffu, up);
             if (lane == 0) flags[warp] = wup ? 1 : 0;
-            named_barrier(1, 128);
-            if (flags[0] | flags[1] | flags[2] | flags[3]) {
+            named_barrier(1, kKeyWarps * 32);
+            const bool tile_up = (flags[0] | flags[1] | flags[2] | flags[3]) != 0;
+            named_barrier(1, kKeyWarps * 32);  // flags read before the next tile's writes
+            if (tile_up) {
                 // a score rose past the running maximum: tile maxima per head
                 float mx[kTcHeads];
 #pragma unroll
@@ -521,7 +612,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) decode_tc_kernel(const DecodeAr
 #pragma unroll
                     for (int h = 0; h < kTcHeads; ++h) red[warp * kTcHeads + h] = mx[h];
                 }
-                named_barrier(1, 128);
+                named_barrier(1, kKeyWarps * 32);
                 float alpha[kTcHeads];
 #pragma unroll
                 for (int h = 0; h < kTcHeads; ++h) {
@@ -531,7 +622,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) decode_tc_kernel(const DecodeAr
                     if (u) m_run[h] = v;
                     l_run[h] *= alpha[h];
                 }
-                if (o_used) {
+                named_barrier(1, kKeyWarps * 32);  // red read before it is written again
+                if (js > 0) {
                     // O^T lane t holds head dims t (+128): scale column h by alpha[h]
 #pragma unroll
                     for (int mb = 0; mb < C::MB; ++mb) {
@@ -555,7 +647,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) decode_tc_kernel(const DecodeAr
             // row t of P^T: 32 bytes, halves swapped on rows 4-7 of each 8 (32-byte swizzle)
             uint32_t hi[8];
 #pragma unroll
-            for (int i = 0; i < 8; ++i) hi[i] = Ops<T>::pack(p[2 * i], p[2 * i + 1]);
+            for (int e = 0; e < 8; ++e) hi[e] = Ops<T>::pack(p[2 * e], p[2 * e + 1]);
             char* prow = sP + t * 32;
             const int sw = ((t >> 2) & 1) * 16;
             *reinterpret_cast<uint4*>(prow + sw) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
@@ -563,86 +655,76 @@ __global__ void __launch_bounds__(kTcThreads, 1) decode_tc_kernel(const DecodeAr
             if constexpr (Ops<T>::kSplitP) {
                 uint32_t lo[8];
 #pragma unroll
-                for (int i = 0; i < 8; ++i) {
-                    const float r0 = p[2 * i] - __uint_as_float(hi[i] << 16);
-                    const float r1 = p[2 * i + 1] - __uint_as_float(hi[i] & 0xffff0000u);
-                    lo[i] = Ops<T>::pack(r0, r1);
+                for (int e = 0; e < 8; ++e) {
+                    const float r0 = p[2 * e] - __uint_as_float(hi[e] << 16);
+                    const float r1 = p[2 * e + 1] - __uint_as_float(hi[e] & 0xffff0000u);
+                    lo[e] = Ops<T>::pack(r0, r1);
                 }
                 char* lrow = prow + C::P_BYTES;
                 *reinterpret_cast<uint4*>(lrow + sw) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
                 *reinterpret_cast<uint4*>(lrow + (16 ^ sw)) = make_uint4(lo[4], lo[5], lo[6], lo[7]);
             }
             fence_proxy_async();
-        } else {
-            // ---------------- V row -> V^T operand ----------------
-            if (o_pending) {  // the previous tile's P V product has read V^T
-                mbar_wait(mbar_o, ph_o, dead);
-                ph_o ^= 1u;
-                o_pending = false;
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(pready_bar);
+            if (i_cur >= ntiles) {
+                ++j;
+                break;
             }
-            const char* s_vsc = s_sc + 2 * C::SC_BYTES;
-            uint32_t sc[C::G], bi[C::G];
-            load_pairs<C::G>(s_vsc, sc);
-            if (has_bias) {
-                load_pairs<C::G>(s_vsc + C::SC_BYTES, bi);
-            } else {
-#pragma unroll
-                for (int g = 0; g < C::G; ++g) bi[g] = 0u;
-            }
+            i_prev = i_cur;
+            i_cur = advance(i_cur + 1);
+        }
+        n_active = j - 1 < 0 ? 0 : j - 1;
+        if (n_active > 0) {  // the last P V product
+            mbar_wait(pfree_bar, (n_active - 1) & 1, dead);
+            tc_fence_after();
+        }
+    } else {
+        // ================= value warps: V -> V^T operand =================
+        int j = 0;
+        for (int i = advance(0); i < ntiles; i = advance(i + 1), ++j) {
+            const int s = j % ST;
+            const int vbuf = j % VB;
+            mbar_wait(full_bar(s), (j / ST) & 1, dead);
+            const char* st = ring + s * C::STAGE_BYTES;
+            const char* s_vsc = st + 2 * C::PACK_BYTES + 2 * C::SC_BYTES + t * C::SROWB;
+            if (j >= VB) mbar_wait(vfree_bar(vbuf), ((j / VB) - 1) & 1, dead);
             // token t's row of each 1024-byte atom (8 tokens x 64 dims) of 64-dim block db
-            char* vrow = sV + (t >> 3) * 1024 + (t & 7) * 128;
-#pragma unroll
+            char* vrow = sV + vbuf * C::V_BYTES + (t >> 3) * 1024 + (t & 7) * 128;
+#pragma unroll 2
             for (int c = 0; c < C::CPR; ++c) {
-                const uint4 w4 = lds128(st + C::PACK_BYTES + swz<C::CPR>(t, c) * 16);
                 const int g = (c * EPC) / GS;
+                const uint32_t s2 = pair_at(s_vsc + g * 2);
+                const uint32_t b2 = has_bias ? pair_at(s_vsc + C::SC_BYTES + g * 2) : 0u;
                 uint32_t o[PPC];
-                dequant_chunk<T, BITS>(w4, sc[g], bi[g], o);
+                dequant_chunk<T, BITS>(lds128(st + C::PACK_BYTES + swz<C::CPR>(t, c) * 16), s2, b2, o);
                 // every 4 pairs are 8 consecutive head dims: one 16-byte store
 #pragma unroll
-                for (int j = 0; j < PPC / 4; ++j) {
-                    const int w8 = c * (PPC / 4) + j;  // 8-dim block index
+                for (int e = 0; e < PPC / 4; ++e) {
+                    const int w8 = c * (PPC / 4) + e;  // 8-dim block index
                     const int db = w8 >> 3, cc = w8 & 7;
                     *reinterpret_cast<uint4*>(vrow + db * C::V_LBO + ((cc ^ (t & 7)) * 16)) =
-                        make_uint4(o[4 * j], o[4 * j + 1], o[4 * j + 2], o[4 * j + 3]);
+                        make_uint4(o[4 * e], o[4 * e + 1], o[4 * e + 2], o[4 * e + 3]);
                 }
             }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(empty_bar(s));
             fence_proxy_async();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(vready_bar(vbuf));
         }
-        tc_fence_before();
-        __syncthreads();
-        if (tid == 0) {
-            tc_fence_after();
-#pragma unroll
-            for (int mb = 0; mb < C::MB; ++mb) {
-#pragma unroll
-                for (int ks_ = 0; ks_ < kTcTile / 16; ++ks_) {
-                    const uint64_t vd = smem_desc(sV_u + (2 * mb) * C::V_LBO + (2 * ks_) * 1024, C::V_LBO, 1024, kSw128);
-                    const uint64_t pd = smem_desc(sP_u + ks_ * 512, C::P_BYTES, 256, kSw32);
-                    mma_ss(tbase + kTmemO + mb * 16, vd, pd, IDESC_PV, (o_used || ks_ > 0) ? 1u : 0u);
-                    if constexpr (Ops<T>::kSplitP) {
-                        const uint64_t pl = smem_desc(sP_u + C::P_BYTES + ks_ * 512, C::P_BYTES, 256, kSw32);
-                        mma_ss(tbase + kTmemO + mb * 16, vd, pl, IDESC_PV, 1u);
-                    }
-                }
-            }
-            mma_commit(mbar_o);
-        }
-        o_used = true;
-        o_pending = true;
     }
 
-    // ---- drain, then the CTA's record: O^T columns, m, l per head ----
-    cp_async_wait<0>();
-    if (o_pending) {
-        mbar_wait(mbar_o, ph_o, dead);
-        ph_o ^= 1u;
-    }
+    // ---- the CTA's record: O^T columns, m, l per head ----
+    tc_fence_before();
+    __syncthreads();  // every role done; the ring is free: reuse it as the merge area
     tc_fence_after();
-    __syncthreads();  // ring is free: reuse it as the merge area
     float* mo = reinterpret_cast<float*>(ring);  // [16][D]
     float* mm = mo + kTcHeads * D;               // [16]
     float* ml = mm + kTcHeads;                   // [16]
-    if (key_warp) {
+    if (warp < kKeyWarps) {
+        const uint32_t lane_off = (uint32_t)(warp * 32) << 16;
 #pragma unroll
         for (int h = 0; h < kTcHeads; ++h) {
             float v = l_run[h];
@@ -653,7 +735,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) decode_tc_kernel(const DecodeAr
 #pragma unroll
         for (int mb = 0; mb < C::MB; ++mb) {
             float o[kTcHeads];
-            if (o_used) {
+            if (n_active > 0) {
                 tmem_ld16(tbase + lane_off + kTmemO + mb * 16, o);
                 tmem_wait_ld();
             } else {
@@ -664,16 +746,16 @@ __global__ void __launch_bounds__(kTcThreads, 1) decode_tc_kernel(const DecodeAr
 #pragma unroll
             for (int h = 0; h < kTcHeads; ++h) mo[h * D + d] = o[h];
         }
-    }
-    if (tid == 0) {
+        if (tid == 0) {
 #pragma unroll
-        for (int h = 0; h < kTcHeads; ++h) mm[h] = m_run[h];
+            for (int h = 0; h < kTcHeads; ++h) mm[h] = m_run[h];
+        }
     }
     tc_fence_before();
     __syncthreads();
     if (tid < kTcHeads) ml[tid] = red[tid] + red[16 + tid] + red[32 + tid] + red[48 + tid];
     __syncthreads();
-    if (warp == 0) {
+    if (warp == kMmaWarp) {
         tc_fence_after();
         tmem_dealloc(tbase, kTmemCols);
     }

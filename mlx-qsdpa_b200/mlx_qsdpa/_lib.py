@@ -17,7 +17,7 @@ from typing import Optional, Tuple
 import torch
 
 _HERE = os.path.dirname(os.path.abspath(__file__))
-LIB_PATH = os.environ.get("QSDPA_LIB", os.path.join(_HERE, "libqsdpa.so"))
+LIB_PATH = os.environ.get("QSDPA_LIB") or os.path.join(_HERE, "libqsdpa.so")
 
 QSDPA_F16, QSDPA_BF16 = 0, 1
 MASK_NONE, MASK_BOOL, MASK_ADD_F16, MASK_ADD_BF16, MASK_ADD_F32 = 0, 1, 2, 3, 4
