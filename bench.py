@@ -51,7 +51,26 @@ def parse():
     ap.add_argument("--layers", type=int, default=LAYERS)
     ap.add_argument("--no-graph", action="store_true", help="launch eagerly instead of CUDA graphs")
     ap.add_argument("--cpu-sample-calls", type=int, default=3)
+    ap.add_argument("--kernel", choices=list(KERNELS), default="auto",
+                    help="decode kernel of the timed path (profiling); e2e always uses the public API's choice")
     return ap.parse_args()
+
+
+KERNELS = {"auto": 0, "tcgen05": 1, "mma": 2, "simt": 3}
+# kernel the library picks with QSDPA_KERNEL_AUTO for this workload, and the
+# profile summaries (ncu --set full on this workload) giving DRAM traffic
+AUTO_KERNEL = "mma"
+PROFILES = {"mma": "profiles/decode_mma_128k_gqa16.md", "tcgen05": "profiles/decode_tcgen05_128k_gqa16.md"}
+
+
+def profiled_traffic(kernel: str):
+    """DRAM bytes (read + write) of one decode launch from the committed ncu summary."""
+    import re
+    path = os.path.join(ROOT, PROFILES.get(AUTO_KERNEL if kernel == "auto" else kernel, ""))
+    if not os.path.isfile(path):
+        return None, None
+    m = re.search(r"traffic per launch \(dram read \+ write\): ([0-9.]+) MB", open(path).read())
+    return (round(float(m.group(1)) * 1e6), os.path.relpath(path, ROOT)) if m else (None, None)
 
 
 def measured_peaks():
@@ -247,13 +266,16 @@ def main():
 
     outs = [torch.empty((B, HQ, 1, D), dtype=torch.float16, device=dev) for _ in range(L)]
 
+    kern_code = KERNELS[args.kernel]
+
     def step(i):
         (pk, ks, kb), (pv, vs, vb) = layers[i % L]
         if world == 1:
-            _lib.decode(q, pk, pv, ks, vs, kb, vb, scale=scale, bits=BITS, group_size=GS, out=outs[i % L])
+            _lib.decode(q, pk, pv, ks, vs, kb, vb, scale=scale, bits=BITS, group_size=GS, out=outs[i % L],
+                        kernel=kern_code)
         else:
             _lib.decode(q, pk, pv, ks, vs, kb, vb, scale=scale, bits=BITS, group_size=GS,
-                        out_mode=_lib.OUT_PARTIAL, part=part)
+                        out_mode=_lib.OUT_PARTIAL, part=part, kernel=kern_code)
             dist.all_gather_into_tensor(gath, rec)
             _lib.combine_packed(gath, rows, D, out=outs[i % L].view(rows, D))
 
@@ -327,7 +349,8 @@ def main():
     # replayed back to back between one pair of events on the launching stream
     def local_decode(i):
         (pk, ks, kb), (pv, vs, vb) = layers[i % L]
-        _lib.decode(q, pk, pv, ks, vs, kb, vb, scale=scale, bits=BITS, group_size=GS, out=outs[i % L])
+        _lib.decode(q, pk, pv, ks, vs, kb, vb, scale=scale, bits=BITS, group_size=GS, out=outs[i % L],
+                    kernel=kern_code)
 
     kgraphs = []
     if world == 1:
@@ -392,7 +415,8 @@ def main():
         bytes_local = algorithmic_bytes(ctx)
         achieved = bytes_local / (per_launch_ms * 1e-3) / 1e9
         (pk0, ks0, kb0), (pv0, vs0, vb0) = layers[0]
-        splits = _lib.plan_splits(q, pk0, pv0, ks0, vs0, kb0, vb0, BITS, GS)
+        splits = _lib.plan_splits(q, pk0, pv0, ks0, vs0, kb0, vb0, BITS, GS, kernel=kern_code)
+        traffic, traffic_src = profiled_traffic(args.kernel)
         launches_per_step = (1 if splits == 1 else 2) + (1 if world > 1 else 0)
         line = {
             "metric": METRIC,
@@ -414,13 +438,15 @@ def main():
                 "context_per_gpu": ctx, "context_total": ctx * world, "layers": L,
                 "l2": "inputs larger than L2: 12 layers x %.1f MB rotated" % (bytes_local / 1e6),
                 "launch": graph_note, "splits": splits,
+                "kernel": AUTO_KERNEL if args.kernel == "auto" else args.kernel,
                 "parallelism": "sequence-sharded" if world > 1 else "single GPU",
             },
             "gbs_per_gpu": round(achieved, 1),
             "roofline": {
                 "bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                 "frac": round(achieved / peak, 4), "peak_kind": peak_kind,
-                "traffic": None,
+                "traffic": traffic, "traffic_source": traffic_src,
+                "launch": "one qsdpa_decode call: decode kernel + split merge",
                 "bytes_per_launch": bytes_local,
                 "launch_us": round(per_launch_ms * 1e3, 3),
             },
