@@ -87,7 +87,7 @@ struct TcCfg {
     static constexpr int SC_CHUNKS = SC_BYTES / 16;
     static constexpr int STAGE_BYTES = 2 * PACK_BYTES + 4 * SC_BYTES;
     static constexpr int V_BYTES = kTcTile * D * 2;       // one V^T operand
-    static constexpr int V_LBO = (kTcTile / 8) * 1024;    // between 64-dim blocks
+    static constexpr int V_LBO = (kTcTile / 8) * 1024;    // V^T: between 64-dim blocks
     static constexpr int Q_BYTES = kTcHeads * D * 2;      // Q operand
     static constexpr int P_BYTES = kTcTile * kTcHeads * 2;  // one P^T operand (hi; lo follows)
     static constexpr int MISC_BYTES = 1024;
@@ -214,6 +214,7 @@ __device__ __forceinline__ void prefetch_l2(const void* p, uint32_t bytes) {
 __device__ __forceinline__ void cp_async_mbar_arrive(uint32_t addr) {
     asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];\n" ::"r"(addr) : "memory");
 }
+// Test for completion of the phase with the given parity.
 __device__ __forceinline__ bool mbar_try(uint32_t addr, uint32_t parity) {
     uint32_t ok;
     asm volatile(
@@ -229,17 +230,73 @@ __device__ __forceinline__ uint64_t global_ns() {
     return t;
 }
 // Wait for completion of the phase with the given parity, for at most about a
-// second.  A thread whose wait ran out stops waiting from then on, so the
-// kernel still finishes.
+// second.  Between polls the warp sleeps, doubling from 32 ns up to `max_ns`,
+// so waiting warps leave the issue slots to the warps sharing their scheduler
+// (short sleeps for roles on the critical path, long ones for the others).  A
+// thread whose wait ran out stops waiting from then on, so the kernel still
+// finishes.
+template <uint32_t MaxNs>
 __device__ __forceinline__ void mbar_wait(uint32_t addr, uint32_t parity, bool& dead) {
     if (dead || mbar_try(addr, parity)) return;
     const uint64_t t0 = global_ns();
-    while (!mbar_try(addr, parity)) {
-        if (global_ns() - t0 > kWaitNs) {
+    uint32_t ns = 32;
+    for (uint32_t it = 1;; ++it) {
+        __nanosleep(ns);
+        if (ns < MaxNs) ns <<= 1;
+        if (mbar_try(addr, parity)) return;
+        if ((it & 63) == 0 && global_ns() - t0 > kWaitNs) {
             atomicOr(&g_device_status, 1u);
             dead = true;
             return;
         }
+    }
+}
+constexpr uint32_t kSleepCrit = 64;   // key and MMA warps
+constexpr uint32_t kSleepIdle = 512;  // value and producer warps
+
+// Byte offsets of the 16-byte chunks of row t in a stage array written with
+// the XOR-128B swizzle (chunk k of the array -> line k/8, slot (k%8)^(line%8)),
+// so the per-chunk cost is one XOR with a per-thread constant.
+template <int CPR>
+struct RowChunks {
+    static constexpr int H = CPR > 8 ? CPR / 8 : 1;  // 128-byte lines per row
+    uint32_t lineb;
+    uint32_t x[H];
+    __device__ __forceinline__ explicit RowChunks(int t) {
+        const int k0 = t * CPR;
+        lineb = (uint32_t)(k0 >> 3) * 128u;
+#pragma unroll
+        for (int h = 0; h < H; ++h) x[h] = (uint32_t)(((k0 & 7) ^ (((k0 >> 3) + h) & 7)) << 4);
+    }
+    __device__ __forceinline__ uint32_t off(int c) const {
+        return lineb + (uint32_t)(c >> 3) * 128u + (((uint32_t)(c & 7) << 4) ^ x[c >> 3]);
+    }
+};
+
+// One broadcast (x, x) pair per group of a scale / bias row of G halves.
+template <int G>
+__device__ __forceinline__ void load_pairs(const char* row, uint32_t out[G]) {
+    if constexpr (G == 8) {
+        const uint4 v = lds128(row);
+        const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            out[2 * i] = __byte_perm(w[i], 0u, 0x1010);
+            out[2 * i + 1] = __byte_perm(w[i], 0u, 0x3232);
+        }
+    } else if constexpr (G == 4) {
+        const uint2 v = lds64(row);
+        out[0] = __byte_perm(v.x, 0u, 0x1010);
+        out[1] = __byte_perm(v.x, 0u, 0x3232);
+        out[2] = __byte_perm(v.y, 0u, 0x1010);
+        out[3] = __byte_perm(v.y, 0u, 0x3232);
+    } else if constexpr (G == 2) {
+        const uint32_t v = lds32(row);
+        out[0] = __byte_perm(v, 0u, 0x1010);
+        out[1] = __byte_perm(v, 0u, 0x3232);
+    } else {
+        const uint32_t v = lds16(row);
+        out[0] = v | (v << 16);
     }
 }
 
@@ -253,12 +310,6 @@ __device__ __forceinline__ int tc_dim(int m) {
     } else {
         return m;
     }
-}
-
-// (x, x) pair of the half at p
-__device__ __forceinline__ uint32_t pair_at(const char* p) {
-    const uint32_t v = lds16(p);
-    return v | (v << 16);
 }
 
 // Dequantise one 16-byte chunk (4 packed words) of a row: 4-bit -> 16 pairs,
@@ -450,18 +501,33 @@ __global__ void __launch_bounds__(kTcThreads, 1) decode_tc_kernel(const DecodeAr
                 ipf = advance(ipf + 1);
             }
             const int s = j % ST;
-            if (j >= ST) mbar_wait(empty_bar(s), ((j / ST) - 1) & 1, dead);
+            if (j >= ST) mbar_wait<kSleepIdle>(empty_bar(s), ((j / ST) - 1) & 1, dead);
             const int p0 = p_lo + i * kTcTile;
             char* st = ring + s * C::STAGE_BYTES;
             const int rows_valid = min(kTcTile, p_hi - p0);
-            const int64_t tile_off = (int64_t)p0 * C::ROWB;
-            for (int k = lane; k < kTcTile * C::CPR; k += 32) {
-                const int r = k / C::CPR, c = k - r * C::CPR;
-                const bool ok = r < rows_valid;
-                const int dst = swz<C::CPR>(r, c) * 16;
-                const int64_t off = ok ? tile_off + r * C::ROWB + c * 16 : 0;
-                cp_async16(st + dst, kp_b + off, ok ? 16 : 0);
-                cp_async16(st + C::PACK_BYTES + dst, vp_b + off, ok ? 16 : 0);
+            const char* ksrc = kp_b + (int64_t)p0 * C::ROWB + lane * 16;
+            const char* vsrc = vp_b + (int64_t)p0 * C::ROWB + lane * 16;
+            // chunk k = lane + 32m of the stage (row k / CPR): source k*16, swizzled
+            // destination line k/8 = lane/8 + 4m, whose parity alternates with m
+            const uint32_t d_even = (uint32_t)swz<8>(lane >> 3, lane & 7) * 16u;
+            const uint32_t d_odd = (uint32_t)swz<8>((lane >> 3) + 4, lane & 7) * 16u - 512u;
+            constexpr int M = kTcTile * C::CPR / 32;
+            if (rows_valid == kTcTile) {
+#pragma unroll 4
+                for (int m = 0; m < M; ++m) {
+                    const uint32_t dst = (m & 1 ? d_odd : d_even) + m * 512u;
+                    cp_async16(st + dst, ksrc + m * 512, 16);
+                    cp_async16(st + C::PACK_BYTES + dst, vsrc + m * 512, 16);
+                }
+            } else {
+                const int kvalid = rows_valid * C::CPR;
+#pragma unroll 4
+                for (int m = 0; m < M; ++m) {
+                    const uint32_t dst = (m & 1 ? d_odd : d_even) + m * 512u;
+                    const bool ok = lane + 32 * m < kvalid;
+                    cp_async16(st + dst, ok ? ksrc + m * 512 : kp_b, ok ? 16 : 0);
+                    cp_async16(st + C::PACK_BYTES + dst, ok ? vsrc + m * 512 : vp_b, ok ? 16 : 0);
+                }
             }
             const int sbytes = rows_valid * C::SROWB;
             char* s0 = st + 2 * C::PACK_BYTES;
@@ -484,7 +550,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) decode_tc_kernel(const DecodeAr
         if (lane == 0) {
             auto issue_qk = [&](int j) {
                 const int kbuf = j & 1;
-                mbar_wait(kready_bar(kbuf), (j >> 1) & 1, dead);
+                mbar_wait<kSleepCrit>(kready_bar(kbuf), (j >> 1) & 1, dead);
                 tc_fence_after();
 #pragma unroll
                 for (int ks_ = 0; ks_ < D / 16; ++ks_) {
@@ -500,8 +566,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) decode_tc_kernel(const DecodeAr
             for (int j = 0; j < n; ++j) {
                 if (j + 1 < n) issue_qk(j + 1);
                 const int vbuf = j % VB;
-                mbar_wait(pready_bar, j & 1, dead);
-                mbar_wait(vready_bar(vbuf), (j / VB) & 1, dead);
+                mbar_wait<kSleepCrit>(pready_bar, j & 1, dead);
+                mbar_wait<kSleepCrit>(vready_bar(vbuf), (j / VB) & 1, dead);
                 tc_fence_after();
 #pragma unroll
                 for (int mb = 0; mb < C::MB; ++mb) {
@@ -527,12 +593,21 @@ __global__ void __launch_bounds__(kTcThreads, 1) decode_tc_kernel(const DecodeAr
         const uint32_t lane_off = (uint32_t)(warp * 32) << 16;
         const int64_t mrow = a.mask ? (int64_t)b * a.m_sb : 0;
         const int hq0 = kvh * a.gqa + h0;
+        const RowChunks<C::CPR> rows(t);
         // dequantise the j-th active tile into K buffer j & 1 of TMEM lane t
         auto load_keys = [&](int j) {
             const int s = j % ST;
-            mbar_wait(full_bar(s), (j / ST) & 1, dead);
+            mbar_wait<kSleepCrit>(full_bar(s), (j / ST) & 1, dead);
             const char* st = ring + s * C::STAGE_BYTES;
             const char* s_sc = st + 2 * C::PACK_BYTES + t * C::SROWB;
+            uint32_t sc[C::G], bi[C::G];
+            load_pairs<C::G>(s_sc, sc);
+            if (has_bias) {
+                load_pairs<C::G>(s_sc + C::SC_BYTES, bi);
+            } else {
+#pragma unroll
+                for (int g = 0; g < C::G; ++g) bi[g] = 0u;
+            }
             constexpr int CPS = 32 / PPC;  // chunks per 32-column store
             const uint32_t kcol = tbase + lane_off + kTmemK + (j & 1) * (D / 2);
 #pragma unroll 1
@@ -542,9 +617,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) decode_tc_kernel(const DecodeAr
                 for (int u = 0; u < CPS; ++u) {
                     const int c = c0 + u;
                     const int g = (c * EPC) / GS;
-                    const uint32_t s2 = pair_at(s_sc + g * 2);
-                    const uint32_t b2 = has_bias ? pair_at(s_sc + C::SC_BYTES + g * 2) : 0u;
-                    dequant_chunk<T, BITS>(lds128(st + swz<C::CPR>(t, c) * 16), s2, b2, &cols[u * PPC]);
+                    dequant_chunk<T, BITS>(lds128(st + rows.off(c)), sc[g], bi[g], &cols[u * PPC]);
                 }
                 tmem_st32(kcol + c0 * PPC, cols);
             }
@@ -569,13 +642,13 @@ __global__ void __launch_bounds__(kTcThreads, 1) decode_tc_kernel(const DecodeAr
             }
             const int js = j - 1;  // the tile whose scores are ready
             const int i = i_prev;
-            mbar_wait(sready_bar(js & 1), (js >> 1) & 1, dead);
+            mbar_wait<kSleepCrit>(sready_bar(js & 1), (js >> 1) & 1, dead);
             tc_fence_after();
             float s[kTcHeads];
             tmem_ld16(tbase + lane_off + kTmemS + 16 * (js & 1), s);
             tmem_wait_ld();
             if (js > 0) {  // the previous P V product is done: P^T free, O^T current
-                mbar_wait(pfree_bar, (js - 1) & 1, dead);
+                mbar_wait<kSleepCrit>(pfree_bar, (js - 1) & 1, dead);
                 tc_fence_after();
             }
 
@@ -677,34 +750,42 @@ __global__ void __launch_bounds__(kTcThreads, 1) decode_tc_kernel(const DecodeAr
         }
         n_active = j - 1 < 0 ? 0 : j - 1;
         if (n_active > 0) {  // the last P V product
-            mbar_wait(pfree_bar, (n_active - 1) & 1, dead);
+            mbar_wait<kSleepCrit>(pfree_bar, (n_active - 1) & 1, dead);
             tc_fence_after();
         }
     } else {
         // ================= value warps: V -> V^T operand =================
+        const RowChunks<C::CPR> rows(t);
         int j = 0;
         for (int i = advance(0); i < ntiles; i = advance(i + 1), ++j) {
             const int s = j % ST;
             const int vbuf = j % VB;
-            mbar_wait(full_bar(s), (j / ST) & 1, dead);
+            mbar_wait<kSleepIdle>(full_bar(s), (j / ST) & 1, dead);
             const char* st = ring + s * C::STAGE_BYTES;
             const char* s_vsc = st + 2 * C::PACK_BYTES + 2 * C::SC_BYTES + t * C::SROWB;
-            if (j >= VB) mbar_wait(vfree_bar(vbuf), ((j / VB) - 1) & 1, dead);
-            // token t's row of each 1024-byte atom (8 tokens x 64 dims) of 64-dim block db
+            uint32_t sc[C::G], bi[C::G];
+            load_pairs<C::G>(s_vsc, sc);
+            if (has_bias) {
+                load_pairs<C::G>(s_vsc + C::SC_BYTES, bi);
+            } else {
+#pragma unroll
+                for (int g = 0; g < C::G; ++g) bi[g] = 0u;
+            }
+            if (j >= VB) mbar_wait<kSleepIdle>(vfree_bar(vbuf), ((j / VB) - 1) & 1, dead);
+            // token t's row of each 1024-byte atom (8 tokens x 64 dims) of 64-dim
+            // block w8/8; 16-byte slot (w8 % 8) ^ (t % 8)
             char* vrow = sV + vbuf * C::V_BYTES + (t >> 3) * 1024 + (t & 7) * 128;
+            const uint32_t vx = (uint32_t)(t & 7) << 4;
 #pragma unroll 2
             for (int c = 0; c < C::CPR; ++c) {
                 const int g = (c * EPC) / GS;
-                const uint32_t s2 = pair_at(s_vsc + g * 2);
-                const uint32_t b2 = has_bias ? pair_at(s_vsc + C::SC_BYTES + g * 2) : 0u;
                 uint32_t o[PPC];
-                dequant_chunk<T, BITS>(lds128(st + C::PACK_BYTES + swz<C::CPR>(t, c) * 16), s2, b2, o);
+                dequant_chunk<T, BITS>(lds128(st + C::PACK_BYTES + rows.off(c)), sc[g], bi[g], o);
                 // every 4 pairs are 8 consecutive head dims: one 16-byte store
 #pragma unroll
                 for (int e = 0; e < PPC / 4; ++e) {
                     const int w8 = c * (PPC / 4) + e;  // 8-dim block index
-                    const int db = w8 >> 3, cc = w8 & 7;
-                    *reinterpret_cast<uint4*>(vrow + db * C::V_LBO + ((cc ^ (t & 7)) * 16)) =
+                    *reinterpret_cast<uint4*>(vrow + (w8 >> 3) * C::V_LBO + (((uint32_t)(w8 & 7) << 4) ^ vx)) =
                         make_uint4(o[4 * e], o[4 * e + 1], o[4 * e + 2], o[4 * e + 3]);
                 }
             }
