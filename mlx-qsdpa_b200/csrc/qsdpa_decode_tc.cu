@@ -44,6 +44,11 @@
 // Every wait on an MMA completion is bounded (about one second of global
 // time); a wait that runs out records bit 0 of the device status word and the
 // kernel finishes without hanging (its output is then undefined).
+#include <cuda.h>
+
+#include <string.h>
+
+#include <mutex>
 #include <type_traits>
 
 #include "qsdpa_regmath.cuh"
@@ -56,11 +61,13 @@ namespace {
 
 using namespace dev;
 
-constexpr int kKeyWarps = 4;    // warps 0-3: keys -> TMEM, softmax
+constexpr int kKeyWarps = 4;    // warps 0-3: keys -> TMEM
 constexpr int kValWarps = 4;    // warps 4-7: values -> V^T operand
-constexpr int kProdWarp = 8;    // ring producer (cp.async)
-constexpr int kMmaWarp = 9;     // TMEM owner and MMA issuer
-constexpr int kTcThreads = 320;
+constexpr int kSmWarps = 4;     // warps 8-11: softmax -> P^T, final O^T read-out
+constexpr int kSmWarp0 = kKeyWarps + kValWarps;
+constexpr int kProdWarp = kSmWarp0 + kSmWarps;  // ring producer (cp.async)
+constexpr int kMmaWarp = kProdWarp + 1;         // TMEM owner and MMA issuer
+constexpr int kTcThreads = (kMmaWarp + 1) * 32;
 constexpr int kTcTile = 128;    // tokens per tile = M of the S MMA
 constexpr int kTcHeads = 16;    // query heads per CTA = N of both MMAs
 constexpr int kTmemCols = 512;  // the whole SM's tensor memory: one CTA per SM
@@ -74,7 +81,7 @@ constexpr int kSmemLimit = 227 * 1024;
 // measured: the extra L2 traffic costs more than the latency it hides)
 constexpr int kPrefetchTiles = 0;
 
-template <int BITS, int D, int GS>
+template <int BITS, int D, int GS, bool SPLITP>
 struct TcCfg {
     static constexpr int EPW = 32 / BITS;
     static constexpr int PD = D / EPW;          // words per packed row
@@ -89,17 +96,28 @@ struct TcCfg {
     static constexpr int V_BYTES = kTcTile * D * 2;       // one V^T operand
     static constexpr int V_LBO = (kTcTile / 8) * 1024;    // V^T: between 64-dim blocks
     static constexpr int Q_BYTES = kTcHeads * D * 2;      // Q operand
-    static constexpr int P_BYTES = kTcTile * kTcHeads * 2;  // one P^T operand (hi; lo follows)
+    static constexpr int P_BYTES = kTcTile * kTcHeads * 2;  // one P^T operand
+    static constexpr int P_BUF = (SPLITP ? 2 : 1) * P_BYTES;  // hi (+ lo) of one of two P buffers
     static constexpr int MISC_BYTES = 1024;
-    static constexpr int FIXED = 1024 + Q_BYTES + 2 * P_BYTES + MISC_BYTES;
-    // two V^T buffers (values run a tile ahead) when two ring stages still fit
-    static constexpr int VBUFS = FIXED + 2 * V_BYTES + 2 * STAGE_BYTES <= kSmemLimit ? 2 : 1;
+    static constexpr int BASE = 1024 + Q_BYTES + MISC_BYTES;
+    static constexpr bool fits(int pb, int vb) {
+        return BASE + pb * P_BUF + vb * V_BYTES + 2 * STAGE_BYTES <= kSmemLimit;
+    }
+    // two P^T buffers (softmax of tile j overlaps the P V MMA of tile j-1) and
+    // two V^T buffers (values run a tile ahead) where they fit
+    static constexpr int PBUFS = fits(2, 1) ? 2 : 1;
+    static constexpr int VBUFS = fits(PBUFS, 2) ? 2 : 1;
+    static constexpr int FIXED = BASE + PBUFS * P_BUF;
     static constexpr int STAGES_FIT = (kSmemLimit - FIXED - VBUFS * V_BYTES) / STAGE_BYTES;
     static constexpr int STAGES = STAGES_FIT > 4 ? 4 : STAGES_FIT;
     // at least 116 KB so no second CTA shares the SM (and its tensor memory)
     static constexpr int SMEM_RAW = FIXED + VBUFS * V_BYTES + STAGES * STAGE_BYTES;
     static constexpr int SMEM = SMEM_RAW > 116 * 1024 ? SMEM_RAW : 116 * 1024;
     static constexpr int MB = D / 128;  // 128-dim blocks of O^T
+    // packed rows of 128 or 256 bytes arrive by TMA (the 128-byte swizzle of a
+    // box of 128-byte rows is exactly the ring's chunk swizzle); 64-byte rows by
+    // the producer lanes' cp.async
+    static constexpr bool TMA_ROWS = ROWB == 128 || ROWB == 256;
     static_assert(STAGES >= 2, "two ring stages must fit");
     static_assert(STAGES * STAGE_BYTES >= kTcHeads * D * 4 + 2 * kTcHeads * 4, "merge area must fit in the ring");
     static_assert(SC_BYTES % 16 == 0 && CPR >= 2, "copy plan");
@@ -162,6 +180,16 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t v[32]) 
         : "memory");
 }
 
+// true in exactly one lane of the (converged) warp
+__device__ __forceinline__ bool elect_one() {
+    uint32_t pred = 0;
+    asm volatile(
+        "{\n .reg .b32 rx;\n .reg .pred px;\n elect.sync rx|px, %1;\n @px mov.s32 %0, 1;\n}\n"
+        : "+r"(pred)
+        : "r"(0xffffffffu));
+    return pred != 0;
+}
+
 // D[tmem] (+)= A[tmem] . B[smem desc]   (kind::f16, fp32 accumulation)
 __device__ __forceinline__ void mma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
                                        uint32_t accumulate) {
@@ -209,6 +237,27 @@ __device__ __forceinline__ void mbar_arrive(uint32_t addr) {
 // bulk prefetch of [p, p + bytes) into L2 (16-byte aligned address and size)
 __device__ __forceinline__ void prefetch_l2(const void* p, uint32_t bytes) {
     asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;\n" ::"l"(p), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(uint32_t addr, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;\n" ::"r"(addr), "r"(bytes) : "memory");
+}
+// One tile of packed rows (128 rows starting at token p0 of (b, kvh)) by TMA,
+// completing on an mbarrier's transaction count.  No multicast.
+template <int ROWB>
+__device__ __forceinline__ void tma_rows(uint32_t dst, const CUtensorMap* map, int p0, int kvh, int b, uint32_t mbar) {
+    if constexpr (ROWB == 128) {
+        asm volatile(
+            "cp.async.bulk.tensor.4d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4, %5}], "
+            "[%6];\n" ::"r"(dst),
+            "l"(reinterpret_cast<uint64_t>(map)), "r"(0), "r"(p0), "r"(kvh), "r"(b), "r"(mbar)
+            : "memory");
+    } else {
+        asm volatile(
+            "cp.async.bulk.tensor.5d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4, %5, "
+            "%6}], [%7];\n" ::"r"(dst),
+            "l"(reinterpret_cast<uint64_t>(map)), "r"(0), "r"(0), "r"(p0), "r"(kvh), "r"(b), "r"(mbar)
+            : "memory");
+    }
 }
 // arrive once every cp.async this thread issued so far has landed
 __device__ __forceinline__ void cp_async_mbar_arrive(uint32_t addr) {
@@ -332,8 +381,9 @@ __device__ __forceinline__ void dequant_chunk(const uint4 w4, uint32_t s2, uint3
 }
 
 template <typename T, int BITS, int D, int GS>
-__global__ void __launch_bounds__(kTcThreads, 1) decode_tc_kernel(const DecodeArgs a) {
-    using C = TcCfg<BITS, D, GS>;
+__global__ void __launch_bounds__(kTcThreads, 1)
+    decode_tc_kernel(const DecodeArgs a, const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v) {
+    using C = TcCfg<BITS, D, GS, Ops<T>::kSplitP>;
     constexpr bool kBf16 = !std::is_same<T, __half>::value;
     constexpr uint32_t IDESC_QK = make_idesc(kBf16, false, false, 128, kTcHeads);
     constexpr uint32_t IDESC_PV = make_idesc(kBf16, true, true, 128, kTcHeads);
@@ -341,6 +391,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) decode_tc_kernel(const DecodeAr
     constexpr int PPC = EPC / 2;        // half2 pairs per chunk
     constexpr int ST = C::STAGES;
     constexpr int VB = C::VBUFS;
+    constexpr int PB = C::PBUFS;
 
     extern __shared__ __align__(1024) char smem_raw[];
     // 1024-byte alignment of the swizzled operands (in the shared window)
@@ -349,7 +400,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) decode_tc_kernel(const DecodeAr
     char* sV = smem;                        // VB x V^T operand
     char* sQ = sV + VB * C::V_BYTES;        // Q operand
     char* sP = sQ + C::Q_BYTES;             // P^T operand: hi, lo
-    char* ring = sP + 2 * C::P_BYTES;       // ST stages of packed rows + scales
+    char* ring = sP + PB * C::P_BUF;        // ST stages of packed rows + scales
     char* misc = ring + ST * C::STAGE_BYTES;
     // mbarriers (8 bytes each)
     const uint32_t mb0 = smem_u32(misc);
@@ -357,11 +408,11 @@ __global__ void __launch_bounds__(kTcThreads, 1) decode_tc_kernel(const DecodeAr
     auto empty_bar = [&](int s) { return mb0 + 8u * (4 + s); };         // count 8 (consumer warps)
     auto kready_bar = [&](int k) { return mb0 + 8u * (8 + k); };        // count 4 (key warps)
     auto sready_bar = [&](int k) { return mb0 + 8u * (10 + k); };       // count 1 (commit)
-    const uint32_t pready_bar = mb0 + 8u * 12;                          // count 4 (key warps)
-    const uint32_t pfree_bar = mb0 + 8u * 13;                           // count 1 (commit)
-    auto vready_bar = [&](int v) { return mb0 + 8u * (14 + v); };       // count 4 (value warps)
-    auto vfree_bar = [&](int v) { return mb0 + 8u * (16 + v); };        // count 1 (commit)
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(misc + 160);
+    auto pready_bar = [&](int k) { return mb0 + 8u * (12 + k); };       // count 4 (softmax warps)
+    auto pfree_bar = [&](int k) { return mb0 + 8u * (14 + k); };        // count 1 (commit)
+    auto vready_bar = [&](int v) { return mb0 + 8u * (16 + v); };       // count 4 (value warps)
+    auto vfree_bar = [&](int v) { return mb0 + 8u * (18 + v); };        // count 1 (commit)
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(misc + 176);
     int* flags = reinterpret_cast<int*>(misc + 192);    // [4]
     float* red = reinterpret_cast<float*>(misc + 256);  // [4][16]
     const uint32_t sV_u = smem_u32(sV), sQ_u = smem_u32(sQ), sP_u = smem_u32(sP);
@@ -409,7 +460,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) decode_tc_kernel(const DecodeAr
     if (tid == 0) {
 #pragma unroll
         for (int s = 0; s < ST; ++s) {
-            mbar_init(full_bar(s), 32);
+            mbar_init(full_bar(s), 32 + (C::TMA_ROWS ? 1 : 0));
             mbar_init(empty_bar(s), kKeyWarps + kValWarps);
         }
 #pragma unroll
@@ -417,8 +468,11 @@ __global__ void __launch_bounds__(kTcThreads, 1) decode_tc_kernel(const DecodeAr
             mbar_init(kready_bar(k), kKeyWarps);
             mbar_init(sready_bar(k), 1);
         }
-        mbar_init(pready_bar, kKeyWarps);
-        mbar_init(pfree_bar, 1);
+#pragma unroll
+        for (int k = 0; k < 2; ++k) {
+            mbar_init(pready_bar(k), kSmWarps);
+            mbar_init(pfree_bar(k), 1);
+        }
 #pragma unroll
         for (int v = 0; v < VB; ++v) {
             mbar_init(vready_bar(v), kValWarps);
@@ -505,28 +559,37 @@ __global__ void __launch_bounds__(kTcThreads, 1) decode_tc_kernel(const DecodeAr
             const int p0 = p_lo + i * kTcTile;
             char* st = ring + s * C::STAGE_BYTES;
             const int rows_valid = min(kTcTile, p_hi - p0);
-            const char* ksrc = kp_b + (int64_t)p0 * C::ROWB + lane * 16;
-            const char* vsrc = vp_b + (int64_t)p0 * C::ROWB + lane * 16;
-            // chunk k = lane + 32m of the stage (row k / CPR): source k*16, swizzled
-            // destination line k/8 = lane/8 + 4m, whose parity alternates with m
-            const uint32_t d_even = (uint32_t)swz<8>(lane >> 3, lane & 7) * 16u;
-            const uint32_t d_odd = (uint32_t)swz<8>((lane >> 3) + 4, lane & 7) * 16u - 512u;
-            constexpr int M = kTcTile * C::CPR / 32;
-            if (rows_valid == kTcTile) {
-#pragma unroll 4
-                for (int m = 0; m < M; ++m) {
-                    const uint32_t dst = (m & 1 ? d_odd : d_even) + m * 512u;
-                    cp_async16(st + dst, ksrc + m * 512, 16);
-                    cp_async16(st + C::PACK_BYTES + dst, vsrc + m * 512, 16);
+            if constexpr (C::TMA_ROWS) {
+                // rows past N arrive zero-filled; rows of the next chunk are masked later
+                if (lane == 0) {
+                    mbar_expect_tx(full_bar(s), 2 * C::PACK_BYTES);
+                    tma_rows<C::ROWB>(smem_u32(st), &tm_k, p0, kvh, b, full_bar(s));
+                    tma_rows<C::ROWB>(smem_u32(st + C::PACK_BYTES), &tm_v, p0, kvh, b, full_bar(s));
                 }
             } else {
-                const int kvalid = rows_valid * C::CPR;
+                const char* ksrc = kp_b + (int64_t)p0 * C::ROWB + lane * 16;
+                const char* vsrc = vp_b + (int64_t)p0 * C::ROWB + lane * 16;
+                // chunk k = lane + 32m of the stage (row k / CPR): source k*16, swizzled
+                // destination line k/8 = lane/8 + 4m, whose parity alternates with m
+                const uint32_t d_even = (uint32_t)swz<8>(lane >> 3, lane & 7) * 16u;
+                const uint32_t d_odd = (uint32_t)swz<8>((lane >> 3) + 4, lane & 7) * 16u - 512u;
+                constexpr int M = kTcTile * C::CPR / 32;
+                if (rows_valid == kTcTile) {
 #pragma unroll 4
-                for (int m = 0; m < M; ++m) {
-                    const uint32_t dst = (m & 1 ? d_odd : d_even) + m * 512u;
-                    const bool ok = lane + 32 * m < kvalid;
-                    cp_async16(st + dst, ok ? ksrc + m * 512 : kp_b, ok ? 16 : 0);
-                    cp_async16(st + C::PACK_BYTES + dst, ok ? vsrc + m * 512 : vp_b, ok ? 16 : 0);
+                    for (int m = 0; m < M; ++m) {
+                        const uint32_t dst = (m & 1 ? d_odd : d_even) + m * 512u;
+                        cp_async16(st + dst, ksrc + m * 512, 16);
+                        cp_async16(st + C::PACK_BYTES + dst, vsrc + m * 512, 16);
+                    }
+                } else {
+                    const int kvalid = rows_valid * C::CPR;
+#pragma unroll 4
+                    for (int m = 0; m < M; ++m) {
+                        const uint32_t dst = (m & 1 ? d_odd : d_even) + m * 512u;
+                        const bool ok = lane + 32 * m < kvalid;
+                        cp_async16(st + dst, ok ? ksrc + m * 512 : kp_b, ok ? 16 : 0);
+                        cp_async16(st + C::PACK_BYTES + dst, ok ? vsrc + m * 512 : vp_b, ok ? 16 : 0);
+                    }
                 }
             }
             const int sbytes = rows_valid * C::SROWB;
@@ -546,53 +609,84 @@ __global__ void __launch_bounds__(kTcThreads, 1) decode_tc_kernel(const DecodeAr
         }
         cp_async_wait<0>();
     } else if (warp == kMmaWarp) {
-        // ================= MMA issuer (one thread) =================
-        if (lane == 0) {
-            auto issue_qk = [&](int j) {
-                const int kbuf = j & 1;
-                mbar_wait<kSleepCrit>(kready_bar(kbuf), (j >> 1) & 1, dead);
-                tc_fence_after();
+        // ================= MMA issuer =================
+        // The warp runs converged (descriptors stay in uniform registers) and
+        // one elected lane issues; every descriptor is a base plus a constant
+        // 16-byte-unit offset in its start-address field.
+        const uint64_t qbase = smem_desc(sQ_u, 16, 1024, kSw128);
+        const uint64_t vbase = smem_desc(sV_u, C::V_LBO, 1024, kSw128);
+        const uint64_t pbase = smem_desc(sP_u, C::P_BYTES, 256, kSw32);
+        auto issue_qk = [&](int j) {  // keys of tile j are in TMEM
+            const int kbuf = j & 1;
+            tc_fence_after();
+            if (elect_one()) {
 #pragma unroll
                 for (int ks_ = 0; ks_ < D / 16; ++ks_) {
-                    const uint64_t qd = smem_desc(sQ_u + (ks_ >> 2) * 2048 + (ks_ & 3) * 32, 16, 1024, kSw128);
+                    const uint64_t qd = qbase + (uint64_t)(((ks_ >> 2) * 2048 + (ks_ & 3) * 32) >> 4);
                     mma_ts(tbase + kTmemS + 16 * kbuf, tbase + kTmemK + kbuf * (D / 2) + ks_ * 8, qd, IDESC_QK,
                            ks_ > 0 ? 1u : 0u);
                 }
                 mma_commit(sready_bar(kbuf));
-            };
-            int n = 0;
-            for (int i = advance(0); i < ntiles; i = advance(i + 1)) ++n;
-            if (n > 0) issue_qk(0);
-            for (int j = 0; j < n; ++j) {
-                if (j + 1 < n) issue_qk(j + 1);
-                const int vbuf = j % VB;
-                mbar_wait<kSleepCrit>(pready_bar, j & 1, dead);
-                mbar_wait<kSleepCrit>(vready_bar(vbuf), (j / VB) & 1, dead);
+            }
+            __syncwarp();
+        };
+        int n = 0;
+        for (int i = advance(0); i < ntiles; i = advance(i + 1)) ++n;
+        // Event-driven: issue the S MMA of tile jq or the P V MMA of tile jp,
+        // whichever operands are ready first.  S has two TMEM buffers, so the
+        // S MMA of tile jq waits until the softmax of tile jq - 2 is done
+        // (its P V MMA issued: jq <= jp + 1).
+        int jq = 0, jp = 0;
+        uint64_t t_idle = 0;
+        uint32_t idle = 0;
+        while (jp < n && !dead) {
+            bool progress = false;
+            if (jq < n && jq <= jp + 1 &&
+                __shfl_sync(0xffffffffu, (int)mbar_try(kready_bar(jq & 1), (jq >> 1) & 1), 0)) {
+                issue_qk(jq);
+                ++jq;
+                progress = true;
+            }
+            if (jp < jq && __shfl_sync(0xffffffffu, (int)(mbar_try(pready_bar(jp % PB), (jp / PB) & 1) &&
+                                                          mbar_try(vready_bar(jp % VB), (jp / VB) & 1)), 0)) {
+                const int vbuf = jp % VB, pbuf = jp % PB;
                 tc_fence_after();
+                if (elect_one()) {
+                    const uint64_t vb0 = vbase + (uint64_t)((vbuf * C::V_BYTES) >> 4);
+                    const uint64_t pb0 = pbase + (uint64_t)((pbuf * C::P_BUF) >> 4);
 #pragma unroll
-                for (int mb = 0; mb < C::MB; ++mb) {
+                    for (int mb = 0; mb < C::MB; ++mb) {
 #pragma unroll
-                    for (int ks_ = 0; ks_ < kTcTile / 16; ++ks_) {
-                        const uint64_t vd = smem_desc(sV_u + vbuf * C::V_BYTES + (2 * mb) * C::V_LBO + (2 * ks_) * 1024,
-                                                      C::V_LBO, 1024, kSw128);
-                        const uint64_t pd = smem_desc(sP_u + ks_ * 512, C::P_BYTES, 256, kSw32);
-                        mma_ss(tbase + kTmemO + mb * 16, vd, pd, IDESC_PV, (j > 0 || ks_ > 0) ? 1u : 0u);
-                        if constexpr (Ops<T>::kSplitP) {
-                            const uint64_t pl = smem_desc(sP_u + C::P_BYTES + ks_ * 512, C::P_BYTES, 256, kSw32);
-                            mma_ss(tbase + kTmemO + mb * 16, vd, pl, IDESC_PV, 1u);
+                        for (int ks_ = 0; ks_ < kTcTile / 16; ++ks_) {
+                            const uint64_t vd = vb0 + (uint64_t)(((2 * mb) * C::V_LBO + (2 * ks_) * 1024) >> 4);
+                            const uint64_t pd = pb0 + (uint64_t)((ks_ * 512) >> 4);
+                            mma_ss(tbase + kTmemO + mb * 16, vd, pd, IDESC_PV, (jp > 0 || ks_ > 0) ? 1u : 0u);
+                            if constexpr (Ops<T>::kSplitP)
+                                mma_ss(tbase + kTmemO + mb * 16, vd, pd + (uint64_t)(C::P_BYTES >> 4), IDESC_PV, 1u);
                         }
                     }
+                    mma_commit(pfree_bar(pbuf));
+                    mma_commit(vfree_bar(vbuf));
                 }
-                mma_commit(pfree_bar);
-                mma_commit(vfree_bar(vbuf));
+                __syncwarp();
+                ++jp;
+                progress = true;
+            }
+            if (progress) {
+                idle = 0;
+            } else {
+                // nothing ready: sleep briefly; give up after about a second
+                if (idle == 0) t_idle = global_ns();
+                __nanosleep(32);
+                if ((++idle & 255) == 0 && global_ns() - t_idle > kWaitNs) {
+                    atomicOr(&g_device_status, 1u);
+                    dead = true;
+                }
             }
         }
-        __syncwarp();
     } else if (warp < kKeyWarps) {
-        // ================= key warps: K -> TMEM, softmax, P^T =================
+        // ================= key warps: K -> TMEM =================
         const uint32_t lane_off = (uint32_t)(warp * 32) << 16;
-        const int64_t mrow = a.mask ? (int64_t)b * a.m_sb : 0;
-        const int hq0 = kvh * a.gqa + h0;
         const RowChunks<C::CPR> rows(t);
         // dequantise the j-th active tile into K buffer j & 1 of TMEM lane t
         auto load_keys = [&](int j) {
@@ -629,26 +723,28 @@ __global__ void __launch_bounds__(kTcThreads, 1) decode_tc_kernel(const DecodeAr
             if (lane == 0) mbar_arrive(kready_bar(j & 1));
         };
 
-        // step j: keys of active tile j into TMEM, then the softmax of tile j - 1
-        // (whose S MMA ran meanwhile)
-        int i_cur = advance(0), i_prev = -1, j = 0;
-        for (;; ++j) {
-            if (i_cur < ntiles) load_keys(j);
-            if (j == 0) {
-                if (i_cur >= ntiles) break;
-                i_prev = i_cur;
-                i_cur = advance(i_cur + 1);
-                continue;
-            }
-            const int js = j - 1;  // the tile whose scores are ready
-            const int i = i_prev;
+        int n = 0;
+        for (int i = advance(0); i < ntiles; i = advance(i + 1)) ++n;
+        for (int j = 0; j < n; ++j) {
+            // K buffer j & 1 was last read by the S MMA of tile j - 2
+            if (j >= 2) mbar_wait<kSleepCrit>(sready_bar(j & 1), ((j - 2) >> 1) & 1, dead);
+            load_keys(j);
+        }
+    } else if (warp >= kSmWarp0) {
+        // ================= softmax warps: S^T -> P^T =================
+        const int qw = warp & 3;  // TMEM lane quadrant: tokens 32qw..32qw+31 of the tile
+        const uint32_t lane_off = (uint32_t)(qw * 32) << 16;
+        const int64_t mrow = a.mask ? (int64_t)b * a.m_sb : 0;
+        const int hq0 = kvh * a.gqa + h0;
+        int js = 0;
+        for (int i = advance(0); i < ntiles; i = advance(i + 1), ++js) {
             mbar_wait<kSleepCrit>(sready_bar(js & 1), (js >> 1) & 1, dead);
             tc_fence_after();
             float s[kTcHeads];
             tmem_ld16(tbase + lane_off + kTmemS + 16 * (js & 1), s);
             tmem_wait_ld();
-            if (js > 0) {  // the previous P V product is done: P^T free, O^T current
-                mbar_wait<kSleepCrit>(pfree_bar, (js - 1) & 1, dead);
+            if (js >= PB) {  // P^T buffer js % PB was read by the P V MMA of tile js - PB
+                mbar_wait<kSleepCrit>(pfree_bar(js % PB), ((js - PB) / PB) & 1, dead);
                 tc_fence_after();
             }
 
@@ -667,10 +763,10 @@ __global__ void __launch_bounds__(kTcThreads, 1) decode_tc_kernel(const DecodeAr
 #pragma unroll
             for (int h = 0; h < kTcHeads; ++h) up |= s[h] > m_run[h] + kRescaleTc;
             const bool wup = __any_sync(0xffffffffu, up);
-            if (lane == 0) flags[warp] = wup ? 1 : 0;
-            named_barrier(1, kKeyWarps * 32);
+            if (lane == 0) flags[qw] = wup ? 1 : 0;
+            named_barrier(1, kSmWarps * 32);
             const bool tile_up = (flags[0] | flags[1] | flags[2] | flags[3]) != 0;
-            named_barrier(1, kKeyWarps * 32);  // flags read before the next tile's writes
+            named_barrier(1, kSmWarps * 32);  // flags read before the next tile's writes
             if (tile_up) {
                 // a score rose past the running maximum: tile maxima per head
                 float mx[kTcHeads];
@@ -683,9 +779,9 @@ __global__ void __launch_bounds__(kTcThreads, 1) decode_tc_kernel(const DecodeAr
                 }
                 if (lane == 0) {
 #pragma unroll
-                    for (int h = 0; h < kTcHeads; ++h) red[warp * kTcHeads + h] = mx[h];
+                    for (int h = 0; h < kTcHeads; ++h) red[qw * kTcHeads + h] = mx[h];
                 }
-                named_barrier(1, kKeyWarps * 32);
+                named_barrier(1, kSmWarps * 32);
                 float alpha[kTcHeads];
 #pragma unroll
                 for (int h = 0; h < kTcHeads; ++h) {
@@ -695,8 +791,11 @@ __global__ void __launch_bounds__(kTcThreads, 1) decode_tc_kernel(const DecodeAr
                     if (u) m_run[h] = v;
                     l_run[h] *= alpha[h];
                 }
-                named_barrier(1, kKeyWarps * 32);  // red read before it is written again
+                named_barrier(1, kSmWarps * 32);  // red read before it is written again
                 if (js > 0) {
+                    // O^T must hold the P V product of tile js - 1 before it is scaled
+                    mbar_wait<kSleepCrit>(pfree_bar((js - 1) % PB), ((js - 1) / PB) & 1, dead);
+                    tc_fence_after();
                     // O^T lane t holds head dims t (+128): scale column h by alpha[h]
 #pragma unroll
                     for (int mb = 0; mb < C::MB; ++mb) {
@@ -721,7 +820,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) decode_tc_kernel(const DecodeAr
             uint32_t hi[8];
 #pragma unroll
             for (int e = 0; e < 8; ++e) hi[e] = Ops<T>::pack(p[2 * e], p[2 * e + 1]);
-            char* prow = sP + t * 32;
+            char* prow = sP + (js % PB) * C::P_BUF + t * 32;
             const int sw = ((t >> 2) & 1) * 16;
             *reinterpret_cast<uint4*>(prow + sw) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
             *reinterpret_cast<uint4*>(prow + (16 ^ sw)) = make_uint4(hi[4], hi[5], hi[6], hi[7]);
@@ -740,17 +839,11 @@ __global__ void __launch_bounds__(kTcThreads, 1) decode_tc_kernel(const DecodeAr
             fence_proxy_async();
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(pready_bar);
-            if (i_cur >= ntiles) {
-                ++j;
-                break;
-            }
-            i_prev = i_cur;
-            i_cur = advance(i_cur + 1);
+            if (lane == 0) mbar_arrive(pready_bar(js % PB));
         }
-        n_active = j - 1 < 0 ? 0 : j - 1;
+        n_active = js;
         if (n_active > 0) {  // the last P V product
-            mbar_wait<kSleepCrit>(pfree_bar, (n_active - 1) & 1, dead);
+            mbar_wait<kSleepCrit>(pfree_bar((n_active - 1) % PB), ((n_active - 1) / PB) & 1, dead);
             tc_fence_after();
         }
     } else {
@@ -804,14 +897,15 @@ __global__ void __launch_bounds__(kTcThreads, 1) decode_tc_kernel(const DecodeAr
     float* mo = reinterpret_cast<float*>(ring);  // [16][D]
     float* mm = mo + kTcHeads * D;               // [16]
     float* ml = mm + kTcHeads;                   // [16]
-    if (warp < kKeyWarps) {
-        const uint32_t lane_off = (uint32_t)(warp * 32) << 16;
+    if (warp >= kSmWarp0 && warp < kSmWarp0 + kSmWarps) {
+        const int qw = warp & 3;
+        const uint32_t lane_off = (uint32_t)(qw * 32) << 16;
 #pragma unroll
         for (int h = 0; h < kTcHeads; ++h) {
             float v = l_run[h];
 #pragma unroll
             for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-            if (lane == 0) red[warp * kTcHeads + h] = v;
+            if (lane == 0) red[qw * kTcHeads + h] = v;
         }
 #pragma unroll
         for (int mb = 0; mb < C::MB; ++mb) {
@@ -827,7 +921,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) decode_tc_kernel(const DecodeAr
 #pragma unroll
             for (int h = 0; h < kTcHeads; ++h) mo[h * D + d] = o[h];
         }
-        if (tid == 0) {
+        if (warp == kSmWarp0 && lane == 0) {
 #pragma unroll
             for (int h = 0; h < kTcHeads; ++h) mm[h] = m_run[h];
         }
@@ -843,9 +937,57 @@ __global__ void __launch_bounds__(kTcThreads, 1) decode_tc_kernel(const DecodeAr
     finish_cta<T>(a, b, kvh, h0, nh, split, mo, mm, ml);
 }
 
+// cuTensorMapEncodeTiled from the driver, looked up once through the runtime
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+EncodeTiledFn encode_tiled() {
+    static EncodeTiledFn fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeTiledFn>(p);
+    });
+    return fn;
+}
+
+// Tensor map over one packed array (B, Hkv, N, ROWB bytes): 128-token boxes of
+// whole rows (a 256-byte row as two 128-byte halves), 128-byte swizzle.
+template <int ROWB>
+int encode_rows(CUtensorMap* m, const void* base, int64_t sb_words, int64_t sh_words, int N, int Hkv, int B) {
+    EncodeTiledFn enc = encode_tiled();
+    if (!enc) return set_error(QSDPA_ERR_CUDA, "cuTensorMapEncodeTiled is not available from the driver");
+    uint64_t sh = (uint64_t)sh_words * 4, sb = (uint64_t)sb_words * 4;
+    const uint64_t head_bytes = (uint64_t)N * ROWB;  // a multiple of 16
+    if (Hkv == 1 || sh < head_bytes) sh = Hkv == 1 ? head_bytes : sh;  // a size-1 dim's stride is free
+    if (B == 1 || sb == 0) sb = B == 1 ? sh * (uint64_t)Hkv : sb;
+    cuuint64_t dims[5], strides[4];
+    cuuint32_t box[5], estr[5] = {1, 1, 1, 1, 1};
+    cuuint32_t rank;
+    if constexpr (ROWB == 128) {
+        rank = 4;
+        dims[0] = 128, dims[1] = (cuuint64_t)N, dims[2] = (cuuint64_t)Hkv, dims[3] = (cuuint64_t)B;
+        strides[0] = 128, strides[1] = sh, strides[2] = sb;
+        box[0] = 128, box[1] = kTcTile, box[2] = 1, box[3] = 1;
+    } else {
+        rank = 5;
+        dims[0] = 128, dims[1] = 2, dims[2] = (cuuint64_t)N, dims[3] = (cuuint64_t)Hkv, dims[4] = (cuuint64_t)B;
+        strides[0] = 128, strides[1] = 256, strides[2] = sh, strides[3] = sb;
+        box[0] = 128, box[1] = 2, box[2] = kTcTile, box[3] = 1, box[4] = 1;
+    }
+    const CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, rank, const_cast<void*>(base), dims, strides, box, estr,
+                           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return set_error(QSDPA_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+    return QSDPA_OK;
+}
+
 template <typename T, int BITS, int D, int GS>
 int launch_tc4(const DecodeArgs& a, cudaStream_t st) {
-    using C = TcCfg<BITS, D, GS>;
+    using C = TcCfg<BITS, D, GS, Ops<T>::kSplitP>;
     auto kern = decode_tc_kernel<T, BITS, D, GS>;
     static bool attr_set[64] = {};
     int dev = 0;
@@ -855,8 +997,18 @@ int launch_tc4(const DecodeArgs& a, cudaStream_t st) {
         if (e != cudaSuccess) return set_error(QSDPA_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
         attr_set[dev] = true;
     }
+    CUtensorMap tm_k, tm_v;
+    memset(&tm_k, 0, sizeof(tm_k));
+    memset(&tm_v, 0, sizeof(tm_v));
+    if constexpr (C::TMA_ROWS) {
+        if (a.N > 0) {
+            int rc = encode_rows<C::ROWB>(&tm_k, a.kp, a.kp_sb, a.kp_sh, a.N, a.Hkv, a.B);
+            if (rc == QSDPA_OK) rc = encode_rows<C::ROWB>(&tm_v, a.vp, a.vp_sb, a.vp_sh, a.N, a.Hkv, a.B);
+            if (rc) return rc;
+        }
+    }
     dim3 grid(a.splits, a.B * a.Hkv, a.head_blocks);
-    kern<<<grid, kTcThreads, C::SMEM, st>>>(a);
+    kern<<<grid, kTcThreads, C::SMEM, st>>>(a, tm_k, tm_v);
     return check_launch("qsdpa_decode (tcgen05)");
 }
 
