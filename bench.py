@@ -59,7 +59,7 @@ def parse():
 KERNELS = {"auto": 0, "tcgen05": 1, "mma": 2, "simt": 3}
 # kernel the library picks with QSDPA_KERNEL_AUTO for this workload, and the
 # profile summaries (ncu --set full on this workload) giving DRAM traffic
-AUTO_KERNEL = "mma"
+AUTO_KERNEL = "tcgen05"
 PROFILES = {"mma": "profiles/decode_mma_128k_gqa16.md", "tcgen05": "profiles/decode_tcgen05_128k_gqa16.md"}
 
 

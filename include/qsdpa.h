@@ -54,8 +54,8 @@ enum {
 /* decode kernel selection (qsdpa_decode_params.kernel) */
 enum {
     QSDPA_KERNEL_AUTO = 0,    /* the fastest kernel that supports the call */
-    QSDPA_KERNEL_TCGEN05 = 1, /* tcgen05 / tensor-memory kernel (GQA >= 4, D 128 or 256) */
-    QSDPA_KERNEL_MMA = 2,     /* warp-level mma.sync kernel (GQA >= 4) */
+    QSDPA_KERNEL_TCGEN05 = 1, /* tcgen05 / tensor-memory kernel (D 128 or 256) */
+    QSDPA_KERNEL_MMA = 2,     /* warp-level mma.sync kernel (D 128 or 256, 64 at 8 bits) */
     QSDPA_KERNEL_SIMT = 3     /* CUDA-core kernel (every supported shape) */
 };
 

@@ -25,8 +25,15 @@ constexpr int kMaxSplits = 1024;
 constexpr int kMinChunk = 64;  // keys per CTA below which splitting stops paying
 constexpr int kLongChunk = 256;  // keys per CTA from which a second CTA per SM pays off
 constexpr int kMinChunkTc = 128;  // one tile of the tcgen05 kernel
-// QSDPA_KERNEL_AUTO prefers the tcgen05 kernel where it applies
-constexpr bool kAutoTc = false;
+constexpr int kTcMaxChunk = 8192;   // keys per CTA above which the keys are split further
+constexpr int kMmaMaxChunk = 4096;
+// QSDPA_KERNEL_AUTO takes the tcgen05 kernel from this many keys per KV head
+// and GQA groups of at least kAutoTcMinGqa heads; below either the mma.sync
+// kernel wins (measured: GQA-16 D=256 10.3 vs 9.2 us at 1K keys, 14.0 vs 14.6
+// at 16K, 35.0 vs 39.3 at 128K; one head per KV head, D=128 8-bit at 128K:
+// 162 vs 102 us)
+constexpr int kAutoTcMinKeys = 16384;
+constexpr int kAutoTcMinGqa = 8;
 }  // namespace
 
 int set_error(int code, const char* fmt, ...) {
@@ -164,18 +171,20 @@ int make_plan(const qsdpa_decode_params* p, const DecodeArgs& a, Plan& pl) {
     const bool tc_ok = tc_supported(a), mma_ok = mma_supported(a);
     switch (p->kernel) {
         case QSDPA_KERNEL_TCGEN05:
-            if (!tc_ok) return set_error(QSDPA_ERR_UNSUPPORTED, "tcgen05 kernel: needs D 128/256, GQA >= 4, 16-byte aligned K/V");
+            if (!tc_ok) return set_error(QSDPA_ERR_UNSUPPORTED, "tcgen05 kernel: needs D 128/256 and 16-byte aligned K/V rows, scales, biases");
             pl.kern = Kern::Tc;
             break;
         case QSDPA_KERNEL_MMA:
-            if (!mma_ok) return set_error(QSDPA_ERR_UNSUPPORTED, "mma kernel: needs D 128/256 (64 at 8 bits), GQA >= 4, 16-byte aligned K/V");
+            if (!mma_ok) return set_error(QSDPA_ERR_UNSUPPORTED, "mma kernel: needs D 128/256 (64 at 8 bits) and 16-byte aligned K/V rows, scales, biases");
             pl.kern = Kern::Mma;
             break;
         case QSDPA_KERNEL_SIMT:
             pl.kern = Kern::Simt;
             break;
         default:
-            pl.kern = kAutoTc && tc_ok ? Kern::Tc : (mma_ok ? Kern::Mma : Kern::Simt);
+            pl.kern = tc_ok && p->N >= kAutoTcMinKeys && a.gqa >= kAutoTcMinGqa ? Kern::Tc
+                      : mma_ok                                                      ? Kern::Mma
+                                                                                    : Kern::Simt;
     }
     pl.use_mma = pl.kern != Kern::Simt;
     pl.heads_per_block = pl.use_mma ? mma_heads_per_block(a) : simt_heads_per_block();
@@ -188,12 +197,18 @@ int make_plan(const qsdpa_decode_params* p, const DecodeArgs& a, Plan& pl) {
         // chunk holds kLongChunk keys; CUDA-core kernel: two waves of 4 per SM.
         // No chunk below kMinChunk.
         if (pl.kern == Kern::Tc) {
-            // one CTA per SM (its shared memory fills the SM), one wave
+            // one CTA per SM (its shared memory fills the SM): one wave, or
+            // more when the units alone fill the GPU, with no CTA walking more
+            // than kTcMaxChunk keys (long chunks leave a ragged last wave)
             splits = (sm_count() + units - 1) / units;
+            const int by_max = (p->N + kTcMaxChunk - 1) / kTcMaxChunk;
+            if (splits < by_max) splits = by_max;
         } else if (pl.use_mma) {
             const int lo = (sm_count() + units - 1) / units, hi = (2 * sm_count() + units - 1) / units;
             const int by_long = (p->N + kLongChunk - 1) / kLongChunk;
             splits = by_long < lo ? lo : (by_long > hi ? hi : by_long);
+            const int by_max = (p->N + kMmaMaxChunk - 1) / kMmaMaxChunk;
+            if (splits < by_max) splits = by_max;
         } else {
             splits = (sm_count() * 4 * 2 + units - 1) / units;
         }

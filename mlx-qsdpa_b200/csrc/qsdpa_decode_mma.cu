@@ -683,22 +683,24 @@ int launch2(const DecodeArgs& a, cudaStream_t st) {
     return set_error(QSDPA_ERR_UNSUPPORTED, "tensor-core decode: D=%d bits=%d", a.D, a.bits);
 }
 
-bool aligned16(const void* p, int64_t sb, int64_t sh, int elt) {
-    return p != nullptr && (uintptr_t)p % 16 == 0 && (sb * elt) % 16 == 0 && (sh * elt) % 16 == 0;
+// 16-byte aligned base and (batch, head) strides; the stride of a size-1
+// dimension is never applied and does not count
+bool aligned16(const void* p, int64_t sb, int64_t sh, int elt, int B, int H) {
+    return p != nullptr && (uintptr_t)p % 16 == 0 && (B == 1 || (sb * elt) % 16 == 0) &&
+           (H == 1 || (sh * elt) % 16 == 0);
 }
 
 }  // namespace
 
-// Minimum GQA group size routed to the tensor-core kernel.
-constexpr int kMinGqaMma = 4;
 
 bool mma_supported(const DecodeArgs& a) {
     // each warp of a pair owns half the head dim in whole packed words
     if (a.D != 128 && a.D != 256 && !(a.D == 64 && a.bits == 8)) return false;
-    if (a.gqa < kMinGqaMma) return false;
-    if (!aligned16(a.kp, a.kp_sb, a.kp_sh, 4) || !aligned16(a.vp, a.vp_sb, a.vp_sh, 4)) return false;
-    if (!aligned16(a.ks, a.ks_sb, a.ks_sh, 2) || !aligned16(a.vs, a.vs_sb, a.vs_sh, 2)) return false;
-    if (a.kb && (!aligned16(a.kb, a.kb_sb, a.kb_sh, 2) || !aligned16(a.vb, a.vb_sb, a.vb_sh, 2))) return false;
+    const int B = a.B, H = a.Hkv;
+    if (!aligned16(a.kp, a.kp_sb, a.kp_sh, 4, B, H) || !aligned16(a.vp, a.vp_sb, a.vp_sh, 4, B, H)) return false;
+    if (!aligned16(a.ks, a.ks_sb, a.ks_sh, 2, B, H) || !aligned16(a.vs, a.vs_sb, a.vs_sh, 2, B, H)) return false;
+    if (a.kb && (!aligned16(a.kb, a.kb_sb, a.kb_sh, 2, B, H) || !aligned16(a.vb, a.vb_sb, a.vb_sh, 2, B, H)))
+        return false;
     return true;
 }
 

@@ -273,6 +273,18 @@ __device__ __forceinline__ bool mbar_try(uint32_t addr, uint32_t parity) {
         : "memory");
     return ok != 0;
 }
+// Non-blocking test for completion of the phase with the given parity
+// (try_wait may suspend the thread for a while; an event loop polling several
+// barriers must not).
+__device__ __forceinline__ bool mbar_test(uint32_t addr, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(ok)
+        : "r"(addr), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
 __device__ __forceinline__ uint64_t global_ns() {
     uint64_t t;
     asm volatile("mov.u64 %0, %%globaltimer;\n" : "=l"(t));
@@ -318,9 +330,21 @@ struct RowChunks {
         for (int h = 0; h < H; ++h) x[h] = (uint32_t)(((k0 & 7) ^ (((k0 >> 3) + h) & 7)) << 4);
     }
     __device__ __forceinline__ uint32_t off(int c) const {
-        return lineb + (uint32_t)(c >> 3) * 128u + (((uint32_t)(c & 7) << 4) ^ x[c >> 3]);
+        if constexpr (H == 1) {
+            return lineb + (((uint32_t)c << 4) ^ x[0]);
+        } else {
+            // two lines per row: select, never index the array at run time
+            const uint32_t xh = (c >> 3) ? x[H > 1 ? 1 : 0] : x[0];
+            return lineb + (uint32_t)(c >> 3) * 128u + (((uint32_t)(c & 7) << 4) ^ xh);
+        }
     }
 };
+
+// (x, x) pair of the half at p
+__device__ __forceinline__ uint32_t pair_at(const char* p) {
+    const uint32_t v = lds16(p);
+    return __byte_perm(v, 0u, 0x1010);
+}
 
 // One broadcast (x, x) pair per group of a scale / bias row of G halves.
 template <int G>
@@ -642,13 +666,13 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         while (jp < n && !dead) {
             bool progress = false;
             if (jq < n && jq <= jp + 1 &&
-                __shfl_sync(0xffffffffu, (int)mbar_try(kready_bar(jq & 1), (jq >> 1) & 1), 0)) {
+                __shfl_sync(0xffffffffu, (int)mbar_test(kready_bar(jq & 1), (jq >> 1) & 1), 0)) {
                 issue_qk(jq);
                 ++jq;
                 progress = true;
             }
-            if (jp < jq && __shfl_sync(0xffffffffu, (int)(mbar_try(pready_bar(jp % PB), (jp / PB) & 1) &&
-                                                          mbar_try(vready_bar(jp % VB), (jp / VB) & 1)), 0)) {
+            if (jp < jq && __shfl_sync(0xffffffffu, (int)(mbar_test(pready_bar(jp % PB), (jp / PB) & 1) &&
+                                                          mbar_test(vready_bar(jp % VB), (jp / VB) & 1)), 0)) {
                 const int vbuf = jp % VB, pbuf = jp % PB;
                 tc_fence_after();
                 if (elect_one()) {
@@ -694,14 +718,6 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             mbar_wait<kSleepCrit>(full_bar(s), (j / ST) & 1, dead);
             const char* st = ring + s * C::STAGE_BYTES;
             const char* s_sc = st + 2 * C::PACK_BYTES + t * C::SROWB;
-            uint32_t sc[C::G], bi[C::G];
-            load_pairs<C::G>(s_sc, sc);
-            if (has_bias) {
-                load_pairs<C::G>(s_sc + C::SC_BYTES, bi);
-            } else {
-#pragma unroll
-                for (int g = 0; g < C::G; ++g) bi[g] = 0u;
-            }
             constexpr int CPS = 32 / PPC;  // chunks per 32-column store
             const uint32_t kcol = tbase + lane_off + kTmemK + (j & 1) * (D / 2);
 #pragma unroll 1
@@ -711,7 +727,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 for (int u = 0; u < CPS; ++u) {
                     const int c = c0 + u;
                     const int g = (c * EPC) / GS;
-                    dequant_chunk<T, BITS>(lds128(st + rows.off(c)), sc[g], bi[g], &cols[u * PPC]);
+                    const uint32_t s2 = pair_at(s_sc + g * 2);
+                    const uint32_t b2 = has_bias ? pair_at(s_sc + C::SC_BYTES + g * 2) : 0u;
+                    dequant_chunk<T, BITS>(lds128(st + rows.off(c)), s2, b2, &cols[u * PPC]);
                 }
                 tmem_st32(kcol + c0 * PPC, cols);
             }
@@ -856,14 +874,6 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             mbar_wait<kSleepIdle>(full_bar(s), (j / ST) & 1, dead);
             const char* st = ring + s * C::STAGE_BYTES;
             const char* s_vsc = st + 2 * C::PACK_BYTES + 2 * C::SC_BYTES + t * C::SROWB;
-            uint32_t sc[C::G], bi[C::G];
-            load_pairs<C::G>(s_vsc, sc);
-            if (has_bias) {
-                load_pairs<C::G>(s_vsc + C::SC_BYTES, bi);
-            } else {
-#pragma unroll
-                for (int g = 0; g < C::G; ++g) bi[g] = 0u;
-            }
             if (j >= VB) mbar_wait<kSleepIdle>(vfree_bar(vbuf), ((j / VB) - 1) & 1, dead);
             // token t's row of each 1024-byte atom (8 tokens x 64 dims) of 64-dim
             // block w8/8; 16-byte slot (w8 % 8) ^ (t % 8)
@@ -872,8 +882,10 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 #pragma unroll 2
             for (int c = 0; c < C::CPR; ++c) {
                 const int g = (c * EPC) / GS;
+                const uint32_t s2 = pair_at(s_vsc + g * 2);
+                const uint32_t b2 = has_bias ? pair_at(s_vsc + C::SC_BYTES + g * 2) : 0u;
                 uint32_t o[PPC];
-                dequant_chunk<T, BITS>(lds128(st + C::PACK_BYTES + rows.off(c)), sc[g], bi[g], o);
+                dequant_chunk<T, BITS>(lds128(st + C::PACK_BYTES + rows.off(c)), s2, b2, o);
                 // every 4 pairs are 8 consecutive head dims: one 16-byte store
 #pragma unroll
                 for (int e = 0; e < PPC / 4; ++e) {
@@ -1029,20 +1041,25 @@ int launch_tc2(const DecodeArgs& a, cudaStream_t st) {
     return set_error(QSDPA_ERR_UNSUPPORTED, "tcgen05 decode: D=%d", a.D);
 }
 
-bool aligned16_tc(const void* p, int64_t sb, int64_t sh, int elt) {
-    return p != nullptr && (uintptr_t)p % 16 == 0 && (sb * elt) % 16 == 0 && (sh * elt) % 16 == 0;
+// 16-byte aligned base and (batch, head) strides; the stride of a size-1
+// dimension is never applied and does not count
+bool aligned16_tc(const void* p, int64_t sb, int64_t sh, int elt, int B, int H) {
+    return p != nullptr && (uintptr_t)p % 16 == 0 && (B == 1 || (sb * elt) % 16 == 0) &&
+           (H == 1 || (sh * elt) % 16 == 0);
 }
 
 }  // namespace
 
-// The tcgen05 kernel: D of 128 or 256, GQA groups of at least 4 heads (padded
-// to the MMA's N = 16), 16-byte aligned packed rows, scales and biases.
+// The tcgen05 kernel: D of 128 or 256, any GQA group (blocks of 16 query heads,
+// the last one padded with zero queries), 16-byte aligned packed rows, scales
+// and biases.
 bool tc_supported(const DecodeArgs& a) {
     if (a.D != 128 && a.D != 256) return false;
-    if (a.gqa < 4) return false;
-    if (!aligned16_tc(a.kp, a.kp_sb, a.kp_sh, 4) || !aligned16_tc(a.vp, a.vp_sb, a.vp_sh, 4)) return false;
-    if (!aligned16_tc(a.ks, a.ks_sb, a.ks_sh, 2) || !aligned16_tc(a.vs, a.vs_sb, a.vs_sh, 2)) return false;
-    if (a.kb && (!aligned16_tc(a.kb, a.kb_sb, a.kb_sh, 2) || !aligned16_tc(a.vb, a.vb_sb, a.vb_sh, 2))) return false;
+    const int B = a.B, H = a.Hkv;
+    if (!aligned16_tc(a.kp, a.kp_sb, a.kp_sh, 4, B, H) || !aligned16_tc(a.vp, a.vp_sb, a.vp_sh, 4, B, H)) return false;
+    if (!aligned16_tc(a.ks, a.ks_sb, a.ks_sh, 2, B, H) || !aligned16_tc(a.vs, a.vs_sb, a.vs_sh, 2, B, H)) return false;
+    if (a.kb && (!aligned16_tc(a.kb, a.kb_sb, a.kb_sh, 2, B, H) || !aligned16_tc(a.vb, a.vb_sb, a.vb_sh, 2, B, H)))
+        return false;
     return true;
 }
 

@@ -191,6 +191,18 @@ def test_long_context(lib):
 
 
 def test_unsupported_shapes_are_errors(lib):
-    c = Case(1, 4, 4, 64, 128, seed=13)  # no GQA
+    c = Case(1, 4, 1, 64, 32, seed=13)  # D = 32
     with pytest.raises(NotImplementedError, match="tcgen05"):
         decode(lib, c)
+
+
+@pytest.mark.parametrize("shape", [(1, 8, 8, 700, 128), (2, 4, 2, 300, 256), (1, 3, 1, 129, 256)])
+@pytest.mark.parametrize("bits,gs", [(8, 64), (4, 128)])
+def test_small_gqa_groups(lib, shape, bits, gs):
+    """GQA groups of 1-3 heads: the 16-head block is padded with zero queries."""
+    B, Hq, Hkv, N, D = shape
+    c = Case(B, Hq, Hkv, N, D, bits=bits, gs=gs, dtype=O.BF16, seed=N + bits)
+    cap = (N + 255) // 256 * 256  # cache capacity: aligned head strides for any N
+    check(lib, c, cap=cap)
+    check(lib, c, splits=1, cap=cap)
+    check(lib, c, kernel=lib.KERNEL_MMA, cap=cap)

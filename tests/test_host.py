@@ -247,3 +247,11 @@ def test_batch_rotating_merge_and_ranges(cpu_kernels):
     assert np.array_equal(b.make_mask(1).numpy(), mb.make_mask(1))
     e = b.extract(2)
     assert e.offset == 8 and e._idx == 8
+
+
+def test_benchmarks_module_imports():
+    """The GPU benchmark CLI (python -m mlx_qsdpa.benchmarks) imports without a device."""
+    import mlx_qsdpa.benchmarks as bm
+    assert set(bm.KERNELS) == {"auto", "tcgen05", "mma", "simt"}
+    # config 2 bytes per call at 128K: q + out + 320 B per key per KV head
+    assert bm.algorithmic_bytes(1, 32, 2, 131072, 256, 4, 32, True) == 2 * 32 * 256 * 2 + 2 * 2 * 131072 * 160
