@@ -51,6 +51,8 @@ def parse():
     ap.add_argument("--layers", type=int, default=LAYERS)
     ap.add_argument("--no-graph", action="store_true", help="launch eagerly instead of CUDA graphs")
     ap.add_argument("--cpu-sample-calls", type=int, default=3)
+    ap.add_argument("--collective", choices=["p2p", "nccl"], default="p2p",
+                    help="N>1: merge the ranks' records over NVLink peer memory or with an NCCL all-gather")
     ap.add_argument("--kernel", choices=list(KERNELS), default="auto",
                     help="decode kernel of the timed path (profiling); e2e always uses the public API's choice")
     return ap.parse_args()
@@ -246,7 +248,7 @@ def main():
 
     import mlx_qsdpa
     from mlx_qsdpa import _lib
-    from mlx_qsdpa.sharded import sharded_quantized_sdpa
+    from mlx_qsdpa.sharded import PeerExchange, sharded_quantized_sdpa
 
     ctx = args.ctx
     L = args.layers
@@ -257,12 +259,14 @@ def main():
     scale = D ** -0.5
     stream = torch.cuda.current_stream(dev)
 
+    exchange = None
     if world > 1:
         # one packed record per rank, [o (rows x D) | m, l (rows x 2)]: one all-gather per step
         rows = B * HQ
         rec = torch.empty(rows * (D + 2), dtype=torch.float32, device=dev)
         part = (rec[: rows * D].view(rows, D), rec[rows * D:].view(rows, 2))
         gath = torch.empty((world, rows * (D + 2)), dtype=torch.float32, device=dev)
+        exchange = PeerExchange(rows, D, device=dev) if args.collective == "p2p" else None
 
     outs = [torch.empty((B, HQ, 1, D), dtype=torch.float16, device=dev) for _ in range(L)]
 
@@ -276,8 +280,11 @@ def main():
         else:
             _lib.decode(q, pk, pv, ks, vs, kb, vb, scale=scale, bits=BITS, group_size=GS,
                         out_mode=_lib.OUT_PARTIAL, part=part, kernel=kern_code)
-            dist.all_gather_into_tensor(gath, rec)
-            _lib.combine_packed(gath, rows, D, out=outs[i % L].view(rows, D))
+            if exchange is not None:
+                exchange.merge(rec, outs[i % L].view(rows, D))
+            else:
+                dist.all_gather_into_tensor(gath, rec)
+                _lib.combine_packed(gath, rows, D, out=outs[i % L].view(rows, D))
 
     # warm-up (also allocates the decode workspace outside any capture)
     for i in range(max(args.warmup, 3)):
@@ -384,7 +391,8 @@ def main():
         if world == 1:
             o = mlx_qsdpa.quantized_sdpa(qd, pk, pv, ks, vs, kb, vb, scale=scale, bits=BITS, group_size=GS)
         else:
-            o = sharded_quantized_sdpa(qd, (pk, ks, kb), (pv, vs, vb), bits=BITS, group_size=GS, scale=scale)
+            o = sharded_quantized_sdpa(qd, (pk, ks, kb), (pv, vs, vb), bits=BITS, group_size=GS, scale=scale,
+                                       exchange=exchange)
         out_host.copy_(o, non_blocking=True)
 
     for i in range(3):
@@ -417,6 +425,8 @@ def main():
         (pk0, ks0, kb0), (pv0, vs0, vb0) = layers[0]
         splits = _lib.plan_splits(q, pk0, pv0, ks0, vs0, kb0, vb0, BITS, GS, kernel=kern_code)
         traffic, traffic_src = profiled_traffic(args.kernel)
+        # decode (+ split merge); N>1: + the peer exchange-and-merge kernel (p2p) or, after NCCL's
+        # all-gather, the record merge
         launches_per_step = (1 if splits == 1 else 2) + (1 if world > 1 else 0)
         line = {
             "metric": METRIC,
@@ -439,7 +449,8 @@ def main():
                 "l2": "inputs larger than L2: 12 layers x %.1f MB rotated" % (bytes_local / 1e6),
                 "launch": graph_note, "splits": splits,
                 "kernel": AUTO_KERNEL if args.kernel == "auto" else args.kernel,
-                "parallelism": "sequence-sharded" if world > 1 else "single GPU",
+                "parallelism": (f"sequence-sharded, records merged over {'NVLink peer memory' if args.collective == 'p2p' else 'NCCL all-gather'}"
+                                if world > 1 else "single GPU"),
             },
             "gbs_per_gpu": round(achieved, 1),
             "roofline": {
@@ -470,6 +481,7 @@ def main():
         torch.cuda.synchronize(dev)
         kgraphs = None
         graphs.clear()
+        exchange = None
         import gc
         gc.collect()
         torch.cuda.synchronize(dev)

@@ -234,10 +234,33 @@ typedef struct qsdpa_dequantize_params {
 int qsdpa_dequantize(const qsdpa_dequantize_params* p, void* stream);
 
 /*
- * Device-side faults recorded by the decode kernels since the last reset:
- * bit 0 = a wait on a tensor-core completion barrier ran out of time (the
- * kernel gave up after ~1 s, left its output undefined and returned instead of
- * hanging).  Synchronises the device.  0 when healthy; `reset` != 0 clears it.
+ * Sequence-sharded decode: merge of the ranks' partial records over NVLink
+ * peer memory (no reference counterpart; replaces an all-gather + qsdpa_combine).
+ *
+ * Each of the `world` (<= 8) ranks owns a buffer of qsdpa_shard_buffer_bytes()
+ * bytes, zero-initialised, that every rank can address (symmetric memory:
+ * `bufs[r]` is rank r's buffer as seen from this process); `state` is two
+ * zero-initialised uint32 on this device.  Every rank calls qsdpa_shard_merge
+ * once per step with its partial record `rec` (rows * (D + 2) fp32:
+ * [o: rows x D | (m, l): rows x 2], as qsdpa_decode writes with
+ * QSDPA_OUT_PARTIAL into one buffer) and gets the merged attention output
+ * (rows x D, `dtype`) in `out`.  The call stores the record into every
+ * rank's buffer, waits for the other ranks' records of the same step and
+ * merges them; the step counter lives on the device, so the calls can be
+ * captured in a CUDA graph.  All ranks must make the same sequence of calls.
+ * A wait that runs out (~1 s: a rank that never arrives) sets bit 1 of
+ * qsdpa_device_status() and leaves `out` undefined.
+ */
+size_t qsdpa_shard_buffer_bytes(int world, int rows, int D);
+int qsdpa_shard_merge(const float* rec, float* const* bufs, unsigned int* state, int rank, int world, int rows,
+                      int D, void* out, int dtype, void* stream);
+
+/*
+ * Device-side faults recorded by the kernels since the last reset: bit 0 = a
+ * wait on a tensor-core completion barrier ran out of time, bit 1 = a
+ * sharded merge waited in vain for another rank (the kernel gave up after
+ * ~1 s, left its output undefined and returned instead of hanging).
+ * Synchronises the device.  0 when healthy; `reset` != 0 clears it.
  */
 int qsdpa_device_status(int reset);
 

@@ -300,6 +300,13 @@ extern "C" int qsdpa_decode(const qsdpa_decode_params* p, void* stream) {
     return QSDPA_OK;
 }
 
+extern "C" int qsdpa_device_status(int reset) {
+    if (cudaDeviceSynchronize() != cudaSuccess) return QSDPA_ERR_CUDA;
+    const int a = read_tc_status(reset), b = read_shard_status(reset);
+    if (a < 0 || b < 0) return QSDPA_ERR_CUDA;
+    return a | b;
+}
+
 extern "C" const char* qsdpa_last_error(void) { return g_last_error.c_str(); }
 
 extern "C" int qsdpa_abi_version(void) { return QSDPA_ABI_VERSION; }

@@ -242,7 +242,7 @@ __device__ __forceinline__ void mbar_expect_tx(uint32_t addr, uint32_t bytes) {
     asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;\n" ::"r"(addr), "r"(bytes) : "memory");
 }
 // One tile of packed rows (128 rows starting at token p0 of (b, kvh)) by TMA,
-// completing on an mbarrier's transaction count.  No multicast.
+// completing on an mbarrier's transaction count; this CTA's own copy only.
 template <int ROWB>
 __device__ __forceinline__ void tma_rows(uint32_t dst, const CUtensorMap* map, int p0, int kvh, int b, uint32_t mbar) {
     if constexpr (ROWB == 128) {
@@ -1068,9 +1068,8 @@ int launch_decode_tc(const DecodeArgs& a, int dtype, cudaStream_t st) {
     return a.bits == 4 ? launch_tc2<__nv_bfloat16, 4>(a, st) : launch_tc2<__nv_bfloat16, 8>(a, st);
 }
 
-int read_device_status(int reset) {
+int read_tc_status(int reset) {
     unsigned int v = 0;
-    if (cudaDeviceSynchronize() != cudaSuccess) return QSDPA_ERR_CUDA;
     if (cudaMemcpyFromSymbol(&v, g_device_status, sizeof(v)) != cudaSuccess) return QSDPA_ERR_CUDA;
     if (reset && v) {
         const unsigned int z = 0;
@@ -1081,4 +1080,3 @@ int read_device_status(int reset) {
 
 }  // namespace qsdpa
 
-extern "C" int qsdpa_device_status(int reset) { return qsdpa::read_device_status(reset); }

@@ -159,6 +159,10 @@ int launch_decode_simt(const DecodeArgs& a, int dtype, cudaStream_t s);
 int launch_decode_mma(const DecodeArgs& a, int dtype, cudaStream_t s);
 int launch_decode_tc(const DecodeArgs& a, int dtype, cudaStream_t s);
 bool tc_supported(const DecodeArgs& a);
+// Device-side fault bits of the tcgen05 kernel and of the sharded merge
+// (each file keeps its own word); reset clears them.
+int read_tc_status(int reset);
+int read_shard_status(int reset);
 bool mma_supported(const DecodeArgs& a);
 int mma_heads_per_block(const DecodeArgs& a);
 // Merge parts of partial records (part p of row r: o at po + p*so + r*ro,

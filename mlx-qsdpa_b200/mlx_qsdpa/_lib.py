@@ -83,8 +83,8 @@ class DequantizeParams(ctypes.Structure):
 # Every function the C header declares (checked by the CPU test suite).
 EXPORTS = (
     "qsdpa_decode", "qsdpa_decode_noalloc", "qsdpa_decode_splits", "qsdpa_decode_workspace_size",
-    "qsdpa_combine", "qsdpa_quantize", "qsdpa_dequantize", "qsdpa_device_status", "qsdpa_last_error",
-    "qsdpa_abi_version",
+    "qsdpa_combine", "qsdpa_quantize", "qsdpa_dequantize", "qsdpa_device_status", "qsdpa_shard_buffer_bytes",
+    "qsdpa_shard_merge", "qsdpa_last_error", "qsdpa_abi_version",
 )
 
 _lib = None
@@ -120,6 +120,11 @@ def load() -> ctypes.CDLL:
         lib.qsdpa_quantize.restype = ctypes.c_int
         lib.qsdpa_dequantize.argtypes = [P(DequantizeParams), _c_vp]
         lib.qsdpa_dequantize.restype = ctypes.c_int
+        lib.qsdpa_shard_buffer_bytes.argtypes = [ctypes.c_int, ctypes.c_int, ctypes.c_int]
+        lib.qsdpa_shard_buffer_bytes.restype = ctypes.c_size_t
+        lib.qsdpa_shard_merge.argtypes = [_c_vp, ctypes.POINTER(_c_vp), _c_vp, ctypes.c_int, ctypes.c_int,
+                                          ctypes.c_int, ctypes.c_int, _c_vp, ctypes.c_int, _c_vp]
+        lib.qsdpa_shard_merge.restype = ctypes.c_int
         lib.qsdpa_device_status.argtypes = [ctypes.c_int]
         lib.qsdpa_device_status.restype = ctypes.c_int
         lib.qsdpa_last_error.argtypes = []
@@ -279,6 +284,21 @@ def plan_splits(q, kp, vp, ks, vs, kb, vb, bits: int, group_size: int, splits: i
     rc = lib.qsdpa_decode_splits(ctypes.byref(p))
     _check(rc if rc < 0 else 0, "qsdpa_decode_splits")
     return rc
+
+
+def shard_buffer_bytes(world: int, rows: int, D: int) -> int:
+    """Bytes of each rank's symmetric buffer for qsdpa_shard_merge."""
+    return int(load().qsdpa_shard_buffer_bytes(world, rows, D))
+
+
+def shard_merge(rec: torch.Tensor, bufs, state: torch.Tensor, rank: int, world: int, rows: int, D: int,
+                out: torch.Tensor):
+    """qsdpa_shard_merge: exchange records over peer memory and merge into out (rows, D)."""
+    lib = load()
+    ptrs = (_c_vp * world)(*[int(b) for b in bufs])
+    _check(lib.qsdpa_shard_merge(rec.data_ptr(), ptrs, state.data_ptr(), rank, world, rows, D, out.data_ptr(),
+                                 dtype_code(out.dtype), _stream(out.device)), "qsdpa_shard_merge")
+    return out
 
 
 def device_status(reset: bool = False) -> int:

@@ -9,6 +9,12 @@ small records (``B*H_q*(D+2)*4`` bytes per rank) and every rank merges them
 with the combine kernel, so the attention output ends up replicated, as the
 next layer needs it.
 
+On one node the records travel over NVLink peer memory instead of a
+collective (:class:`PeerExchange`): every rank stores its record into every
+rank's symmetric buffer and merges as soon as the others' records of the same
+step have arrived -- two kernels, no NCCL call.  The all-gather path remains
+for process groups without peer access (gloo, tests).
+
 Appends go to the rank that owns the tail of the sequence
 (:class:`SequenceShardedCache`).  Batches shard by sequence instead and need no
 collective at all (each rank runs the unsharded decode on its own rows).
@@ -24,7 +30,43 @@ import torch.distributed as dist
 from . import _lib
 from .cache import QuantizedSDPACache
 
-__all__ = ["sharded_quantized_sdpa", "merge_partials", "SequenceShardedCache"]
+__all__ = ["sharded_quantized_sdpa", "merge_partials", "SequenceShardedCache", "PeerExchange"]
+
+
+class PeerExchange:
+    """Peer-memory merge of the ranks' partial records (qsdpa_shard_merge).
+
+    Allocates this rank's symmetric buffer (torch symmetric memory, addressable
+    by every rank of ``group`` over NVLink) and a two-word device step counter.
+    Collective: every rank of the group constructs it with the same sizes.
+    """
+
+    def __init__(self, rows: int, D: int, group=None, device=None):
+        import torch.distributed._symmetric_memory as symm
+        self.group = group if group is not None else dist.group.WORLD
+        self.rank = dist.get_rank(self.group)
+        self.world = dist.get_world_size(self.group)
+        self.rows, self.D = rows, D
+        dev = device if device is not None else torch.device("cuda", torch.cuda.current_device())
+        nbytes = _lib.shard_buffer_bytes(self.world, rows, D)
+        if nbytes == 0:
+            raise ValueError(f"peer exchange supports up to 8 ranks, got {self.world}")
+        if hasattr(symm, "enable_symm_mem_for_group"):
+            try:
+                symm.enable_symm_mem_for_group(self.group.group_name)
+            except Exception:  # noqa: BLE001 - already enabled / not needed in this torch version
+                pass
+        self.buf = symm.empty((nbytes + 3) // 4, dtype=torch.float32, device=dev)
+        self.buf.zero_()
+        self.handle = symm.rendezvous(self.buf, self.group)
+        self.ptrs = list(self.handle.buffer_ptrs)
+        self.state = torch.zeros(2, dtype=torch.int32, device=dev)
+        torch.cuda.synchronize(dev)
+        dist.barrier(group=self.group)
+
+    def merge(self, rec: torch.Tensor, out: torch.Tensor) -> torch.Tensor:
+        """Merge this step's records of all ranks; rec is (rows*(D+2),) fp32, out (rows, D)."""
+        return _lib.shard_merge(rec, self.ptrs, self.state, self.rank, self.world, self.rows, self.D, out)
 
 
 def _gather(t: torch.Tensor, group) -> torch.Tensor:
@@ -46,7 +88,7 @@ def merge_partials(gath_o: torch.Tensor, gath_ml: torch.Tensor, dtype: torch.dty
 
 def sharded_quantized_sdpa(q, k_quant, v_quant, *, bits=4, group_size=32, scale=None, mask=None,
                            group=None, partial_fn: Optional[Callable] = None,
-                           combine_fn: Optional[Callable] = None):
+                           combine_fn: Optional[Callable] = None, exchange: Optional[PeerExchange] = None):
     """Decode attention over a sequence sharded across the ranks of ``group``.
 
     Args:
@@ -59,7 +101,9 @@ def sharded_quantized_sdpa(q, k_quant, v_quant, *, bits=4, group_size=32, scale=
 
     ``partial_fn(q, k_quant, v_quant, scale, bits, group_size, mask)`` and
     ``combine_fn(gath_o, gath_ml, dtype)`` default to the CUDA kernels; the
-    CPU tests substitute the oracle to exercise the collective logic.
+    CPU tests substitute the oracle to exercise the collective logic.  With
+    ``exchange`` (a :class:`PeerExchange` for this group and shape) the records
+    move over peer memory instead of an all-gather.
     """
     B, Hq, qL, D = q.shape
     if qL != 1:
@@ -76,6 +120,9 @@ def sharded_quantized_sdpa(q, k_quant, v_quant, *, bits=4, group_size=32, scale=
         po, pml = partial_fn(q, k_quant, v_quant, scale, bits, group_size, mask)
         part[0].copy_(po)
         part[1].copy_(pml)
+    if exchange is not None:
+        out = torch.empty((rows, D), dtype=q.dtype, device=q.device)
+        return exchange.merge(rec, out).view(B, Hq, 1, D)
     gath = _gather(rec, group)
     if combine_fn is None:
         out = _lib.combine_packed(gath, rows, D, dtype=q.dtype)

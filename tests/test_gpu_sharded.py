@@ -1,0 +1,100 @@
+"""Sequence-sharded decode on GPUs: the peer-memory merge (qsdpa_shard_merge).
+
+* With two or more GPUs: two ranks (NCCL, one process per GPU) hold halves
+  of the keys; the merged output over NVLink peer memory, and over the NCCL
+  all-gather path, must match the single-GPU decode of the whole sequence
+  and the oracle.  Skipped on a one-GPU box.
+* On one GPU: a merge whose peer never arrives (its flag is never set) must
+  give up after about a second and report it in bit 1 of the device status
+  word, without hanging the device.
+"""
+
+import os
+import socket
+
+import numpy as np
+import pytest
+
+import qsdpa_oracle as O
+from qsdpa_testlib import Case, assert_close, from_torch
+
+torch = pytest.importorskip("torch")
+pytestmark = pytest.mark.gpu
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _worker(rank, world, port, q_list):
+    import datetime
+    import torch.distributed as dist
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=dev,
+                            timeout=datetime.timedelta(seconds=60))
+    try:
+        from mlx_qsdpa import _lib
+        from mlx_qsdpa.sharded import PeerExchange, sharded_quantized_sdpa
+        c = Case(1, 32, 2, 4096, 256, seed=7)
+        q, pk, pv, ks, vs, kb, vb = c.torch_args(device=f"cuda:{rank}")
+        n = c.N // world
+        sl = lambda t: t[:, :, rank * n:(rank + 1) * n]
+        kq, vq = (sl(pk), sl(ks), sl(kb)), (sl(pv), sl(vs), sl(vb))
+        ex = PeerExchange(32, 256, device=dev)
+        errs = []
+        for step in range(3):  # several steps: the device step counter and both slot parities
+            out = sharded_quantized_sdpa(q, kq, vq, bits=4, group_size=32, exchange=ex)
+            errs.append(from_torch(out))
+        out_nccl = from_torch(sharded_quantized_sdpa(q, kq, vq, bits=4, group_size=32))
+        full = from_torch(_lib.decode(q, pk, pv, ks, vs, kb, vb, scale=256 ** -0.5, bits=4, group_size=32))
+        status = _lib.device_status(reset=True)
+        q_list.put((rank, errs, out_nccl, full, status))
+        del ex
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_two_rank_peer_merge_matches_single_gpu():
+    import torch.multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    q_list = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, q_list)) for r in range(2)]
+    for p in procs:
+        p.start()
+    results = [q_list.get(timeout=300) for _ in procs]
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    ref = Case(1, 32, 2, 4096, 256, seed=7).reference()
+    for rank, outs, out_nccl, full, status in results:
+        assert status == 0, f"rank {rank}: device status {status}"
+        for o in outs:
+            assert_close(o, ref, what=f"rank {rank} peer merge")
+            assert np.abs(o - full).max() < 2e-3
+        assert_close(out_nccl, ref, what=f"rank {rank} nccl merge")
+
+
+@pytest.mark.skipif(not torch.cuda.is_available(), reason="needs a GPU")
+def test_missing_peer_times_out_and_reports():
+    """World of two on one GPU where rank 1 never runs: rank 0's wait for its
+    flag ends after ~1 s with bit 1 of the status word set."""
+    from mlx_qsdpa import _lib
+    _lib.load()
+    _lib.device_status(reset=True)
+    rows, D = 32, 256
+    nbytes = _lib.shard_buffer_bytes(2, rows, D)
+    bufs = [torch.zeros(nbytes // 4 + 4, dtype=torch.float32, device="cuda") for _ in range(2)]
+    state = torch.zeros(2, dtype=torch.int32, device="cuda")
+    rec = torch.zeros(rows * (D + 2), dtype=torch.float32, device="cuda")
+    out = torch.empty((rows, D), dtype=torch.float16, device="cuda")
+    _lib.shard_merge(rec, [b.data_ptr() for b in bufs], state, 0, 2, rows, D, out)
+    torch.cuda.synchronize()
+    assert _lib.device_status(reset=True) & 2
+    assert _lib.device_status() == 0
