@@ -22,6 +22,8 @@ collective at all (each rank runs the unsharded decode on its own rows).
 
 from __future__ import annotations
 
+import warnings
+
 from typing import Callable, Optional
 
 import torch
@@ -52,10 +54,12 @@ class PeerExchange:
         if nbytes == 0:
             raise ValueError(f"peer exchange supports up to 8 ranks, got {self.world}")
         if hasattr(symm, "enable_symm_mem_for_group"):
-            try:
-                symm.enable_symm_mem_for_group(self.group.group_name)
-            except Exception:  # noqa: BLE001 - already enabled / not needed in this torch version
-                pass
+            with warnings.catch_warnings():  # deprecated (a no-op) in newer torch, required in older
+                warnings.simplefilter("ignore", FutureWarning)
+                try:
+                    symm.enable_symm_mem_for_group(self.group.group_name)
+                except Exception:  # noqa: BLE001 - already enabled
+                    pass
         self.buf = symm.empty((nbytes + 3) // 4, dtype=torch.float32, device=dev)
         self.buf.zero_()
         self.handle = symm.rendezvous(self.buf, self.group)
