@@ -65,9 +65,10 @@ constexpr int kKeyWarps = 4;    // warps 0-3: keys -> TMEM
 constexpr int kValWarps = 4;    // warps 4-7: values -> V^T operand
 constexpr int kSmWarps = 4;     // warps 8-11: softmax -> P^T, final O^T read-out
 constexpr int kSmWarp0 = kKeyWarps + kValWarps;
-constexpr int kProdWarp = kSmWarp0 + kSmWarps;  // ring producer (cp.async)
-constexpr int kMmaWarp = kProdWarp + 1;         // TMEM owner and MMA issuer
-constexpr int kTcThreads = (kMmaWarp + 1) * 32;
+constexpr int kProdWarp = kSmWarp0 + kSmWarps;  // ring producer (TMA / cp.async)
+constexpr int kMmaWarp = kProdWarp + 1;         // TMEM owner, issues the S MMAs
+constexpr int kPvWarp = kMmaWarp + 1;           // issues the P V MMAs
+constexpr int kTcThreads = (kPvWarp + 1) * 32;
 constexpr int kTcTile = 128;    // tokens per tile = M of the S MMA
 constexpr int kTcHeads = 16;    // query heads per CTA = N of both MMAs
 constexpr int kTmemCols = 512;  // the whole SM's tensor memory: one CTA per SM
@@ -273,47 +274,38 @@ __device__ __forceinline__ bool mbar_try(uint32_t addr, uint32_t parity) {
         : "memory");
     return ok != 0;
 }
-// Non-blocking test for completion of the phase with the given parity
-// (try_wait may suspend the thread for a while; an event loop polling several
-// barriers must not).
-__device__ __forceinline__ bool mbar_test(uint32_t addr, uint32_t parity) {
-    uint32_t ok;
-    asm volatile(
-        "{\n .reg .pred p;\n mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
-        : "=r"(ok)
-        : "r"(addr), "r"(parity)
-        : "memory");
-    return ok != 0;
-}
 __device__ __forceinline__ uint64_t global_ns() {
     uint64_t t;
     asm volatile("mov.u64 %0, %%globaltimer;\n" : "=l"(t));
     return t;
 }
+// try_wait that suspends the thread until the phase completes or about
+// `hint_ns` pass: a waiting warp issues nothing and wakes when the barrier
+// completes.
+__device__ __forceinline__ bool mbar_try_sleep(uint32_t addr, uint32_t parity, uint32_t hint_ns) {
+    uint32_t ok;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n selp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(ok)
+        : "r"(addr), "r"(parity), "r"(hint_ns)
+        : "memory");
+    return ok != 0;
+}
+constexpr uint32_t kSuspendNs = 50000;  // longest suspension of one try_wait
 // Wait for completion of the phase with the given parity, for at most about a
-// second.  Between polls the warp sleeps, doubling from 32 ns up to `max_ns`,
-// so waiting warps leave the issue slots to the warps sharing their scheduler
-// (short sleeps for roles on the critical path, long ones for the others).  A
-// thread whose wait ran out stops waiting from then on, so the kernel still
-// finishes.
-template <uint32_t MaxNs>
+// second.  A thread whose wait ran out stops waiting from then on, so the
+// kernel still finishes.
 __device__ __forceinline__ void mbar_wait(uint32_t addr, uint32_t parity, bool& dead) {
     if (dead || mbar_try(addr, parity)) return;
     const uint64_t t0 = global_ns();
-    uint32_t ns = 32;
-    for (uint32_t it = 1;; ++it) {
-        __nanosleep(ns);
-        if (ns < MaxNs) ns <<= 1;
-        if (mbar_try(addr, parity)) return;
-        if ((it & 63) == 0 && global_ns() - t0 > kWaitNs) {
+    while (!mbar_try_sleep(addr, parity, kSuspendNs)) {
+        if (global_ns() - t0 > kWaitNs) {
             atomicOr(&g_device_status, 1u);
             dead = true;
             return;
         }
     }
 }
-constexpr uint32_t kSleepCrit = 64;   // key and MMA warps
-constexpr uint32_t kSleepIdle = 512;  // value and producer warps
 
 // Byte offsets of the 16-byte chunks of row t in a stage array written with
 // the XOR-128B swizzle (chunk k of the array -> line k/8, slot (k%8)^(line%8)),
@@ -436,6 +428,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     auto pfree_bar = [&](int k) { return mb0 + 8u * (14 + k); };        // count 1 (commit)
     auto vready_bar = [&](int v) { return mb0 + 8u * (16 + v); };       // count 4 (value warps)
     auto vfree_bar = [&](int v) { return mb0 + 8u * (18 + v); };        // count 1 (commit)
+    auto sfree_bar = [&](int k) { return mb0 + 8u * (20 + k); };        // count 4 (softmax warps read S)
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(misc + 176);
     int* flags = reinterpret_cast<int*>(misc + 192);    // [4]
     float* red = reinterpret_cast<float*>(misc + 256);  // [4][16]
@@ -502,6 +495,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             mbar_init(vready_bar(v), kValWarps);
             mbar_init(vfree_bar(v), 1);
         }
+#pragma unroll
+        for (int k = 0; k < 2; ++k) mbar_init(sfree_bar(k), kSmWarps);
         asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
     }
     {
@@ -579,7 +574,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 ipf = advance(ipf + 1);
             }
             const int s = j % ST;
-            if (j >= ST) mbar_wait<kSleepIdle>(empty_bar(s), ((j / ST) - 1) & 1, dead);
+            if (j >= ST) mbar_wait(empty_bar(s), ((j / ST) - 1) & 1, dead);
             const int p0 = p_lo + i * kTcTile;
             char* st = ring + s * C::STAGE_BYTES;
             const int rows_valid = min(kTcTile, p_hi - p0);
@@ -633,13 +628,11 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         }
         cp_async_wait<0>();
     } else if (warp == kMmaWarp) {
-        // ================= MMA issuer =================
-        // The warp runs converged (descriptors stay in uniform registers) and
-        // one elected lane issues; every descriptor is a base plus a constant
-        // 16-byte-unit offset in its start-address field.
+        // ================= S MMA issuer =================
+        // The MMA warps run converged (descriptors stay in uniform registers)
+        // and one elected lane issues; every descriptor is a base plus a
+        // constant 16-byte-unit offset in its start-address field.
         const uint64_t qbase = smem_desc(sQ_u, 16, 1024, kSw128);
-        const uint64_t vbase = smem_desc(sV_u, C::V_LBO, 1024, kSw128);
-        const uint64_t pbase = smem_desc(sP_u, C::P_BYTES, 256, kSw32);
         auto issue_qk = [&](int j) {  // keys of tile j are in TMEM
             const int kbuf = j & 1;
             tc_fence_after();
@@ -656,57 +649,44 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         };
         int n = 0;
         for (int i = advance(0); i < ntiles; i = advance(i + 1)) ++n;
-        // Event-driven: issue the S MMA of tile jq or the P V MMA of tile jp,
-        // whichever operands are ready first.  S has two TMEM buffers, so the
-        // S MMA of tile jq waits until the softmax of tile jq - 2 is done
-        // (its P V MMA issued: jq <= jp + 1).
-        int jq = 0, jp = 0;
-        uint64_t t_idle = 0;
-        uint32_t idle = 0;
-        while (jp < n && !dead) {
-            bool progress = false;
-            if (jq < n && jq <= jp + 1 &&
-                __shfl_sync(0xffffffffu, (int)mbar_test(kready_bar(jq & 1), (jq >> 1) & 1), 0)) {
-                issue_qk(jq);
-                ++jq;
-                progress = true;
-            }
-            if (jp < jq && __shfl_sync(0xffffffffu, (int)(mbar_test(pready_bar(jp % PB), (jp / PB) & 1) &&
-                                                          mbar_test(vready_bar(jp % VB), (jp / VB) & 1)), 0)) {
-                const int vbuf = jp % VB, pbuf = jp % PB;
-                tc_fence_after();
-                if (elect_one()) {
-                    const uint64_t vb0 = vbase + (uint64_t)((vbuf * C::V_BYTES) >> 4);
-                    const uint64_t pb0 = pbase + (uint64_t)((pbuf * C::P_BUF) >> 4);
+        // S MMA of tile j once its keys are in TMEM and the softmax warps have
+        // read S buffer j & 1 (tile j - 2)
+        for (int j = 0; j < n && !dead; ++j) {
+            mbar_wait(kready_bar(j & 1), (j >> 1) & 1, dead);
+            if (j >= 2) mbar_wait(sfree_bar(j & 1), ((j - 2) >> 1) & 1, dead);
+            if (dead) break;
+            issue_qk(j);
+        }
+    } else if (warp == kPvWarp) {
+        // ================= P V MMA issuer =================
+        const uint64_t vbase = smem_desc(sV_u, C::V_LBO, 1024, kSw128);
+        const uint64_t pbase = smem_desc(sP_u, C::P_BYTES, 256, kSw32);
+        int n = 0;
+        for (int i = advance(0); i < ntiles; i = advance(i + 1)) ++n;
+        for (int jp = 0; jp < n && !dead; ++jp) {
+            mbar_wait(pready_bar(jp % PB), (jp / PB) & 1, dead);
+            mbar_wait(vready_bar(jp % VB), (jp / VB) & 1, dead);
+            if (dead) break;
+            const int vbuf = jp % VB, pbuf = jp % PB;
+            tc_fence_after();
+            if (elect_one()) {
+                const uint64_t vb0 = vbase + (uint64_t)((vbuf * C::V_BYTES) >> 4);
+                const uint64_t pb0 = pbase + (uint64_t)((pbuf * C::P_BUF) >> 4);
 #pragma unroll
-                    for (int mb = 0; mb < C::MB; ++mb) {
+                for (int mb = 0; mb < C::MB; ++mb) {
 #pragma unroll
-                        for (int ks_ = 0; ks_ < kTcTile / 16; ++ks_) {
-                            const uint64_t vd = vb0 + (uint64_t)(((2 * mb) * C::V_LBO + (2 * ks_) * 1024) >> 4);
-                            const uint64_t pd = pb0 + (uint64_t)((ks_ * 512) >> 4);
-                            mma_ss(tbase + kTmemO + mb * 16, vd, pd, IDESC_PV, (jp > 0 || ks_ > 0) ? 1u : 0u);
-                            if constexpr (Ops<T>::kSplitP)
-                                mma_ss(tbase + kTmemO + mb * 16, vd, pd + (uint64_t)(C::P_BYTES >> 4), IDESC_PV, 1u);
-                        }
+                    for (int ks_ = 0; ks_ < kTcTile / 16; ++ks_) {
+                        const uint64_t vd = vb0 + (uint64_t)(((2 * mb) * C::V_LBO + (2 * ks_) * 1024) >> 4);
+                        const uint64_t pd = pb0 + (uint64_t)((ks_ * 512) >> 4);
+                        mma_ss(tbase + kTmemO + mb * 16, vd, pd, IDESC_PV, (jp > 0 || ks_ > 0) ? 1u : 0u);
+                        if constexpr (Ops<T>::kSplitP)
+                            mma_ss(tbase + kTmemO + mb * 16, vd, pd + (uint64_t)(C::P_BYTES >> 4), IDESC_PV, 1u);
                     }
-                    mma_commit(pfree_bar(pbuf));
-                    mma_commit(vfree_bar(vbuf));
                 }
-                __syncwarp();
-                ++jp;
-                progress = true;
+                mma_commit(pfree_bar(pbuf));
+                mma_commit(vfree_bar(vbuf));
             }
-            if (progress) {
-                idle = 0;
-            } else {
-                // nothing ready: sleep briefly; give up after about a second
-                if (idle == 0) t_idle = global_ns();
-                __nanosleep(32);
-                if ((++idle & 255) == 0 && global_ns() - t_idle > kWaitNs) {
-                    atomicOr(&g_device_status, 1u);
-                    dead = true;
-                }
-            }
+            __syncwarp();
         }
     } else if (warp < kKeyWarps) {
         // ================= key warps: K -> TMEM =================
@@ -715,7 +695,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         // dequantise the j-th active tile into K buffer j & 1 of TMEM lane t
         auto load_keys = [&](int j) {
             const int s = j % ST;
-            mbar_wait<kSleepCrit>(full_bar(s), (j / ST) & 1, dead);
+            mbar_wait(full_bar(s), (j / ST) & 1, dead);
             const char* st = ring + s * C::STAGE_BYTES;
             const char* s_sc = st + 2 * C::PACK_BYTES + t * C::SROWB;
             constexpr int CPS = 32 / PPC;  // chunks per 32-column store
@@ -745,7 +725,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         for (int i = advance(0); i < ntiles; i = advance(i + 1)) ++n;
         for (int j = 0; j < n; ++j) {
             // K buffer j & 1 was last read by the S MMA of tile j - 2
-            if (j >= 2) mbar_wait<kSleepCrit>(sready_bar(j & 1), ((j - 2) >> 1) & 1, dead);
+            if (j >= 2) mbar_wait(sready_bar(j & 1), ((j - 2) >> 1) & 1, dead);
             load_keys(j);
         }
     } else if (warp >= kSmWarp0) {
@@ -756,13 +736,16 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         const int hq0 = kvh * a.gqa + h0;
         int js = 0;
         for (int i = advance(0); i < ntiles; i = advance(i + 1), ++js) {
-            mbar_wait<kSleepCrit>(sready_bar(js & 1), (js >> 1) & 1, dead);
+            mbar_wait(sready_bar(js & 1), (js >> 1) & 1, dead);
             tc_fence_after();
             float s[kTcHeads];
             tmem_ld16(tbase + lane_off + kTmemS + 16 * (js & 1), s);
             tmem_wait_ld();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(sfree_bar(js & 1));  // S buffer js & 1 is read
             if (js >= PB) {  // P^T buffer js % PB was read by the P V MMA of tile js - PB
-                mbar_wait<kSleepCrit>(pfree_bar(js % PB), ((js - PB) / PB) & 1, dead);
+                mbar_wait(pfree_bar(js % PB), ((js - PB) / PB) & 1, dead);
                 tc_fence_after();
             }
 
@@ -812,7 +795,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 named_barrier(1, kSmWarps * 32);  // red read before it is written again
                 if (js > 0) {
                     // O^T must hold the P V product of tile js - 1 before it is scaled
-                    mbar_wait<kSleepCrit>(pfree_bar((js - 1) % PB), ((js - 1) / PB) & 1, dead);
+                    mbar_wait(pfree_bar((js - 1) % PB), ((js - 1) / PB) & 1, dead);
                     tc_fence_after();
                     // O^T lane t holds head dims t (+128): scale column h by alpha[h]
 #pragma unroll
@@ -861,7 +844,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         }
         n_active = js;
         if (n_active > 0) {  // the last P V product
-            mbar_wait<kSleepCrit>(pfree_bar((n_active - 1) % PB), ((n_active - 1) / PB) & 1, dead);
+            mbar_wait(pfree_bar((n_active - 1) % PB), ((n_active - 1) / PB) & 1, dead);
             tc_fence_after();
         }
     } else {
@@ -871,10 +854,10 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         for (int i = advance(0); i < ntiles; i = advance(i + 1), ++j) {
             const int s = j % ST;
             const int vbuf = j % VB;
-            mbar_wait<kSleepIdle>(full_bar(s), (j / ST) & 1, dead);
+            mbar_wait(full_bar(s), (j / ST) & 1, dead);
             const char* st = ring + s * C::STAGE_BYTES;
             const char* s_vsc = st + 2 * C::PACK_BYTES + 2 * C::SC_BYTES + t * C::SROWB;
-            if (j >= VB) mbar_wait<kSleepIdle>(vfree_bar(vbuf), ((j / VB) - 1) & 1, dead);
+            if (j >= VB) mbar_wait(vfree_bar(vbuf), ((j / VB) - 1) & 1, dead);
             // token t's row of each 1024-byte atom (8 tokens x 64 dims) of 64-dim
             // block w8/8; 16-byte slot (w8 % 8) ^ (t % 8)
             char* vrow = sV + vbuf * C::V_BYTES + (t >> 3) * 1024 + (t & 7) * 128;
