@@ -78,9 +78,6 @@ constexpr int kTmemK = 64;      // K operand: two buffers of D/2 columns
 constexpr float kRescaleTc = 8.f;
 constexpr unsigned long long kWaitNs = 1000000000ull;
 constexpr int kSmemLimit = 227 * 1024;
-// tiles the producer asks L2 for ahead of its cp.async stream (0 = none;
-// measured: the extra L2 traffic costs more than the latency it hides)
-constexpr int kPrefetchTiles = 0;
 
 template <int BITS, int D, int GS, bool SPLITP>
 struct TcCfg {
@@ -234,10 +231,6 @@ __device__ __forceinline__ void mbar_init(uint32_t addr, int count) {
 }
 __device__ __forceinline__ void mbar_arrive(uint32_t addr) {
     asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];\n" ::"r"(addr) : "memory");
-}
-// bulk prefetch of [p, p + bytes) into L2 (16-byte aligned address and size)
-__device__ __forceinline__ void prefetch_l2(const void* p, uint32_t bytes) {
-    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;\n" ::"l"(p), "r"(bytes) : "memory");
 }
 __device__ __forceinline__ void mbar_expect_tx(uint32_t addr, uint32_t bytes) {
     asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;\n" ::"r"(addr), "r"(bytes) : "memory");
@@ -429,7 +422,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     auto vready_bar = [&](int v) { return mb0 + 8u * (16 + v); };       // count 4 (value warps)
     auto vfree_bar = [&](int v) { return mb0 + 8u * (18 + v); };        // count 1 (commit)
     auto sfree_bar = [&](int k) { return mb0 + 8u * (20 + k); };        // count 4 (softmax warps read S)
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(misc + 176);
+    const uint32_t qready_bar = mb0 + 8u * 22;                          // count 4 (softmax warps staged Q)
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(misc + 184);
     int* flags = reinterpret_cast<int*>(misc + 192);    // [4]
     float* red = reinterpret_cast<float*>(misc + 256);  // [4][16]
     const uint32_t sV_u = smem_u32(sV), sQ_u = smem_u32(sQ), sP_u = smem_u32(sP);
@@ -469,69 +463,95 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     const char* vb = has_bias ? static_cast<const char*>(a.vb) + ((int64_t)b * a.vb_sb + (int64_t)kvh * a.vb_sh) * 2
                               : nullptr;
 
-    // ---- prologue: TMEM, barriers, Q operand ----
+    // ---- producer: one ring stage = packed K and V rows of a tile (TMA, or
+    // 16-byte cp.async for 64-byte rows) + its scale / bias rows ----
+    auto issue_stage = [&](int j, int i) {
+        const int s = j % ST;
+        const int p0 = p_lo + i * kTcTile;
+        char* st = ring + s * C::STAGE_BYTES;
+        const int rows_valid = min(kTcTile, p_hi - p0);
+        if constexpr (C::TMA_ROWS) {
+            // rows past N arrive zero-filled; rows of the next chunk are masked later
+            if (lane == 0) {
+                mbar_expect_tx(full_bar(s), 2 * C::PACK_BYTES);
+                tma_rows<C::ROWB>(smem_u32(st), &tm_k, p0, kvh, b, full_bar(s));
+                tma_rows<C::ROWB>(smem_u32(st + C::PACK_BYTES), &tm_v, p0, kvh, b, full_bar(s));
+            }
+        } else {
+            const char* ksrc = kp_b + (int64_t)p0 * C::ROWB + lane * 16;
+            const char* vsrc = vp_b + (int64_t)p0 * C::ROWB + lane * 16;
+            // chunk k = lane + 32m of the stage (row k / CPR): source k*16, swizzled
+            // destination line k/8 = lane/8 + 4m, whose parity alternates with m
+            const uint32_t d_even = (uint32_t)swz<8>(lane >> 3, lane & 7) * 16u;
+            const uint32_t d_odd = (uint32_t)swz<8>((lane >> 3) + 4, lane & 7) * 16u - 512u;
+            constexpr int M = kTcTile * C::CPR / 32;
+            if (rows_valid == kTcTile) {
+#pragma unroll 4
+                for (int m = 0; m < M; ++m) {
+                    const uint32_t dst = (m & 1 ? d_odd : d_even) + m * 512u;
+                    cp_async16(st + dst, ksrc + m * 512, 16);
+                    cp_async16(st + C::PACK_BYTES + dst, vsrc + m * 512, 16);
+                }
+            } else {
+                const int kvalid = rows_valid * C::CPR;
+#pragma unroll 4
+                for (int m = 0; m < M; ++m) {
+                    const uint32_t dst = (m & 1 ? d_odd : d_even) + m * 512u;
+                    const bool ok = lane + 32 * m < kvalid;
+                    cp_async16(st + dst, ok ? ksrc + m * 512 : kp_b, ok ? 16 : 0);
+                    cp_async16(st + C::PACK_BYTES + dst, ok ? vsrc + m * 512 : vp_b, ok ? 16 : 0);
+                }
+            }
+        }
+        const int sbytes = rows_valid * C::SROWB;
+        char* s0 = st + 2 * C::PACK_BYTES;
+        for (int k = lane; k < C::SC_CHUNKS; k += 32) {
+            const int off = k * 16;
+            const int nb = max(0, min(16, sbytes - off));
+            const int64_t goff = (int64_t)p0 * C::SROWB + (nb > 0 ? off : 0);
+            cp_async16(s0 + off, ks + goff, nb);
+            cp_async16(s0 + 2 * C::SC_BYTES + off, vs + goff, nb);
+            if (has_bias) {
+                cp_async16(s0 + C::SC_BYTES + off, kb + goff, nb);
+                cp_async16(s0 + 3 * C::SC_BYTES + off, vb + goff, nb);
+            }
+        }
+        cp_async_mbar_arrive(full_bar(s));
+    };
+    int prod_j = 0, prod_i = advance(0);  // producer: next stage and its tile
+
+    // ---- prologue: barriers (initialised by the producer warp, which then
+    // requests the first stages at once) and TMEM; the softmax warps stage Q
+    // after it ----
+    if (warp == kProdWarp) {
+        if (lane == 0) {
+#pragma unroll
+            for (int s = 0; s < ST; ++s) {
+                mbar_init(full_bar(s), 32 + (C::TMA_ROWS ? 1 : 0));
+                mbar_init(empty_bar(s), kKeyWarps + kValWarps);
+            }
+#pragma unroll
+            for (int k = 0; k < 2; ++k) {
+                mbar_init(kready_bar(k), kKeyWarps);
+                mbar_init(sready_bar(k), 1);
+                mbar_init(pready_bar(k), kSmWarps);
+                mbar_init(pfree_bar(k), 1);
+                mbar_init(sfree_bar(k), kSmWarps);
+            }
+#pragma unroll
+            for (int v = 0; v < VB; ++v) {
+                mbar_init(vready_bar(v), kValWarps);
+                mbar_init(vfree_bar(v), 1);
+            }
+            mbar_init(qready_bar, kSmWarps);
+            asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
+        }
+        __syncwarp();
+        for (; prod_j < ST && prod_i < ntiles; prod_i = advance(prod_i + 1), ++prod_j) issue_stage(prod_j, prod_i);
+    }
     if (warp == kMmaWarp) {
         tmem_alloc(smem_u32(tmem_slot), kTmemCols);
         tmem_relinquish();
-    }
-    if (tid == 0) {
-#pragma unroll
-        for (int s = 0; s < ST; ++s) {
-            mbar_init(full_bar(s), 32 + (C::TMA_ROWS ? 1 : 0));
-            mbar_init(empty_bar(s), kKeyWarps + kValWarps);
-        }
-#pragma unroll
-        for (int k = 0; k < 2; ++k) {
-            mbar_init(kready_bar(k), kKeyWarps);
-            mbar_init(sready_bar(k), 1);
-        }
-#pragma unroll
-        for (int k = 0; k < 2; ++k) {
-            mbar_init(pready_bar(k), kSmWarps);
-            mbar_init(pfree_bar(k), 1);
-        }
-#pragma unroll
-        for (int v = 0; v < VB; ++v) {
-            mbar_init(vready_bar(v), kValWarps);
-            mbar_init(vfree_bar(v), 1);
-        }
-#pragma unroll
-        for (int k = 0; k < 2; ++k) mbar_init(sfree_bar(k), kSmWarps);
-        asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
-    }
-    {
-        // Q rows h0.. of this KV head, K-major with the 128-byte swizzle:
-        // 64-dim block kb at kb*2048, heads 8g.. at +g*1024, row h at +(h%8)*128
-        const T* q = static_cast<const T*>(a.q) + (int64_t)b * a.q_sb + (int64_t)(kvh * a.gqa + h0) * a.q_sh;
-        const bool q_vec = ((uintptr_t)q % 16 == 0) && ((a.q_sh * 2) % 16 == 0);
-        constexpr int CH = kTcHeads * D / 8;  // 16-byte chunks
-        for (int i = tid; i < CH; i += kTcThreads) {
-            const int h = i / (D / 8), w = i - h * (D / 8);  // chunk w = dims 8w..8w+7
-            uint32_t s[4] = {0u, 0u, 0u, 0u};
-            if (h < nh) {
-                const T* src = q + (int64_t)h * a.q_sh + w * 8;
-                if (q_vec) {
-                    const uint4 v = *reinterpret_cast<const uint4*>(src);
-                    s[0] = v.x, s[1] = v.y, s[2] = v.z, s[3] = v.w;
-                } else {
-                    const uint16_t* s16 = reinterpret_cast<const uint16_t*>(src);
-#pragma unroll
-                    for (int e = 0; e < 4; ++e) s[e] = (uint32_t)s16[2 * e] | ((uint32_t)s16[2 * e + 1] << 16);
-                }
-            }
-            uint4 d;
-            if constexpr (BITS == 4) {  // positions 0..7 <- dims 0,4,1,5,2,6,3,7
-                d.x = __byte_perm(s[0], s[2], 0x5410);
-                d.y = __byte_perm(s[0], s[2], 0x7632);
-                d.z = __byte_perm(s[1], s[3], 0x5410);
-                d.w = __byte_perm(s[1], s[3], 0x7632);
-            } else {
-                d = make_uint4(s[0], s[1], s[2], s[3]);
-            }
-            const int kblk = w >> 3, c = w & 7;
-            *reinterpret_cast<uint4*>(sQ + kblk * 2048 + (h >> 3) * 1024 + (h & 7) * 128 + ((c ^ (h & 7)) * 16)) = d;
-        }
-        fence_proxy_async();
     }
     tc_fence_before();
     __syncthreads();
@@ -545,86 +565,10 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     int n_active = 0;
 
     if (warp == kProdWarp) {
-        // ================= producer: ring stages with 16-byte cp.async =================
-        // lane 0 keeps bulk L2 prefetches kPrefetchTiles active tiles ahead
-        auto prefetch = [&](int i) {
-            const int p0 = p_lo + i * kTcTile;
-            const int rows = min(kTcTile, p_hi - p0);
-            const uint32_t pb = (uint32_t)(rows * C::ROWB);
-            const uint32_t sb = (uint32_t)(rows * C::SROWB) & ~15u;
-            prefetch_l2(kp_b + (int64_t)p0 * C::ROWB, pb);
-            prefetch_l2(vp_b + (int64_t)p0 * C::ROWB, pb);
-            if (sb) {
-                prefetch_l2(ks + (int64_t)p0 * C::SROWB, sb);
-                prefetch_l2(vs + (int64_t)p0 * C::SROWB, sb);
-                if (has_bias) {
-                    prefetch_l2(kb + (int64_t)p0 * C::SROWB, sb);
-                    prefetch_l2(vb + (int64_t)p0 * C::SROWB, sb);
-                }
-            }
-        };
-        int ipf = advance(0);
-        if (kPrefetchTiles > 0 && lane == 0) {
-            for (int k = 0; k < kPrefetchTiles && ipf < ntiles; ++k, ipf = advance(ipf + 1)) prefetch(ipf);
-        }
-        int j = 0;
-        for (int i = advance(0); i < ntiles; i = advance(i + 1), ++j) {
-            if (kPrefetchTiles > 0 && lane == 0 && ipf < ntiles) {
-                prefetch(ipf);
-                ipf = advance(ipf + 1);
-            }
-            const int s = j % ST;
-            if (j >= ST) mbar_wait(empty_bar(s), ((j / ST) - 1) & 1, dead);
-            const int p0 = p_lo + i * kTcTile;
-            char* st = ring + s * C::STAGE_BYTES;
-            const int rows_valid = min(kTcTile, p_hi - p0);
-            if constexpr (C::TMA_ROWS) {
-                // rows past N arrive zero-filled; rows of the next chunk are masked later
-                if (lane == 0) {
-                    mbar_expect_tx(full_bar(s), 2 * C::PACK_BYTES);
-                    tma_rows<C::ROWB>(smem_u32(st), &tm_k, p0, kvh, b, full_bar(s));
-                    tma_rows<C::ROWB>(smem_u32(st + C::PACK_BYTES), &tm_v, p0, kvh, b, full_bar(s));
-                }
-            } else {
-                const char* ksrc = kp_b + (int64_t)p0 * C::ROWB + lane * 16;
-                const char* vsrc = vp_b + (int64_t)p0 * C::ROWB + lane * 16;
-                // chunk k = lane + 32m of the stage (row k / CPR): source k*16, swizzled
-                // destination line k/8 = lane/8 + 4m, whose parity alternates with m
-                const uint32_t d_even = (uint32_t)swz<8>(lane >> 3, lane & 7) * 16u;
-                const uint32_t d_odd = (uint32_t)swz<8>((lane >> 3) + 4, lane & 7) * 16u - 512u;
-                constexpr int M = kTcTile * C::CPR / 32;
-                if (rows_valid == kTcTile) {
-#pragma unroll 4
-                    for (int m = 0; m < M; ++m) {
-                        const uint32_t dst = (m & 1 ? d_odd : d_even) + m * 512u;
-                        cp_async16(st + dst, ksrc + m * 512, 16);
-                        cp_async16(st + C::PACK_BYTES + dst, vsrc + m * 512, 16);
-                    }
-                } else {
-                    const int kvalid = rows_valid * C::CPR;
-#pragma unroll 4
-                    for (int m = 0; m < M; ++m) {
-                        const uint32_t dst = (m & 1 ? d_odd : d_even) + m * 512u;
-                        const bool ok = lane + 32 * m < kvalid;
-                        cp_async16(st + dst, ok ? ksrc + m * 512 : kp_b, ok ? 16 : 0);
-                        cp_async16(st + C::PACK_BYTES + dst, ok ? vsrc + m * 512 : vp_b, ok ? 16 : 0);
-                    }
-                }
-            }
-            const int sbytes = rows_valid * C::SROWB;
-            char* s0 = st + 2 * C::PACK_BYTES;
-            for (int k = lane; k < C::SC_CHUNKS; k += 32) {
-                const int off = k * 16;
-                const int n = max(0, min(16, sbytes - off));
-                const int64_t goff = (int64_t)p0 * C::SROWB + (n > 0 ? off : 0);
-                cp_async16(s0 + off, ks + goff, n);
-                cp_async16(s0 + 2 * C::SC_BYTES + off, vs + goff, n);
-                if (has_bias) {
-                    cp_async16(s0 + C::SC_BYTES + off, kb + goff, n);
-                    cp_async16(s0 + 3 * C::SC_BYTES + off, vb + goff, n);
-                }
-            }
-            cp_async_mbar_arrive(full_bar(s));
+        // ================= producer: the remaining stages =================
+        for (; prod_i < ntiles && !dead; prod_i = advance(prod_i + 1), ++prod_j) {
+            mbar_wait(empty_bar(prod_j % ST), ((prod_j / ST) - 1) & 1, dead);
+            issue_stage(prod_j, prod_i);
         }
         cp_async_wait<0>();
     } else if (warp == kMmaWarp) {
@@ -651,6 +595,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         for (int i = advance(0); i < ntiles; i = advance(i + 1)) ++n;
         // S MMA of tile j once its keys are in TMEM and the softmax warps have
         // read S buffer j & 1 (tile j - 2)
+        mbar_wait(qready_bar, 0, dead);  // the Q operand is staged
         for (int j = 0; j < n && !dead; ++j) {
             mbar_wait(kready_bar(j & 1), (j >> 1) & 1, dead);
             if (j >= 2) mbar_wait(sfree_bar(j & 1), ((j - 2) >> 1) & 1, dead);
@@ -730,6 +675,43 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         }
     } else if (warp >= kSmWarp0) {
         // ================= softmax warps: S^T -> P^T =================
+        {
+            // the Q operand: rows h0.. of this KV head, K-major with the
+            // 128-byte swizzle: 64-dim block kb at kb*2048, heads 8g.. at
+            // +g*1024, row h at +(h%8)*128
+            const T* q = static_cast<const T*>(a.q) + (int64_t)b * a.q_sb + (int64_t)(kvh * a.gqa + h0) * a.q_sh;
+            const bool q_vec = ((uintptr_t)q % 16 == 0) && ((a.q_sh * 2) % 16 == 0);
+            constexpr int CH = kTcHeads * D / 8;  // 16-byte chunks
+            for (int i = tid - kSmWarp0 * 32; i < CH; i += kSmWarps * 32) {
+                const int h = i / (D / 8), w = i - h * (D / 8);  // chunk w = dims 8w..8w+7
+                uint32_t s[4] = {0u, 0u, 0u, 0u};
+                if (h < nh) {
+                    const T* src = q + (int64_t)h * a.q_sh + w * 8;
+                    if (q_vec) {
+                        const uint4 v = *reinterpret_cast<const uint4*>(src);
+                        s[0] = v.x, s[1] = v.y, s[2] = v.z, s[3] = v.w;
+                    } else {
+                        const uint16_t* s16 = reinterpret_cast<const uint16_t*>(src);
+#pragma unroll
+                        for (int e = 0; e < 4; ++e) s[e] = (uint32_t)s16[2 * e] | ((uint32_t)s16[2 * e + 1] << 16);
+                    }
+                }
+                uint4 d;
+                if constexpr (BITS == 4) {  // positions 0..7 <- dims 0,4,1,5,2,6,3,7
+                    d.x = __byte_perm(s[0], s[2], 0x5410);
+                    d.y = __byte_perm(s[0], s[2], 0x7632);
+                    d.z = __byte_perm(s[1], s[3], 0x5410);
+                    d.w = __byte_perm(s[1], s[3], 0x7632);
+                } else {
+                    d = make_uint4(s[0], s[1], s[2], s[3]);
+                }
+                const int kblk = w >> 3, c = w & 7;
+                *reinterpret_cast<uint4*>(sQ + kblk * 2048 + (h >> 3) * 1024 + (h & 7) * 128 + ((c ^ (h & 7)) * 16)) = d;
+            }
+            fence_proxy_async();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(qready_bar);
+        }
         const int qw = warp & 3;  // TMEM lane quadrant: tokens 32qw..32qw+31 of the tile
         const uint32_t lane_off = (uint32_t)(qw * 32) << 16;
         const int64_t mrow = a.mask ? (int64_t)b * a.m_sb : 0;
