@@ -78,6 +78,9 @@ constexpr int kTmemK = 64;      // K operand: two buffers of D/2 columns
 constexpr float kRescaleTc = 8.f;
 constexpr unsigned long long kWaitNs = 1000000000ull;
 constexpr int kSmemLimit = 227 * 1024;
+#ifndef QSDPA_TC_VREG
+#define QSDPA_TC_VREG 1
+#endif
 
 template <int BITS, int D, int GS, bool SPLITP>
 struct TcCfg {
@@ -116,6 +119,10 @@ struct TcCfg {
     // box of 128-byte rows is exactly the ring's chunk swizzle); 64-byte rows by
     // the producer lanes' cp.async
     static constexpr bool TMA_ROWS = ROWB == 128 || ROWB == 256;
+    // value rows of up to 128 bytes are copied to registers and the stage
+    // released before they are dequantised (the key warps finish a stage
+    // first, so the value warps decide when the producer may refill it)
+    static constexpr bool VAL_REGS = QSDPA_TC_VREG && CPR <= 8;
     static_assert(STAGES >= 2, "two ring stages must fit");
     static_assert(STAGES * STAGE_BYTES >= kTcHeads * D * 4 + 2 * kTcHeads * 4, "merge area must fit in the ring");
     static_assert(SC_BYTES % 16 == 0 && CPR >= 2, "copy plan");
@@ -839,28 +846,57 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             mbar_wait(full_bar(s), (j / ST) & 1, dead);
             const char* st = ring + s * C::STAGE_BYTES;
             const char* s_vsc = st + 2 * C::PACK_BYTES + 2 * C::SC_BYTES + t * C::SROWB;
-            if (j >= VB) mbar_wait(vfree_bar(vbuf), ((j / VB) - 1) & 1, dead);
             // token t's row of each 1024-byte atom (8 tokens x 64 dims) of 64-dim
             // block w8/8; 16-byte slot (w8 % 8) ^ (t % 8)
             char* vrow = sV + vbuf * C::V_BYTES + (t >> 3) * 1024 + (t & 7) * 128;
             const uint32_t vx = (uint32_t)(t & 7) << 4;
-#pragma unroll 2
-            for (int c = 0; c < C::CPR; ++c) {
-                const int g = (c * EPC) / GS;
-                const uint32_t s2 = pair_at(s_vsc + g * 2);
-                const uint32_t b2 = has_bias ? pair_at(s_vsc + C::SC_BYTES + g * 2) : 0u;
-                uint32_t o[PPC];
-                dequant_chunk<T, BITS>(lds128(st + C::PACK_BYTES + rows.off(c)), s2, b2, o);
-                // every 4 pairs are 8 consecutive head dims: one 16-byte store
+            // every 4 pairs are 8 consecutive head dims: one 16-byte store
+            auto store_chunk = [&](int c, const uint32_t* o) {
 #pragma unroll
                 for (int e = 0; e < PPC / 4; ++e) {
                     const int w8 = c * (PPC / 4) + e;  // 8-dim block index
                     *reinterpret_cast<uint4*>(vrow + (w8 >> 3) * C::V_LBO + (((uint32_t)(w8 & 7) << 4) ^ vx)) =
                         make_uint4(o[4 * e], o[4 * e + 1], o[4 * e + 2], o[4 * e + 3]);
                 }
+            };
+            if constexpr (C::VAL_REGS) {
+                // the row and its scale / bias pairs into registers and the stage
+                // released before the wait for the V^T buffer: the producer
+                // refills it while this tile is dequantised
+                uint4 w[C::CPR];
+#pragma unroll
+                for (int c = 0; c < C::CPR; ++c) w[c] = lds128(st + C::PACK_BYTES + rows.off(c));
+                uint32_t sc2[C::G], bi2[C::G];
+                load_pairs<C::G>(s_vsc, sc2);
+                if (has_bias) {
+                    load_pairs<C::G>(s_vsc + C::SC_BYTES, bi2);
+                } else {
+#pragma unroll
+                    for (int g = 0; g < C::G; ++g) bi2[g] = 0u;
+                }
+                __syncwarp();
+                if (lane == 0) mbar_arrive(empty_bar(s));
+                if (j >= VB) mbar_wait(vfree_bar(vbuf), ((j / VB) - 1) & 1, dead);
+#pragma unroll
+                for (int c = 0; c < C::CPR; ++c) {
+                    uint32_t o[PPC];
+                    dequant_chunk<T, BITS>(w[c], sc2[(c * EPC) / GS], bi2[(c * EPC) / GS], o);
+                    store_chunk(c, o);
+                }
+            } else {
+                if (j >= VB) mbar_wait(vfree_bar(vbuf), ((j / VB) - 1) & 1, dead);
+#pragma unroll 2
+                for (int c = 0; c < C::CPR; ++c) {
+                    const int g = (c * EPC) / GS;
+                    const uint32_t s2 = pair_at(s_vsc + g * 2);
+                    const uint32_t b2 = has_bias ? pair_at(s_vsc + C::SC_BYTES + g * 2) : 0u;
+                    uint32_t o[PPC];
+                    dequant_chunk<T, BITS>(lds128(st + C::PACK_BYTES + rows.off(c)), s2, b2, o);
+                    store_chunk(c, o);
+                }
+                __syncwarp();
+                if (lane == 0) mbar_arrive(empty_bar(s));
             }
-            __syncwarp();
-            if (lane == 0) mbar_arrive(empty_bar(s));
             fence_proxy_async();
             __syncwarp();
             if (lane == 0) mbar_arrive(vready_bar(vbuf));
