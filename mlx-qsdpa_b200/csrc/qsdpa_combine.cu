@@ -19,6 +19,8 @@ constexpr int kThreadsC = 256;
 constexpr int kDimQuads = 16;                       // 4-dim groups per CTA: 64 dims
 constexpr int kSplitLanes = kThreadsC / kDimQuads;  // 16 lanes walk the parts
 constexpr int kMaxPartsSmem = 2048;
+constexpr int kPrefetch = 8;  // records per lane loaded before the weights are known
+constexpr int kMlRegs = 2;    // (m, l) pairs per thread held in registers (parts up to 512)
 
 __device__ __forceinline__ float block_reduce(float v, float* scratch, bool is_max) {
 #pragma unroll
@@ -35,10 +37,12 @@ __device__ __forceinline__ float block_reduce(float v, float* scratch, bool is_m
     return v;
 }
 
-// CTA (row, 64-dim slice).  Phase 1: the parts' maxima and weights
-// w_p = 2^(m_p - max) into shared memory, and l = sum w_p l_p.  Phase 2: 16
-// lanes each walk every 16th part with float4 loads (unrolled, so several
-// records are in flight per thread), then a shared-memory reduction.
+// CTA (row, 64-dim slice).  Each of 16 lanes per 4-dim quad walks every 16th
+// part; its first kPrefetch records are loaded up front, so they travel while
+// phase 1 runs.  Phase 1: the parts' maxima and weights w_p = 2^(m_p - max)
+// into shared memory, and l = sum w_p l_p.  Phase 2: the lanes accumulate
+// w_p * o_p (the prefetched records, then the rest with float4 loads unrolled
+// by 4), then a shared-memory reduction.
 template <typename T>
 __global__ void __launch_bounds__(kThreadsC)
     combine_kernel(const float* __restrict__ po, const float* __restrict__ pml, int64_t so, int64_t sml, int64_t ro,
@@ -53,12 +57,38 @@ __global__ void __launch_bounds__(kThreadsC)
     const int row = blockIdx.x;
     const float* ml = pml + (int64_t)row * rml;
     const int tid = threadIdx.x;
+    const int dq = tid % kDimQuads, sl = tid / kDimQuads;
+    const int d = blockIdx.y * (kDimQuads * 4) + dq * 4;
+    const float* o = po + (int64_t)row * ro + d;
+    float4 pre[kPrefetch];
+#pragma unroll
+    for (int u = 0; u < kPrefetch; ++u) {
+        const int p = sl + u * kSplitLanes;
+        pre[u] = d < D && p < parts ? __ldcg(reinterpret_cast<const float4*>(o + (int64_t)p * so))
+                                    : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
 
+    // (m, l) of parts tid, tid + 256, ... : the first kMlRegs kept in registers
+    float mr[kMlRegs], lr[kMlRegs];
     float mt = -INFINITY;
-    for (int p = tid; p < parts; p += kThreadsC) mt = fmaxf(mt, __ldcg(ml + (int64_t)p * sml));
+#pragma unroll
+    for (int u = 0; u < kMlRegs; ++u) {
+        const int p = tid + u * kThreadsC;
+        mr[u] = p < parts ? __ldcg(ml + (int64_t)p * sml) : -INFINITY;
+        lr[u] = p < parts ? __ldcg(ml + (int64_t)p * sml + 1) : 0.f;
+        mt = fmaxf(mt, mr[u]);
+    }
+    for (int p = tid + kMlRegs * kThreadsC; p < parts; p += kThreadsC) mt = fmaxf(mt, __ldcg(ml + (int64_t)p * sml));
     mt = block_reduce(mt, s_scr, true);
     float lt = 0.f;
-    for (int p = tid; p < parts; p += kThreadsC) {
+#pragma unroll
+    for (int u = 0; u < kMlRegs; ++u) {
+        const int p = tid + u * kThreadsC;
+        const float w = mr[u] == -INFINITY ? 0.f : exp2f(mr[u] - mt);
+        if (p < parts) s_w[p] = w;
+        lt += w * lr[u];
+    }
+    for (int p = tid + kMlRegs * kThreadsC; p < parts; p += kThreadsC) {
         const float m = __ldcg(ml + (int64_t)p * sml);
         const float w = m == -INFINITY ? 0.f : exp2f(m - mt);
         s_w[p] = w;
@@ -66,12 +96,18 @@ __global__ void __launch_bounds__(kThreadsC)
     }
     lt = block_reduce(lt, s_scr, false);  // its __syncthreads also publishes s_w
 
-    const int dq = tid % kDimQuads, sl = tid / kDimQuads;
-    const int d = blockIdx.y * (kDimQuads * 4) + dq * 4;
     float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
     if (d < D) {
-        const float* o = po + (int64_t)row * ro + d;
-        int p = sl;
+#pragma unroll
+        for (int u = 0; u < kPrefetch; ++u) {
+            const int p = sl + u * kSplitLanes;
+            const float w = p < parts ? s_w[p] : 0.f;
+            acc.x += w * pre[u].x;
+            acc.y += w * pre[u].y;
+            acc.z += w * pre[u].z;
+            acc.w += w * pre[u].w;
+        }
+        int p = sl + kPrefetch * kSplitLanes;
         for (; p + 3 * kSplitLanes < parts; p += 4 * kSplitLanes) {
             float4 v[4];
 #pragma unroll
