@@ -57,6 +57,51 @@ namespace qsdpa {
 
 __device__ unsigned int g_device_status = 0;
 
+// Optional timelines (builds with -DQSDPA_TC_TRACE only).  Per CTA: global ns
+// at entry, after the prologue and at the end, and the SM (qsdpa_tc_trace_ctas).
+// Per tile of CTA (0, 0, 0): the SM clock at each role's hand-off
+// (qsdpa_tc_trace_tiles; events kEv*).
+enum : int {
+    kEvProd = 0,    // producer: stage of tile j requested
+    kEvKeyGo = 1,   // key warp 0: stage j full
+    kEvKeyEnd = 2,  // key warp 0: keys of tile j in TMEM
+    kEvValGo = 3,   // value warp 4: V^T buffer free, dequantisation starts
+    kEvValEnd = 4,  // value warp 4: V^T of tile j written
+    kEvSmGo = 5,    // softmax warp 8: scores of tile j available
+    kEvSmEnd = 6,   // softmax warp 8: P^T of tile j written
+    kEvMmaS = 7,    // S MMA of tile j issued
+    kEvMmaPV = 8,   // P V MMA of tile j issued
+};
+#ifdef QSDPA_TC_TRACE
+constexpr int kTraceCtas = 1024, kTraceEvents = 9, kTraceTiles = 64;
+__device__ long long g_tc_cta[4][kTraceCtas];
+__device__ long long g_tc_tile[kTraceEvents][kTraceTiles];
+#define TC_TRACE_CTA(ev)                                                                  \
+    do {                                                                                  \
+        const int cta_ = blockIdx.x + gridDim.x * (blockIdx.y + gridDim.y * blockIdx.z);  \
+        if (threadIdx.x == 0 && cta_ < kTraceCtas) {                                      \
+            long long t_;                                                                 \
+            asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t_));                       \
+            g_tc_cta[(ev)][cta_] = t_;                                                    \
+            unsigned sm_;                                                                 \
+            asm volatile("mov.u32 %0, %%smid;" : "=r"(sm_));                              \
+            g_tc_cta[3][cta_] = sm_;                                                      \
+        }                                                                                 \
+    } while (0)
+#define TC_TRACE(ev, j)                                                                                 \
+    do {                                                                                                \
+        if ((threadIdx.x & 31) == 0 && blockIdx.x + blockIdx.y + blockIdx.z == 0 && (j) < kTraceTiles) \
+            g_tc_tile[(ev)][(j)] = clock64();                                                           \
+    } while (0)
+#else
+#define TC_TRACE_CTA(ev) \
+    do {                 \
+    } while (0)
+#define TC_TRACE(ev, j) \
+    do {                \
+    } while (0)
+#endif
+
 namespace {
 
 using namespace dev;
@@ -409,6 +454,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     constexpr int VB = C::VBUFS;
     constexpr int PB = C::PBUFS;
 
+    TC_TRACE_CTA(0);
     extern __shared__ __align__(1024) char smem_raw[];
     // 1024-byte alignment of the swizzled operands (in the shared window)
     const uint32_t raw_u32 = smem_u32(smem_raw);
@@ -473,6 +519,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     // ---- producer: one ring stage = packed K and V rows of a tile (TMA, or
     // 16-byte cp.async for 64-byte rows) + its scale / bias rows ----
     auto issue_stage = [&](int j, int i) {
+        TC_TRACE(kEvProd, j);
         const int s = j % ST;
         const int p0 = p_lo + i * kTcTile;
         char* st = ring + s * C::STAGE_BYTES;
@@ -565,6 +612,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     tc_fence_after();
     const uint32_t tbase = *tmem_slot;
     bool dead = false;
+    TC_TRACE_CTA(1);
 
     float m_run[kTcHeads], l_run[kTcHeads];
 #pragma unroll
@@ -608,6 +656,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             if (j >= 2) mbar_wait(sfree_bar(j & 1), ((j - 2) >> 1) & 1, dead);
             if (dead) break;
             issue_qk(j);
+            TC_TRACE(kEvMmaS, j);
         }
     } else if (warp == kPvWarp) {
         // ================= P V MMA issuer =================
@@ -639,6 +688,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 mma_commit(vfree_bar(vbuf));
             }
             __syncwarp();
+            TC_TRACE(kEvMmaPV, jp);
         }
     } else if (warp < kKeyWarps) {
         // ================= key warps: K -> TMEM =================
@@ -648,6 +698,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         auto load_keys = [&](int j) {
             const int s = j % ST;
             mbar_wait(full_bar(s), (j / ST) & 1, dead);
+            if (warp == 0) TC_TRACE(kEvKeyGo, j);
             const char* st = ring + s * C::STAGE_BYTES;
             const char* s_sc = st + 2 * C::PACK_BYTES + t * C::SROWB;
             constexpr int CPS = 32 / PPC;  // chunks per 32-column store
@@ -671,6 +722,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(kready_bar(j & 1));
+            if (warp == 0) TC_TRACE(kEvKeyEnd, j);
         };
 
         int n = 0;
@@ -726,6 +778,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         int js = 0;
         for (int i = advance(0); i < ntiles; i = advance(i + 1), ++js) {
             mbar_wait(sready_bar(js & 1), (js >> 1) & 1, dead);
+            if (warp == kSmWarp0) TC_TRACE(kEvSmGo, js);
             tc_fence_after();
             float s[kTcHeads];
             tmem_ld16(tbase + lane_off + kTmemS + 16 * (js & 1), s);
@@ -830,6 +883,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(pready_bar(js % PB));
+            if (warp == kSmWarp0) TC_TRACE(kEvSmEnd, js);
         }
         n_active = js;
         if (n_active > 0) {  // the last P V product
@@ -877,6 +931,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 __syncwarp();
                 if (lane == 0) mbar_arrive(empty_bar(s));
                 if (j >= VB) mbar_wait(vfree_bar(vbuf), ((j / VB) - 1) & 1, dead);
+                if (warp == kKeyWarps) TC_TRACE(kEvValGo, j);
 #pragma unroll
                 for (int c = 0; c < C::CPR; ++c) {
                     uint32_t o[PPC];
@@ -900,6 +955,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             fence_proxy_async();
             __syncwarp();
             if (lane == 0) mbar_arrive(vready_bar(vbuf));
+            if (warp == kKeyWarps) TC_TRACE(kEvValEnd, j);
         }
     }
 
@@ -948,6 +1004,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         tmem_dealloc(tbase, kTmemCols);
     }
     finish_cta<T>(a, b, kvh, h0, nh, split, mo, mm, ml);
+    TC_TRACE_CTA(2);
 }
 
 // cuTensorMapEncodeTiled from the driver, looked up once through the runtime
@@ -1068,6 +1125,15 @@ int launch_decode_tc(const DecodeArgs& a, int dtype, cudaStream_t st) {
     if (dtype == QSDPA_F16) return a.bits == 4 ? launch_tc2<__half, 4>(a, st) : launch_tc2<__half, 8>(a, st);
     return a.bits == 4 ? launch_tc2<__nv_bfloat16, 4>(a, st) : launch_tc2<__nv_bfloat16, 8>(a, st);
 }
+
+#ifdef QSDPA_TC_TRACE
+extern "C" int qsdpa_tc_trace_ctas(long long* host) {
+    return cudaMemcpyFromSymbol(host, g_tc_cta, sizeof(g_tc_cta)) == cudaSuccess ? 0 : -1;
+}
+extern "C" int qsdpa_tc_trace_tiles(long long* host) {
+    return cudaMemcpyFromSymbol(host, g_tc_tile, sizeof(g_tc_tile)) == cudaSuccess ? 0 : -1;
+}
+#endif
 
 int read_tc_status(int reset) {
     unsigned int v = 0;
