@@ -50,6 +50,9 @@ __global__ void __launch_bounds__(kThreadsC)
                    float* __restrict__ out_ml) {
 #if defined(__CUDA_ARCH__) && __CUDA_ARCH__ >= 900
     cudaGridDependencySynchronize();
+    // the next kernel on the stream may launch now (the decode kernel waits
+    // for this one's completion before it reads or writes global memory)
+    cudaTriggerProgrammaticLaunchCompletion();
 #endif
     __shared__ float s_w[kMaxPartsSmem];
     __shared__ float s_red[kSplitLanes][kDimQuads * 4 + 4];

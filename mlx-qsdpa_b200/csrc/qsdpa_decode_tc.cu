@@ -123,6 +123,11 @@ constexpr int kTmemK = 64;      // K operand: two buffers of D/2 columns
 constexpr float kRescaleTc = 8.f;
 constexpr unsigned long long kWaitNs = 1000000000ull;
 constexpr int kSmemLimit = 227 * 1024;
+// launch as a programmatic dependent of the previous kernel on the stream
+#ifndef QSDPA_TC_PDL
+#define QSDPA_TC_PDL 1
+#endif
+constexpr bool kTcPdl = QSDPA_TC_PDL != 0;
 #ifndef QSDPA_TC_VREG
 #define QSDPA_TC_VREG 1
 #endif
@@ -276,6 +281,10 @@ __host__ __device__ constexpr uint32_t make_idesc(bool bf16, bool a_mn, bool b_m
     return (1u << 4) | ((bf16 ? 1u : 0u) << 7) | ((bf16 ? 1u : 0u) << 10) | ((a_mn ? 1u : 0u) << 15) |
            ((b_mn ? 1u : 0u) << 16) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
 }
+
+// Wait until the grids this one depends on (programmatic dependent launch)
+// have completed and their writes are visible; a no-op without one.
+__device__ __forceinline__ void grid_dep_wait() { asm volatile("griddepcontrol.wait;\n" ::: "memory"); }
 
 // --------------------------------------------------------------- mbarrier --
 __device__ __forceinline__ void mbar_init(uint32_t addr, int count) {
@@ -601,13 +610,14 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
         }
         __syncwarp();
+        grid_dep_wait();  // the previous kernel's writes (K/V appends) are visible
         for (; prod_j < ST && prod_i < ntiles; prod_i = advance(prod_i + 1), ++prod_j) issue_stage(prod_j, prod_i);
     }
     if (warp == kMmaWarp) {
         tmem_alloc(smem_u32(tmem_slot), kTmemCols);
         tmem_relinquish();
     }
-    tc_fence_before();
+    if (warp != kProdWarp) grid_dep_wait();  // before any global read or write    tc_fence_before();
     __syncthreads();
     tc_fence_after();
     const uint32_t tbase = *tmem_slot;
@@ -1077,8 +1087,21 @@ int launch_tc4(const DecodeArgs& a, cudaStream_t st) {
             if (rc) return rc;
         }
     }
-    dim3 grid(a.splits, a.B * a.Hkv, a.head_blocks);
-    kern<<<grid, kTcThreads, C::SMEM, st>>>(a, tm_k, tm_v);
+    // a programmatic dependent launch: the CTAs may start (barriers, tensor
+    // memory) while the previous kernel on the stream finishes; they wait for
+    // it before touching global memory
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(a.splits, a.B * a.Hkv, a.head_blocks);
+    cfg.blockDim = dim3(kTcThreads);
+    cfg.dynamicSmemBytes = C::SMEM;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = kTcPdl ? 1 : 0;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, a, tm_k, tm_v);
+    if (e != cudaSuccess) return set_error(QSDPA_ERR_CUDA, "qsdpa_decode (tcgen05) launch: %s", cudaGetErrorString(e));
     return check_launch("qsdpa_decode (tcgen05)");
 }
 
