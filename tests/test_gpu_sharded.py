@@ -1,9 +1,10 @@
 """Sequence-sharded decode on GPUs: the peer-memory merge (qsdpa_shard_merge).
 
-* With two or more GPUs: two ranks (NCCL, one process per GPU) hold halves
-  of the keys; the merged output over NVLink peer memory, and over the NCCL
-  all-gather path, must match the single-GPU decode of the whole sequence
-  and the oracle.  Skipped on a one-GPU box.
+* With two or more GPUs: two ranks, and four where the box has four GPUs
+  (NCCL, one process per GPU), each hold a slice of the keys; the merged
+  output over NVLink peer memory, and over the NCCL all-gather path, must
+  match the single-GPU decode of the whole sequence and the oracle.  Skipped
+  on a one-GPU box.
 * On one GPU: a merge whose peer never arrives (its flag is never set) must
   give up after about a second and report it in bit 1 of the device status
   word, without hanging the device.
@@ -59,13 +60,15 @@ def _worker(rank, world, port, q_list):
         dist.destroy_process_group()
 
 
-@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs two GPUs")
-def test_two_rank_peer_merge_matches_single_gpu():
+@pytest.mark.parametrize("world", [2, 4])
+def test_peer_merge_matches_single_gpu(world):
+    if not torch.cuda.is_available() or torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
     import torch.multiprocessing as mp
     ctx = mp.get_context("spawn")
     q_list = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, 2, port, q_list)) for r in range(2)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, q_list)) for r in range(world)]
     for p in procs:
         p.start()
     results = [q_list.get(timeout=300) for _ in procs]
