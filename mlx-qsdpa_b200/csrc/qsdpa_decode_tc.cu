@@ -1,6 +1,6 @@
 // Blackwell decode kernel on the fifth-generation tensor cores (tcgen05):
 // accumulators and the key operand live in tensor memory (TMEM), the other
-// operands in shared memory, and one thread issues every MMA.
+// operands in shared memory, and single threads issue the MMAs.
 //
 // The GQA group of 16 query heads is too small for tcgen05's M (64 or 128),
 // so both products are taken transposed, with the 16 heads as N:
@@ -14,36 +14,41 @@
 // k, q.k, online softmax, dequantise v, accumulate) done for a 128-token tile
 // at a time.
 //
-// Roles (10 warps, one CTA per SM), handing work to each other through
+// Roles (15 warps, one CTA per SM), handing work to each other through
 // mbarriers only -- no CTA-wide barrier inside the key loop:
-//   * warps 0-3 ("key warps"): thread t owns token t of the tile.  It
-//     dequantises the token's packed key row (scale * code + bias, one
-//     rounding) straight into its TMEM lane, then, once the S MMA is done,
-//     reads the token's 16 scores back (tcgen05.ld), runs the online softmax
-//     (log2 domain, running maximum raised only when a score exceeds it by more
-//     than 2^8) and writes the token's 16 probabilities as one row of P^T.
-//   * warps 4-7 ("value warps"): thread t dequantises token t's value row into
-//     the V^T operand (128-byte swizzled, head dims contiguous).
-//   * warp 8 ("producer"): streams packed rows, scales and biases of the next
-//     tiles into a ring of shared-memory stages with 16-byte cp.async (rows
-//     stored with the XOR-128B swizzle, so a thread reading its own row is
-//     bank-conflict free); completion is signalled on the stage's "full"
-//     mbarrier by cp.async.mbarrier.arrive, consumers release it on "empty".
-//   * warp 9: owns the tensor memory and issues the MMAs from one thread
-//     (tcgen05.mma; completion via tcgen05.commit on mbarriers).  It issues
-//     the S MMA of tile j+1 before the P V MMA of tile j, so the key warps
-//     dequantise tile j+1 while the scores of tile j are computed.
-// Buffers: two K operands and two S^T accumulators in TMEM, one P^T operand,
-// two V^T operands in shared memory when they fit (values run a tile ahead).
+//   * warps 0-3 ("key warps"): thread t owns token t of the tile and
+//     dequantises its packed key row (scale * code + bias, one rounding)
+//     straight into its TMEM lane.
+//   * warps 4-7 ("value warps"): thread t copies token t's value row and its
+//     scale / bias pairs to registers (rows of up to 128 bytes), releases the
+//     ring stage, and dequantises the row into the V^T operand (128-byte
+//     swizzled, head dims contiguous).
+//   * warps 8-11 ("softmax warps"): stage Q once, then per tile read the 16
+//     scores of token t back (tcgen05.ld), run the online softmax (log2
+//     domain, running maximum raised only when a score exceeds it by more
+//     than 2^8) and write the token's 16 probabilities as one row of P^T; at
+//     the end read O^T out.
+//   * warp 12 ("producer"): streams packed rows (TMA, or 16-byte cp.async for
+//     64-byte rows), scales and biases of the next tiles into a ring of
+//     shared-memory stages stored with the XOR-128B swizzle, so a thread
+//     reading its own row is bank-conflict free; the stage's "full" mbarrier
+//     completes on the copies, consumers release it on "empty".
+//   * warp 13 owns the tensor memory and issues the S MMAs, warp 14 the P V
+//     MMAs, each from one elected thread (tcgen05.mma; completion via
+//     tcgen05.commit on mbarriers).
+// Buffers: two K operands and two S^T accumulators in TMEM, two P^T operands
+// and two V^T operands in shared memory when they fit (values run a tile
+// ahead).  Every wait is an mbarrier.try_wait that suspends the warp until
+// the phase completes, so waiting warps take no issue slots.
 //
 // Dimension order: the exact nibble -> half conversion yields the pairs
 // (d, d+4) of each 8-dim word, so K columns and V^T rows hold the head dims of
 // each word in the order 0,4,1,5,2,6,3,7.  Q is staged in the same order (a dot
 // product does not care) and the O^T rows are put back in order when read out.
 //
-// Every wait on an MMA completion is bounded (about one second of global
-// time); a wait that runs out records bit 0 of the device status word and the
-// kernel finishes without hanging (its output is then undefined).
+// Every wait is bounded (about one second of global time); a wait that runs
+// out records bit 0 of the device status word and the kernel finishes without
+// hanging (its output is then undefined).
 #include <cuda.h>
 
 #include <string.h>
