@@ -277,14 +277,15 @@ def main():
         if world == 1:
             _lib.decode(q, pk, pv, ks, vs, kb, vb, scale=scale, bits=BITS, group_size=GS, out=outs[i % L],
                         kernel=kern_code)
+        elif exchange is not None:
+            # decode + merge with the other ranks over peer memory in one call
+            _lib.decode(q, pk, pv, ks, vs, kb, vb, scale=scale, bits=BITS, group_size=GS, out=outs[i % L],
+                        part=part, kernel=kern_code, shard=exchange.shard_args())
         else:
             _lib.decode(q, pk, pv, ks, vs, kb, vb, scale=scale, bits=BITS, group_size=GS,
                         out_mode=_lib.OUT_PARTIAL, part=part, kernel=kern_code)
-            if exchange is not None:
-                exchange.merge(rec, outs[i % L].view(rows, D))
-            else:
-                dist.all_gather_into_tensor(gath, rec)
-                _lib.combine_packed(gath, rows, D, out=outs[i % L].view(rows, D))
+            dist.all_gather_into_tensor(gath, rec)
+            _lib.combine_packed(gath, rows, D, out=outs[i % L].view(rows, D))
 
     # warm-up (also allocates the decode workspace outside any capture)
     for i in range(max(args.warmup, 3)):
@@ -425,9 +426,13 @@ def main():
         (pk0, ks0, kb0), (pv0, vs0, vb0) = layers[0]
         splits = _lib.plan_splits(q, pk0, pv0, ks0, vs0, kb0, vb0, BITS, GS, kernel=kern_code)
         traffic, traffic_src = profiled_traffic(args.kernel)
-        # decode (+ split merge); N>1: + the peer exchange-and-merge kernel (p2p) or, after NCCL's
-        # all-gather, the record merge
-        launches_per_step = (1 if splits == 1 else 2) + (1 if world > 1 else 0)
+        # decode (+ split merge); N>1 over peer memory: decode + the fused split merge / exchange /
+        # rank merge (or, keys not split, the exchange-and-merge kernel); over NCCL: + the record
+        # merge after NCCL's all-gather
+        if world > 1 and exchange is not None:
+            launches_per_step = 2
+        else:
+            launches_per_step = (1 if splits == 1 else 2) + (1 if world > 1 else 0)
         line = {
             "metric": METRIC,
             "value": round(ms_per_step * 1e3, 3),

@@ -256,6 +256,23 @@ int qsdpa_shard_merge(const float* rec, float* const* bufs, unsigned int* state,
                       int D, void* out, int dtype, void* stream);
 
 /*
+ * Sequence-sharded decode step in one call (no reference counterpart): this
+ * rank's decode over its key shard followed by the merge with the other
+ * ranks, over the same buffers and step counter as qsdpa_shard_merge.  `p`
+ * is a qsdpa_decode call with out_mode QSDPA_OUT_FINAL whose `out` receives
+ * the merged output (B, H_q, 1, D); `part_o` / `part_ml` must point to this
+ * rank's record buffers (B*H_q x D and B*H_q x 2 fp32), which hold the record
+ * when the keys are not split.  When they are split, one kernel merges the
+ * split records of each 64-dim slice, stores the slice to every rank and
+ * merges the ranks' slices (no record round trip through memory and one
+ * kernel fewer than qsdpa_decode + qsdpa_shard_merge).  Every rank makes the
+ * same calls in the same order; errors and the ~1 s wait bound as
+ * qsdpa_shard_merge.
+ */
+int qsdpa_decode_shard(const qsdpa_decode_params* p, float* const* bufs, unsigned int* state, int rank, int world,
+                       void* stream);
+
+/*
  * Device-side faults recorded by the kernels since the last reset: bit 0 = a
  * wait on a tensor-core completion barrier ran out of time, bit 1 = a
  * sharded merge waited in vain for another rank (the kernel gave up after

@@ -260,12 +260,15 @@ extern "C" size_t qsdpa_decode_workspace_size(const qsdpa_decode_params* p) {
     return pl.ws_bytes;
 }
 
-extern "C" int qsdpa_decode(const qsdpa_decode_params* p, void* stream) {
+namespace qsdpa {
+namespace {
+
+// validate, plan, lay out the workspace and launch the decode kernel (split
+// records into the workspace when the keys are split)
+int launch_decode(const qsdpa_decode_params* p, cudaStream_t st, DecodeArgs& a, Plan& pl) {
     int rc = validate(p);
     if (rc) return rc;
-    DecodeArgs a;
     fill_args(p, a);
-    Plan pl;
     rc = make_plan(p, a, pl);
     if (rc) return rc;
     a.heads_per_block = pl.heads_per_block;
@@ -283,10 +286,19 @@ extern "C" int qsdpa_decode(const qsdpa_decode_params* p, void* stream) {
         a.ws_o = reinterpret_cast<float*>(ws);
         a.ws_ml = reinterpret_cast<float*>(ws + align256(rows * pl.splits * a.D * sizeof(float)));
     }
+    return pl.kern == Kern::Tc    ? launch_decode_tc(a, p->dtype, st)
+           : pl.kern == Kern::Mma ? launch_decode_mma(a, p->dtype, st)
+                                  : launch_decode_simt(a, p->dtype, st);
+}
+
+}  // namespace
+}  // namespace qsdpa
+
+extern "C" int qsdpa_decode(const qsdpa_decode_params* p, void* stream) {
+    DecodeArgs a;
+    Plan pl;
     cudaStream_t st = static_cast<cudaStream_t>(stream);
-    rc = pl.kern == Kern::Tc    ? launch_decode_tc(a, p->dtype, st)
-         : pl.kern == Kern::Mma ? launch_decode_mma(a, p->dtype, st)
-                                : launch_decode_simt(a, p->dtype, st);
+    const int rc = launch_decode(p, st, a, pl);
     if (rc) return rc;
     if (pl.splits > 1) {
         // merge the (row, split, D) workspace records with a second launch
@@ -298,6 +310,30 @@ extern "C" int qsdpa_decode(const qsdpa_decode_params* p, void* stream) {
                                       p->out_mode == QSDPA_OUT_PARTIAL ? p->part_ml : nullptr, true, st);
     }
     return QSDPA_OK;
+}
+
+extern "C" int qsdpa_decode_shard(const qsdpa_decode_params* p, float* const* bufs, unsigned int* state, int rank,
+                                  int world, void* stream) {
+    if (!p) return set_error(QSDPA_ERR_INVALID, "qsdpa_decode_shard: params is NULL");
+    if (p->out_mode != QSDPA_OUT_FINAL || !p->out || !p->part_o || !p->part_ml)
+        return set_error(QSDPA_ERR_INVALID,
+                         "qsdpa_decode_shard: out_mode must be QSDPA_OUT_FINAL with out, part_o and part_ml set");
+    int rc = check_shard_args(bufs, state, rank, world, p->B * p->Hq, p->D, p->dtype, "qsdpa_decode_shard");
+    if (rc) return rc;
+    // the decode writes this rank's record: split records into the workspace,
+    // or (keys not split) the record itself into part_o / part_ml
+    qsdpa_decode_params q = *p;
+    q.out_mode = QSDPA_OUT_PARTIAL;
+    DecodeArgs a;
+    Plan pl;
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    rc = launch_decode(&q, st, a, pl);
+    if (rc) return rc;
+    const int rows = a.B * a.Hq;
+    if (pl.splits > 1)
+        return launch_shard_combine(a.ws_o, a.ws_ml, a.D, 2, (int64_t)pl.splits * a.D, (int64_t)pl.splits * 2,
+                                    pl.splits, bufs, state, rank, world, rows, a.D, p->out, p->dtype, st);
+    return launch_shard_merge(p->part_o, p->part_ml, bufs, state, rank, world, rows, a.D, p->out, p->dtype, st);
 }
 
 extern "C" int qsdpa_device_status(int reset) {

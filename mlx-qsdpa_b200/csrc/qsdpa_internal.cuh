@@ -163,6 +163,17 @@ bool tc_supported(const DecodeArgs& a);
 // (each file keeps its own word); reset clears them.
 int read_tc_status(int reset);
 int read_shard_status(int reset);
+// Sequence-sharded merge over peer memory (qsdpa_shard.cu): argument checks,
+// the rank merge of one record per rank (o: rows x D, (m, l): rows x 2) and
+// the fused split merge + rank merge of the decode's split records (layout as
+// launch_combine_strided).
+int check_shard_args(float* const* bufs, const unsigned int* state, int rank, int world, int rows, int D, int dtype,
+                     const char* what);
+int launch_shard_merge(const float* rec_o, const float* rec_ml, float* const* bufs, unsigned int* state, int rank,
+                       int world, int rows, int D, void* out, int dtype, cudaStream_t st);
+int launch_shard_combine(const float* po, const float* pml, int64_t so, int64_t sml, int64_t ro, int64_t rml,
+                         int parts, float* const* bufs, unsigned int* state, int rank, int world, int rows, int D,
+                         void* out, int dtype, cudaStream_t st);
 bool mma_supported(const DecodeArgs& a);
 int mma_heads_per_block(const DecodeArgs& a);
 // Merge parts of partial records (part p of row r: o at po + p*so + r*ro,

@@ -22,9 +22,13 @@
 // parity e & 1, and it cannot store step e+2 before every other rank has
 // stored e+1, which they do only after merging e.  A wait that runs out sets
 // bit 1 of the device status word and the kernel returns (output undefined).
+//
+// qsdpa_decode_shard fuses the split merge into the exchange: its kernel
+// merges the split records of a slice (merge::slice_merge), stores the merged
+// slice to the peers as above and merges the ranks' slices, all in one CTA.
 #include <algorithm>
 
-#include "qsdpa_internal.cuh"
+#include "qsdpa_merge.cuh"
 
 namespace qsdpa {
 
@@ -68,9 +72,47 @@ __device__ __forceinline__ bool wait_word(const uint2* p, unsigned int e, uint64
     return true;
 }
 
+// Thread t < kDims: merge dim t of slice c of the world ranks' records of step
+// e (words in this rank's buffer `own`, one rank's slices every `slab` words)
+// into *o_out / *l_out; false when a rank's word did not arrive in time.
+__device__ __forceinline__ bool merge_ranks(const uint2* own, int64_t slab, int c, int world, unsigned int e, int t,
+                                           float& o_out, float& l_out) {
+    const uint64_t t0 = now_ns();
+    float mt = -INFINITY, lt = 0.f, ot = 0.f;
+    for (int r = 0; r < world; ++r) {
+        const uint2* src = own + r * slab + (int64_t)c * kWords;
+        float o, m, l;
+        if (!(wait_word(src + t, e, t0, o) && wait_word(src + kDims, e, t0, m) && wait_word(src + kDims + 1, e, t0, l)))
+            return false;
+        if (m == -INFINITY) continue;
+        if (m > mt) {  // running maximum: no per-rank arrays
+            const float sc = mt == -INFINITY ? 0.f : exp2f(mt - m);
+            lt = lt * sc + l;
+            ot = ot * sc + o;
+            mt = m;
+        } else {
+            const float w = exp2f(m - mt);
+            lt += w * l;
+            ot += w * o;
+        }
+    }
+    o_out = ot;
+    l_out = lt;
+    return true;
+}
+
+// the last CTA of step e resets the count and publishes e for the next step
+__device__ __forceinline__ void finish_step(unsigned int* state, unsigned int e) {
+    if (threadIdx.x == 0 && atomicAdd(state + 1, 1u) + 1u == gridDim.x) {
+        state[1] = 0;
+        atomicExch(state, e);
+    }
+}
+
 template <typename T>
-__global__ void __launch_bounds__(kDims) shard_merge_kernel(const float* __restrict__ rec, int rows, int D, PeerBufs peers,
-                                                            int rank, int world, unsigned int* state,
+__global__ void __launch_bounds__(kDims) shard_merge_kernel(const float* __restrict__ rec_o,
+                                                            const float* __restrict__ rec_ml, int rows, int D,
+                                                            PeerBufs peers, int rank, int world, unsigned int* state,
                                                             T* __restrict__ out) {
 #if defined(__CUDA_ARCH__) && __CUDA_ARCH__ >= 900
     cudaGridDependencySynchronize();  // the record is written by the preceding kernel
@@ -85,47 +127,66 @@ __global__ void __launch_bounds__(kDims) shard_merge_kernel(const float* __restr
     // depends on is always running.
     for (int c = blockIdx.x; c < ncta; c += gridDim.x) {
         const int row = c % rows, d = (c / rows) * kDims + tid;
-        const float ov = d < D ? rec[(int64_t)row * D + d] : 0.f;
-        const float mlv = tid < 2 ? rec[(int64_t)rows * D + 2 * row + tid] : 0.f;
+        const float ov = d < D ? rec_o[(int64_t)row * D + d] : 0.f;
+        const float mlv = tid < 2 ? rec_ml[2 * row + tid] : 0.f;
         for (int r = 0; r < world; ++r) {
             uint2* dst = peers.buf[r] + ((int64_t)(e & 1u) * world + rank) * slab + (int64_t)c * kWords;
             st_word(dst + tid, ov, e);
             if (tid < 2) st_word(dst + kDims + tid, mlv, e);
         }
-        // merge the world records of slice c (running maximum: no per-rank arrays)
-        const uint64_t t0 = now_ns();
-        bool ok = true;
-        float mt = -INFINITY, lt = 0.f, ot = 0.f;
-        for (int r = 0; r < world && ok; ++r) {
-            const uint2* src = own + r * slab + (int64_t)c * kWords;
-            float o, m, l;
-            ok = wait_word(src + tid, e, t0, o) && wait_word(src + kDims, e, t0, m) &&
-                 wait_word(src + kDims + 1, e, t0, l);
-            if (!ok || m == -INFINITY) continue;
-            if (m > mt) {
-                const float s = mt == -INFINITY ? 0.f : exp2f(mt - m);
-                lt = lt * s + l;
-                ot = ot * s + o;
-                mt = m;
-            } else {
-                const float w = exp2f(m - mt);
-                lt += w * l;
-                ot += w * o;
-            }
-        }
+        // merge the world records of slice c
+        float ot, lt;
+        const bool ok = merge_ranks(own, slab, c, world, e, tid, ot, lt);
         if (__syncthreads_or(!ok)) {
             if (tid == 0) atomicOr(&g_shard_status, 2u);
             break;
         }
         if (d < D) out[(int64_t)row * D + d] = Dt<T>::from_f(lt > 0.f ? ot / lt : 0.f);
     }
-    if (tid == 0) {
-        // the last CTA of this step resets the count and publishes e
-        if (atomicAdd(state + 1, 1u) + 1u == gridDim.x) {
-            state[1] = 0;
-            atomicExch(state, e);
+    finish_step(state, e);
+}
+
+// Fused split merge + exchange + rank merge (qsdpa_decode_shard): the CTA
+// (merge::kThreads threads) handles slices blockIdx.x, + gridDim.x, ...; for
+// each it merges the `parts` split records of the slice, stores the merged
+// slice to every rank (threads t < kDims: dim t; threads 0, 1: m, l), then
+// threads t < kDims merge the ranks' slices into the output.
+template <typename T>
+__global__ void __launch_bounds__(merge::kThreads)
+    shard_combine_kernel(const float* __restrict__ po, const float* __restrict__ pml, int64_t so, int64_t sml,
+                         int64_t ro, int64_t rml, int parts, int rows, int D, PeerBufs peers, int rank, int world,
+                         unsigned int* state, T* __restrict__ out) {
+#if defined(__CUDA_ARCH__) && __CUDA_ARCH__ >= 900
+    cudaGridDependencySynchronize();  // the split records are written by the decode kernel
+#endif
+    static_assert(merge::kSlice == kDims, "a merge slice is an exchange slice");
+    __shared__ merge::Smem sm;
+    const unsigned int e = state[0] + 1u;
+    const int tid = threadIdx.x;
+    const int ncta = rows * ((D + kDims - 1) / kDims);
+    const int64_t slab = (int64_t)ncta * kWords;
+    const uint2* own = peers.buf[rank] + (int64_t)(e & 1u) * world * slab;
+    // every rank walks the slices in the same order with the same (resident) grid
+    for (int c = blockIdx.x; c < ncta; c += gridDim.x) {
+        const int row = c % rows, sl = c / rows, d = sl * kDims + tid;
+        float m_loc, l_loc;
+        const float o_loc = merge::slice_merge(po, pml, so, sml, ro, rml, parts, D, row, sl, sm, m_loc, l_loc);
+        if (tid < kDims) {
+            for (int r = 0; r < world; ++r) {
+                uint2* dst = peers.buf[r] + ((int64_t)(e & 1u) * world + rank) * slab + (int64_t)c * kWords;
+                st_word(dst + tid, d < D ? o_loc : 0.f, e);
+                if (tid < 2) st_word(dst + kDims + tid, tid == 0 ? m_loc : l_loc, e);
+            }
         }
+        float ot = 0.f, lt = 0.f;
+        const bool ok = tid < kDims ? merge_ranks(own, slab, c, world, e, tid, ot, lt) : true;
+        if (__syncthreads_or(!ok)) {
+            if (tid == 0) atomicOr(&g_shard_status, 2u);
+            break;
+        }
+        if (tid < kDims && d < D) out[(int64_t)row * D + d] = Dt<T>::from_f(lt > 0.f ? ot / lt : 0.f);
     }
+    finish_step(state, e);
 }
 
 }  // namespace
@@ -144,6 +205,87 @@ int read_shard_status(int reset) {
 
 using namespace qsdpa;
 
+namespace qsdpa {
+
+int check_shard_args(float* const* bufs, const unsigned int* state, int rank, int world, int rows, int D, int dtype,
+                     const char* what) {
+    if (world < 1 || world > kMaxWorld || rank < 0 || rank >= world)
+        return set_error(QSDPA_ERR_INVALID, "%s: world %d / rank %d (world <= %d)", what, world, rank, kMaxWorld);
+    if (rows <= 0 || D <= 0 || D % 32 || !bufs || !state)
+        return set_error(QSDPA_ERR_INVALID, "%s: bad arguments (rows %d, D %d)", what, rows, D);
+    if (dtype != QSDPA_F16 && dtype != QSDPA_BF16)
+        return set_error(QSDPA_ERR_INVALID, "%s: dtype must be QSDPA_F16 or QSDPA_BF16", what);
+    for (int r = 0; r < world; ++r) {
+        if (!bufs[r] || (uintptr_t)bufs[r] % 16)
+            return set_error(QSDPA_ERR_INVALID, "%s: buffer of rank %d is NULL or not 16-byte aligned", what, r);
+    }
+    return QSDPA_OK;
+}
+
+namespace {
+
+PeerBufs peer_bufs(float* const* bufs, int world) {
+    PeerBufs peers = {};
+    for (int r = 0; r < world; ++r) peers.buf[r] = reinterpret_cast<uint2*>(bufs[r]);
+    return peers;
+}
+
+cudaLaunchConfig_t pdl_config(int ctas, int threads, cudaStream_t st, cudaLaunchAttribute* attr) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(ctas);
+    cfg.blockDim = dim3(threads);
+    cfg.stream = st;
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cfg;
+}
+
+}  // namespace
+
+int launch_shard_merge(const float* rec_o, const float* rec_ml, float* const* bufs, unsigned int* state, int rank,
+                       int world, int rows, int D, void* out, int dtype, cudaStream_t st) {
+    const int rc = check_shard_args(bufs, state, rank, world, rows, D, dtype, "qsdpa_shard_merge");
+    if (rc) return rc;
+    const PeerBufs peers = peer_bufs(bufs, world);
+    cudaLaunchAttribute attr[1];
+    const cudaLaunchConfig_t cfg = pdl_config(std::min(rows * ((D + kDims - 1) / kDims), kMaxCtas), kDims, st, attr);
+    const cudaError_t err =
+        dtype == QSDPA_F16
+            ? cudaLaunchKernelEx(&cfg, shard_merge_kernel<__half>, rec_o, rec_ml, rows, D, peers, rank, world, state,
+                                 static_cast<__half*>(out))
+            : cudaLaunchKernelEx(&cfg, shard_merge_kernel<__nv_bfloat16>, rec_o, rec_ml, rows, D, peers, rank, world,
+                                 state, static_cast<__nv_bfloat16*>(out));
+    if (err != cudaSuccess) return set_error(QSDPA_ERR_CUDA, "qsdpa_shard_merge launch: %s", cudaGetErrorString(err));
+    return check_launch("qsdpa_shard_merge");
+}
+
+int launch_shard_combine(const float* po, const float* pml, int64_t so, int64_t sml, int64_t ro, int64_t rml,
+                         int parts, float* const* bufs, unsigned int* state, int rank, int world, int rows, int D,
+                         void* out, int dtype, cudaStream_t st) {
+    const int rc = check_shard_args(bufs, state, rank, world, rows, D, dtype, "qsdpa_decode_shard");
+    if (rc) return rc;
+    const PeerBufs peers = peer_bufs(bufs, world);
+    if (parts > merge::kMaxParts)
+        return set_error(QSDPA_ERR_INVALID, "qsdpa_decode_shard: at most %d splits, got %d", merge::kMaxParts, parts);
+    // two 256-thread CTAs per SM at most, so the whole grid is resident and a
+    // wait on another rank never depends on a CTA that has not started
+    const int ctas = std::min(rows * ((D + kDims - 1) / kDims), 2 * sm_count());
+    cudaLaunchAttribute attr[1];
+    const cudaLaunchConfig_t cfg = pdl_config(ctas, merge::kThreads, st, attr);
+    const cudaError_t err =
+        dtype == QSDPA_F16
+            ? cudaLaunchKernelEx(&cfg, shard_combine_kernel<__half>, po, pml, so, sml, ro, rml, parts, rows, D, peers,
+                                 rank, world, state, static_cast<__half*>(out))
+            : cudaLaunchKernelEx(&cfg, shard_combine_kernel<__nv_bfloat16>, po, pml, so, sml, ro, rml, parts, rows, D,
+                                 peers, rank, world, state, static_cast<__nv_bfloat16*>(out));
+    if (err != cudaSuccess) return set_error(QSDPA_ERR_CUDA, "qsdpa_decode_shard launch: %s", cudaGetErrorString(err));
+    return check_launch("qsdpa_decode_shard");
+}
+
+}  // namespace qsdpa
+
 extern "C" size_t qsdpa_shard_buffer_bytes(int world, int rows, int D) {
     if (world < 1 || world > kMaxWorld || rows <= 0 || D <= 0) return 0;
     const size_t ncta = (size_t)rows * ((D + kDims - 1) / kDims);
@@ -152,34 +294,8 @@ extern "C" size_t qsdpa_shard_buffer_bytes(int world, int rows, int D) {
 
 extern "C" int qsdpa_shard_merge(const float* rec, float* const* bufs, unsigned int* state, int rank, int world,
                                  int rows, int D, void* out, int dtype, void* stream) {
-    if (world < 1 || world > kMaxWorld || rank < 0 || rank >= world)
-        return set_error(QSDPA_ERR_INVALID, "qsdpa_shard_merge: world %d / rank %d (world <= %d)", world, rank,
-                         kMaxWorld);
-    if (rows <= 0 || rows > 65535 || D <= 0 || D % 32 || !rec || !bufs || !state || !out)
+    if (!rec || !out || rows <= 0 || D <= 0)
         return set_error(QSDPA_ERR_INVALID, "qsdpa_shard_merge: bad arguments (rows %d, D %d)", rows, D);
-    if (dtype != QSDPA_F16 && dtype != QSDPA_BF16)
-        return set_error(QSDPA_ERR_INVALID, "qsdpa_shard_merge: dtype must be QSDPA_F16 or QSDPA_BF16");
-    PeerBufs peers = {};
-    for (int r = 0; r < world; ++r) {
-        if (!bufs[r] || (uintptr_t)bufs[r] % 16)
-            return set_error(QSDPA_ERR_INVALID, "qsdpa_shard_merge: buffer of rank %d is NULL or not 16-byte aligned",
-                             r);
-        peers.buf[r] = reinterpret_cast<uint2*>(bufs[r]);
-    }
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(std::min(rows * ((D + kDims - 1) / kDims), kMaxCtas));
-    cfg.blockDim = dim3(kDims);
-    cfg.stream = static_cast<cudaStream_t>(stream);
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[0].val.programmaticStreamSerializationAllowed = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    cudaError_t err = dtype == QSDPA_F16
-                          ? cudaLaunchKernelEx(&cfg, shard_merge_kernel<__half>, rec, rows, D, peers, rank, world,
-                                               state, static_cast<__half*>(out))
-                          : cudaLaunchKernelEx(&cfg, shard_merge_kernel<__nv_bfloat16>, rec, rows, D, peers, rank,
-                                               world, state, static_cast<__nv_bfloat16*>(out));
-    if (err != cudaSuccess) return set_error(QSDPA_ERR_CUDA, "qsdpa_shard_merge launch: %s", cudaGetErrorString(err));
-    return check_launch("qsdpa_shard_merge");
+    return launch_shard_merge(rec, rec + (size_t)rows * D, bufs, state, rank, world, rows, D, out, dtype,
+                              static_cast<cudaStream_t>(stream));
 }

@@ -84,7 +84,7 @@ class DequantizeParams(ctypes.Structure):
 EXPORTS = (
     "qsdpa_decode", "qsdpa_decode_noalloc", "qsdpa_decode_splits", "qsdpa_decode_workspace_size",
     "qsdpa_combine", "qsdpa_quantize", "qsdpa_dequantize", "qsdpa_device_status", "qsdpa_shard_buffer_bytes",
-    "qsdpa_shard_merge", "qsdpa_last_error", "qsdpa_abi_version",
+    "qsdpa_shard_merge", "qsdpa_decode_shard", "qsdpa_last_error", "qsdpa_abi_version",
 )
 
 _lib = None
@@ -125,6 +125,9 @@ def load() -> ctypes.CDLL:
         lib.qsdpa_shard_merge.argtypes = [_c_vp, ctypes.POINTER(_c_vp), _c_vp, ctypes.c_int, ctypes.c_int,
                                           ctypes.c_int, ctypes.c_int, _c_vp, ctypes.c_int, _c_vp]
         lib.qsdpa_shard_merge.restype = ctypes.c_int
+        lib.qsdpa_decode_shard.argtypes = [P(DecodeParams), ctypes.POINTER(_c_vp), _c_vp, ctypes.c_int, ctypes.c_int,
+                                           _c_vp]
+        lib.qsdpa_decode_shard.restype = ctypes.c_int
         lib.qsdpa_device_status.argtypes = [ctypes.c_int]
         lib.qsdpa_device_status.restype = ctypes.c_int
         lib.qsdpa_last_error.argtypes = []
@@ -210,12 +213,15 @@ def decode(q: torch.Tensor, kp, vp, ks, vs, kb, vb, *, scale: float, bits: int, 
            kv_start: Optional[torch.Tensor] = None, kv_len: Optional[torch.Tensor] = None,
            splits: int = 0, out_mode: int = OUT_FINAL,
            out: Optional[torch.Tensor] = None, part: Optional[Tuple[torch.Tensor, torch.Tensor]] = None,
-           kernel: int = KERNEL_AUTO):
+           kernel: int = KERNEL_AUTO, shard: Optional[tuple] = None):
     """Fused decode through ``qsdpa_decode``.
 
     q: (B, Hq, 1, D); kp/vp: (B, Hkv, N, pd) uint32; ks/vs/kb/vb: (B, Hkv, N, G).
     mask (optional): 4-D (B|1, Hq|1, 1, N) with contiguous last dim.
     Returns ``out`` (FINAL) or ``(part_o, part_ml)`` (PARTIAL).
+    ``shard = (bufs, state, rank, world)``: one step of a sequence-sharded
+    decode through ``qsdpa_decode_shard`` (this rank's keys, merged with the
+    other ranks over their peer buffers); returns the merged ``out``.
     """
     lib = load()
     B, Hq, qL, D = q.shape
@@ -247,7 +253,7 @@ def decode(q: torch.Tensor, kp, vp, ks, vs, kb, vb, *, scale: float, bits: int, 
         if out is None:
             out = torch.empty((B, Hq, 1, D), dtype=q.dtype, device=dev)
         p.out = out.data_ptr()
-    else:
+    if shard is not None or out_mode != OUT_FINAL:
         if part is None:
             part = (torch.empty((B * Hq, D), dtype=torch.float32, device=dev),
                     torch.empty((B * Hq, 2), dtype=torch.float32, device=dev))
@@ -258,6 +264,11 @@ def decode(q: torch.Tensor, kp, vp, ks, vs, kb, vb, *, scale: float, bits: int, 
         ws = workspace(dev, nbytes + 256)
         p.workspace = _aligned_ptr(ws)
         p.workspace_bytes = nbytes
+    if shard is not None:
+        bufs, state, rank, world = shard
+        ptrs = (_c_vp * world)(*[int(b) for b in bufs])
+        _check(lib.qsdpa_decode_shard(ref, ptrs, state.data_ptr(), rank, world, _stream(dev)), "qsdpa_decode_shard")
+        return out
     _check(lib.qsdpa_decode(ref, _stream(dev)), "qsdpa_decode")
     return out if out_mode == OUT_FINAL else part
 

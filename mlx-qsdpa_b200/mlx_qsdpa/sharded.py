@@ -72,6 +72,10 @@ class PeerExchange:
         """Merge this step's records of all ranks; rec is (rows*(D+2),) fp32, out (rows, D)."""
         return _lib.shard_merge(rec, self.ptrs, self.state, self.rank, self.world, self.rows, self.D, out)
 
+    def shard_args(self):
+        """(bufs, state, rank, world) for ``_lib.decode(..., shard=...)`` (qsdpa_decode_shard)."""
+        return self.ptrs, self.state, self.rank, self.world
+
 
 def _gather(t: torch.Tensor, group) -> torch.Tensor:
     world = dist.get_world_size(group)
@@ -118,6 +122,12 @@ def sharded_quantized_sdpa(q, k_quant, v_quant, *, bits=4, group_size=32, scale=
     # one packed record per rank, [o (rows x D) | m, l (rows x 2)]: one all-gather
     rec = torch.empty(rows * (D + 2), dtype=torch.float32, device=q.device)
     part = (rec[: rows * D].view(rows, D), rec[rows * D:].view(rows, 2))
+    if exchange is not None and partial_fn is None:
+        # decode and peer merge in one call (the split records merged and
+        # exchanged by one kernel)
+        out = torch.empty((B, Hq, 1, D), dtype=q.dtype, device=q.device)
+        return _partial_cuda(q, k_quant, v_quant, scale, bits, group_size, mask, part, out=out,
+                             shard=exchange.shard_args())
     if partial_fn is None:
         _partial_cuda(q, k_quant, v_quant, scale, bits, group_size, mask, part)
     else:
@@ -135,7 +145,7 @@ def sharded_quantized_sdpa(q, k_quant, v_quant, *, bits=4, group_size=32, scale=
     return out.view(B, Hq, 1, D)
 
 
-def _partial_cuda(q, k_quant, v_quant, scale, bits, group_size, mask, part):
+def _partial_cuda(q, k_quant, v_quant, scale, bits, group_size, mask, part, out=None, shard=None):
     from .dispatch import _fused_mask, _mask_kind  # local: shared validation helpers
     pk, ks, kb = k_quant
     pv, vs, vb = v_quant
@@ -147,7 +157,8 @@ def _partial_cuda(q, k_quant, v_quant, scale, bits, group_size, mask, part):
         _lib.rows_contiguous(vb) if vb is not None else None, scale=scale, bits=bits, group_size=group_size,
         mask=m, mask_kind=_mask_kind(m) if m is not None else _lib.MASK_NONE,
         kv_start=ranges.start if ranges is not None else None,
-        kv_len=ranges.length if ranges is not None else None, out_mode=_lib.OUT_PARTIAL, part=part)
+        kv_len=ranges.length if ranges is not None else None,
+        out_mode=_lib.OUT_FINAL if shard is not None else _lib.OUT_PARTIAL, part=part, out=out, shard=shard)
 
 
 class SequenceShardedCache:

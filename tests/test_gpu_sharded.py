@@ -101,3 +101,33 @@ def test_missing_peer_times_out_and_reports():
     torch.cuda.synchronize()
     assert _lib.device_status(reset=True) & 2
     assert _lib.device_status() == 0
+
+
+@pytest.mark.skipif(not torch.cuda.is_available(), reason="needs a GPU")
+@pytest.mark.parametrize("kernel,N,splits", [("mma", 3000, 0), ("mma", 3000, 1), ("tcgen05", 40000, 0),
+                                             ("tcgen05", 40000, 1)])
+def test_decode_shard_single_rank_matches_decode(kernel, N, splits):
+    """qsdpa_decode_shard with a world of one: the fused split merge + exchange
+    (or, keys not split, the record + exchange kernel) must give what
+    qsdpa_decode gives, on consecutive steps (both parities of the step
+    counter)."""
+    from mlx_qsdpa import _lib
+    _lib.load()
+    _lib.device_status(reset=True)
+    c = Case(1, 32, 2, N, 256, seed=N + splits)
+    q, pk, pv, ks, vs, kb, vb = c.torch_args()
+    code = _lib.KERNEL_TCGEN05 if kernel == "tcgen05" else _lib.KERNEL_MMA
+    rows, D = 32, 256
+    buf = torch.zeros(_lib.shard_buffer_bytes(1, rows, D) // 4, dtype=torch.float32, device="cuda")
+    state = torch.zeros(2, dtype=torch.int32, device="cuda")
+    part = (torch.empty((rows, D), dtype=torch.float32, device="cuda"),
+            torch.empty((rows, 2), dtype=torch.float32, device="cuda"))
+    ref = _lib.decode(q, pk, pv, ks, vs, kb, vb, scale=D ** -0.5, bits=4, group_size=32, kernel=code, splits=splits)
+    for step in range(3):
+        out = torch.empty_like(q)
+        _lib.decode(q, pk, pv, ks, vs, kb, vb, scale=D ** -0.5, bits=4, group_size=32, kernel=code, splits=splits,
+                    out=out, part=part, shard=([buf.data_ptr()], state, 0, 1))
+        torch.cuda.synchronize()
+        assert (out.float() - ref.float()).abs().max().item() < 2e-3, f"step {step}"
+    assert_close(from_torch(out), c.reference(), what=f"decode_shard {kernel}")
+    assert _lib.device_status(reset=True) == 0
