@@ -22,6 +22,7 @@ LIB_PATH = os.environ.get("QSDPA_LIB") or os.path.join(_HERE, "libqsdpa.so")
 QSDPA_F16, QSDPA_BF16 = 0, 1
 MASK_NONE, MASK_BOOL, MASK_ADD_F16, MASK_ADD_BF16, MASK_ADD_F32 = 0, 1, 2, 3, 4
 OUT_FINAL, OUT_PARTIAL = 0, 1
+ERR_WORKSPACE = -3  # QSDPA_ERR_WORKSPACE: workspace missing or too small
 KERNEL_AUTO, KERNEL_TCGEN05, KERNEL_MMA, KERNEL_SIMT = 0, 1, 2, 3
 ABI_VERSION = 2
 
@@ -162,7 +163,13 @@ def _ptr(t: Optional[torch.Tensor]) -> Optional[int]:
     return None if t is None else t.data_ptr()
 
 
+# the current stream's raw handle without building a torch.cuda.Stream object
+_raw_stream = getattr(torch._C, "_cuda_getCurrentRawStream", None)
+
+
 def _stream(dev: torch.device) -> int:
+    if _raw_stream is not None:
+        return _raw_stream(dev.index if dev.index is not None else torch.cuda.current_device())
     return torch.cuda.current_stream(dev).cuda_stream
 
 
@@ -184,14 +191,14 @@ _ws_cache: dict = {}
 _ws_lock = threading.Lock()
 
 
-def workspace(device: torch.device, nbytes: int) -> torch.Tensor:
+def workspace(device: torch.device, nbytes: int, stream: Optional[int] = None) -> torch.Tensor:
     """Per-(device, stream) decode workspace (split-K partial records) of >= nbytes.
 
     Calls on one stream are ordered, so sharing one workspace per stream is
     race-free; the caching allocator keeps a replaced buffer alive until the
     work queued on that stream has used it.
     """
-    key = (device.index, _stream(device))
+    key = (device.index, _stream(device) if stream is None else stream)
     with _ws_lock:
         buf = _ws_cache.get(key)
         if buf is None or buf.numel() < nbytes:
@@ -227,15 +234,17 @@ def decode(q: torch.Tensor, kp, vp, ks, vs, kb, vb, *, scale: float, bits: int, 
     B, Hq, qL, D = q.shape
     _, Hkv, N, _ = kp.shape
     dev = q.device
-    p = DecodeParams()
-    p.q = q.data_ptr(); p.q_sb = q.stride(0); p.q_sh = q.stride(1)
-    p.k_packed = kp.data_ptr(); p.kp_sb = kp.stride(0); p.kp_sh = kp.stride(1)
-    p.v_packed = vp.data_ptr(); p.vp_sb = vp.stride(0); p.vp_sh = vp.stride(1)
-    p.k_scales = ks.data_ptr(); p.ks_sb = ks.stride(0); p.ks_sh = ks.stride(1)
-    p.v_scales = vs.data_ptr(); p.vs_sb = vs.stride(0); p.vs_sh = vs.stride(1)
+    stream = _stream(dev)
+    qs, kps, vps, kss, vss = q.stride(), kp.stride(), vp.stride(), ks.stride(), vs.stride()
+    p = DecodeParams(q=q.data_ptr(), q_sb=qs[0], q_sh=qs[1],
+                     k_packed=kp.data_ptr(), kp_sb=kps[0], kp_sh=kps[1],
+                     v_packed=vp.data_ptr(), vp_sb=vps[0], vp_sh=vps[1],
+                     k_scales=ks.data_ptr(), ks_sb=kss[0], ks_sh=kss[1],
+                     v_scales=vs.data_ptr(), vs_sb=vss[0], vs_sh=vss[1])
     if kb is not None:
-        p.k_biases = kb.data_ptr(); p.kb_sb = kb.stride(0); p.kb_sh = kb.stride(1)
-        p.v_biases = vb.data_ptr(); p.vb_sb = vb.stride(0); p.vb_sh = vb.stride(1)
+        kbs, vbs = kb.stride(), vb.stride()
+        p.k_biases = kb.data_ptr(); p.kb_sb = kbs[0]; p.kb_sh = kbs[1]
+        p.v_biases = vb.data_ptr(); p.vb_sb = vbs[0]; p.vb_sh = vbs[1]
     if mask is not None:
         p.mask = mask.data_ptr(); p.mask_kind = mask_kind
         p.m_sb = mask.stride(0) if mask.shape[0] > 1 else 0
@@ -259,18 +268,30 @@ def decode(q: torch.Tensor, kp, vp, ks, vs, kb, vb, *, scale: float, bits: int, 
                     torch.empty((B * Hq, 2), dtype=torch.float32, device=dev))
         p.part_o, p.part_ml = part[0].data_ptr(), part[1].data_ptr()
     ref = ctypes.byref(p)
-    nbytes = lib.qsdpa_decode_workspace_size(ref)
-    if nbytes:
-        ws = workspace(dev, nbytes + 256)
-        p.workspace = _aligned_ptr(ws)
-        p.workspace_bytes = nbytes
     if shard is not None:
         bufs, state, rank, world = shard
         ptrs = (_c_vp * world)(*[int(b) for b in bufs])
-        _check(lib.qsdpa_decode_shard(ref, ptrs, state.data_ptr(), rank, world, _stream(dev)), "qsdpa_decode_shard")
-        return out
-    _check(lib.qsdpa_decode(ref, _stream(dev)), "qsdpa_decode")
-    return out if out_mode == OUT_FINAL else part
+        call = lambda: lib.qsdpa_decode_shard(ref, ptrs, state.data_ptr(), rank, world, stream)  # noqa: E731
+        what = "qsdpa_decode_shard"
+    else:
+        call = lambda: lib.qsdpa_decode(ref, stream)  # noqa: E731
+        what = "qsdpa_decode"
+    # the stream's cached workspace first; the size query only when it is too small
+    ws = _ws_cache.get((dev.index, stream))
+    rc = ERR_WORKSPACE
+    if ws is not None:
+        p.workspace = _aligned_ptr(ws)
+        p.workspace_bytes = ws.numel() - 256
+        rc = call()
+    if rc == ERR_WORKSPACE:
+        nbytes = lib.qsdpa_decode_workspace_size(ref)
+        if nbytes:
+            ws = workspace(dev, nbytes + 256, stream)
+            p.workspace = _aligned_ptr(ws)
+            p.workspace_bytes = nbytes
+        rc = call()
+    _check(rc, what)
+    return out if (out_mode == OUT_FINAL or shard is not None) else part
 
 
 def plan_splits(q, kp, vp, ks, vs, kb, vb, bits: int, group_size: int, splits: int = 0,
