@@ -62,6 +62,31 @@ def test_invalid_args_rejected_without_gpu(lib_path):
     assert lib.qsdpa_quantize(None, None) == -1
 
 
+def test_sharded_step_rejects_bad_arguments_without_gpu(lib_path):
+    """qsdpa_decode_shard checks its own arguments (params, world / rank, the
+    ranks' buffers, out_mode and record buffers) on the host before any launch."""
+    from mlx_qsdpa import _lib
+    lib = _lib.load()
+    bufs = (ctypes.c_void_p * 2)(256, 512)
+    state = ctypes.c_void_p(1024)
+    assert lib.qsdpa_decode_shard(None, bufs, state, 0, 2, None) == -1
+    p = _lib.DecodeParams()
+    p.B, p.Hq, p.Hkv, p.N, p.D, p.bits, p.group_size = 1, 32, 2, 4096, 256, 4, 32
+    p.q = p.k_packed = p.v_packed = p.k_scales = p.v_scales = p.out = 1
+    assert lib.qsdpa_decode_shard(ctypes.byref(p), bufs, state, 0, 2, None) == -1  # no record buffers
+    assert b"part_o" in lib.qsdpa_last_error()
+    p.part_o = p.part_ml = 1
+    p.out_mode = _lib.OUT_PARTIAL
+    assert lib.qsdpa_decode_shard(ctypes.byref(p), bufs, state, 0, 2, None) == -1
+    p.out_mode = _lib.OUT_FINAL
+    assert lib.qsdpa_decode_shard(ctypes.byref(p), bufs, state, 2, 2, None) == -1  # rank out of range
+    assert b"rank" in lib.qsdpa_last_error()
+    assert lib.qsdpa_decode_shard(ctypes.byref(p), bufs, state, 0, 9, None) == -1  # world above 8
+    bad = (ctypes.c_void_p * 2)(256, 520)  # rank 1's buffer not 16-byte aligned
+    assert lib.qsdpa_decode_shard(ctypes.byref(p), bad, state, 0, 2, None) == -1
+    assert b"aligned" in lib.qsdpa_last_error()
+
+
 def test_struct_layout_matches_c(tmp_path):
     """sizeof / offsetof of the C structs equal the ctypes mirrors."""
     from mlx_qsdpa import _lib
