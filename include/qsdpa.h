@@ -30,7 +30,7 @@
 extern "C" {
 #endif
 
-#define QSDPA_ABI_VERSION 2
+#define QSDPA_ABI_VERSION 3
 
 
 /* element types */
@@ -42,7 +42,10 @@ enum {
     QSDPA_MASK_BOOL = 1,     /* uint8/bool, nonzero = key kept */
     QSDPA_MASK_ADD_F16 = 2,  /* additive float16, added to the scaled score */
     QSDPA_MASK_ADD_BF16 = 3, /* additive bfloat16 */
-    QSDPA_MASK_ADD_F32 = 4   /* additive float32 */
+    QSDPA_MASK_ADD_F32 = 4,  /* additive float32 */
+    QSDPA_MASK_CAUSAL = 5    /* no mask array: with qL > 1 query i of a head sees the keys of
+                              * its window up to position len - qL + i (bottom-right aligned);
+                              * with qL <= 1 every key, as no mask */
 };
 
 /* decode output modes */
@@ -140,6 +143,13 @@ typedef struct qsdpa_decode_params {
     int32_t out_mode;   /* QSDPA_OUT_* */
     int32_t kernel;     /* QSDPA_KERNEL_*; a kernel that cannot run the call
                          * is an error (QSDPA_ERR_UNSUPPORTED), not a fallback */
+    /* queries per head (0 or 1: decode).  qL > 1 (at most 16; e.g. the draft
+     * tokens of speculative decoding): q is (B, H_q, qL, D) with each head's
+     * qL rows contiguous (stride D, q_sh = qL * D), out is (B, H_q, qL, D)
+     * contiguous and part_o / part_ml have B * H_q * qL rows; mask_kind must
+     * be QSDPA_MASK_NONE or QSDPA_MASK_CAUSAL, and a causal call runs on the
+     * tcgen05 kernel only */
+    int32_t qL;
 } qsdpa_decode_params;
 
 int qsdpa_decode(const qsdpa_decode_params* p, void* stream);

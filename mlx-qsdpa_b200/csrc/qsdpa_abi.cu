@@ -25,6 +25,7 @@ constexpr int kMaxSplits = 1024;
 constexpr int kMinChunk = 64;  // keys per CTA below which splitting stops paying
 constexpr int kLongChunk = 256;  // keys per CTA from which a second CTA per SM pays off
 constexpr int kMinChunkTc = 128;  // one tile of the tcgen05 kernel
+constexpr int kMaxQL = 16;        // queries per head of one call
 constexpr int kTcMaxChunk = 8192;   // keys per CTA above which the keys are split further
 constexpr int kMmaMaxChunk = 4096;
 // QSDPA_KERNEL_AUTO takes the tcgen05 kernel from this many keys per KV head
@@ -94,10 +95,16 @@ int validate(const qsdpa_decode_params* p) {
         return set_error(QSDPA_ERR_INVALID, "H_q (%d) must be divisible by H_kv (%d)", p->Hq, p->Hkv);
     if (p->dtype != QSDPA_F16 && p->dtype != QSDPA_BF16)
         return set_error(QSDPA_ERR_INVALID, "dtype must be QSDPA_F16 or QSDPA_BF16, got %d", p->dtype);
-    if (p->mask_kind < QSDPA_MASK_NONE || p->mask_kind > QSDPA_MASK_ADD_F32)
+    if (p->mask_kind < QSDPA_MASK_NONE || p->mask_kind > QSDPA_MASK_CAUSAL)
         return set_error(QSDPA_ERR_INVALID, "unknown mask kind %d", p->mask_kind);
-    if ((p->mask_kind != QSDPA_MASK_NONE) != (p->mask != nullptr))
+    if ((p->mask_kind != QSDPA_MASK_NONE && p->mask_kind != QSDPA_MASK_CAUSAL) != (p->mask != nullptr))
         return set_error(QSDPA_ERR_INVALID, "mask pointer and mask_kind disagree");
+    if (p->qL < 0 || p->qL > kMaxQL)
+        return set_error(QSDPA_ERR_INVALID, "qL must be in [0, %d], got %d", kMaxQL, p->qL);
+    if (p->qL > 1 && p->mask_kind != QSDPA_MASK_NONE && p->mask_kind != QSDPA_MASK_CAUSAL)
+        return set_error(QSDPA_ERR_INVALID, "with qL > 1 the mask must be QSDPA_MASK_NONE or QSDPA_MASK_CAUSAL");
+    if (p->qL > 1 && p->q_sh != (int64_t)p->qL * p->D)
+        return set_error(QSDPA_ERR_INVALID, "with qL > 1 each head's query rows must be contiguous (q_sh = qL * D)");
     if ((p->k_biases == nullptr) != (p->v_biases == nullptr))
         return set_error(QSDPA_ERR_INVALID, "pass both biases or neither (symmetric)");
     if (p->out_mode != QSDPA_OUT_FINAL && p->out_mode != QSDPA_OUT_PARTIAL)
@@ -160,6 +167,16 @@ void fill_args(const qsdpa_decode_params* p, DecodeArgs& a) {
     a.G = p->D / p->group_size;
     a.pd = p->D * p->bits / 32;
     a.gqa = p->Hq / p->Hkv;
+    a.causal_qL = 0;
+    if (p->qL > 1) {
+        // every query position is a head row of its own: H_q * qL rows, GQA
+        // groups of gqa * qL rows, rows D elements apart
+        a.Hq = p->Hq * p->qL;
+        a.gqa *= p->qL;
+        a.q_sh = p->D;
+        if (p->mask_kind == QSDPA_MASK_CAUSAL) a.causal_qL = p->qL;
+    }
+    if (a.mask_kind == QSDPA_MASK_CAUSAL) a.mask_kind = QSDPA_MASK_NONE;  // no array to read
     a.out_mode = p->out_mode;
     a.scale_log2 = p->scale * kLog2e;
 }
@@ -182,10 +199,13 @@ int make_plan(const qsdpa_decode_params* p, const DecodeArgs& a, Plan& pl) {
             pl.kern = Kern::Simt;
             break;
         default:
-            pl.kern = tc_ok && p->N >= kAutoTcMinKeys && a.gqa >= kAutoTcMinGqa ? Kern::Tc
-                      : mma_ok                                                      ? Kern::Mma
-                                                                                    : Kern::Simt;
+            pl.kern = tc_ok && (a.causal_qL || (p->N >= kAutoTcMinKeys && a.gqa >= kAutoTcMinGqa)) ? Kern::Tc
+                      : mma_ok                                                                       ? Kern::Mma
+                                                                                                     : Kern::Simt;
     }
+    if (a.causal_qL && pl.kern != Kern::Tc)
+        return set_error(QSDPA_ERR_UNSUPPORTED,
+                         "causal qL > 1 runs on the tcgen05 kernel only (D 128/256, 16-byte aligned K/V rows)");
     pl.use_mma = pl.kern != Kern::Simt;
     pl.heads_per_block = pl.use_mma ? mma_heads_per_block(a) : simt_heads_per_block();
     pl.head_blocks = (a.gqa + pl.heads_per_block - 1) / pl.heads_per_block;

@@ -455,7 +455,7 @@ __device__ __forceinline__ void dequant_chunk(const uint4 w4, uint32_t s2, uint3
     }
 }
 
-template <typename T, int BITS, int D, int GS>
+template <typename T, int BITS, int D, int GS, bool CAUSAL>
 __global__ void __launch_bounds__(kTcThreads, 1)
     decode_tc_kernel(const DecodeArgs a, const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v) {
     using C = TcCfg<BITS, D, GS, Ops<T>::kSplitP>;
@@ -817,6 +817,16 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 for (int h = 0; h < kTcHeads; ++h)
                     if (h < nh) s[h] += mask_offset(a.mask, a.mask_kind, mrow + (int64_t)(hq0 + h) * a.m_sh + tok);
             }
+            if (CAUSAL && valid) {
+                // qL > 1, causal: head row h0 + h is query position (h0 + h) % qL,
+                // which sees the window's keys up to logical position len - qL + position
+                int rel = tok - win.start;
+                if (rel < 0) rel += a.N;
+                const int lim0 = win.len - a.causal_qL;
+#pragma unroll
+                for (int h = 0; h < kTcHeads; ++h)
+                    if (rel > lim0 + (h0 + h) % a.causal_qL) s[h] = -INFINITY;
+            }
             bool up = false;
 #pragma unroll
             for (int h = 0; h < kTcHeads; ++h) up |= s[h] > m_run[h] + kRescaleTc;
@@ -1073,14 +1083,17 @@ int encode_rows(CUtensorMap* m, const void* base, int64_t sb_words, int64_t sh_w
 template <typename T, int BITS, int D, int GS>
 int launch_tc4(const DecodeArgs& a, cudaStream_t st) {
     using C = TcCfg<BITS, D, GS, Ops<T>::kSplitP>;
-    auto kern = decode_tc_kernel<T, BITS, D, GS>;
-    static bool attr_set[64] = {};
+    // the causal multi-query variant is a separate instantiation, so the
+    // decode kernel's code is not touched by it
+    const bool causal = a.causal_qL != 0;
+    auto kern = causal ? decode_tc_kernel<T, BITS, D, GS, true> : decode_tc_kernel<T, BITS, D, GS, false>;
+    static bool attr_set[2][64] = {};
     int dev = 0;
     cudaGetDevice(&dev);
-    if (dev >= 0 && dev < 64 && !attr_set[dev]) {
+    if (dev >= 0 && dev < 64 && !attr_set[causal][dev]) {
         cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
         if (e != cudaSuccess) return set_error(QSDPA_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
-        attr_set[dev] = true;
+        attr_set[causal][dev] = true;
     }
     CUtensorMap tm_k, tm_v;
     memset(&tm_k, 0, sizeof(tm_k));

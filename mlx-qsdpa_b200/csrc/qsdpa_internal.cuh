@@ -89,6 +89,10 @@ struct DecodeArgs {
     int head_blocks;  // query-head blocks per GQA group
     int heads_per_block;
     int splits, chunk, out_mode;
+    // qL > 1 with a causal mask: the query position of head row r is r % causal_qL
+    // and it sees the window's keys up to logical position len - causal_qL + i
+    // (0: no per-row limit)
+    int causal_qL;
     float scale_log2;  // scale * log2(e)
 };
 

@@ -20,11 +20,11 @@ _HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.environ.get("QSDPA_LIB") or os.path.join(_HERE, "libqsdpa.so")
 
 QSDPA_F16, QSDPA_BF16 = 0, 1
-MASK_NONE, MASK_BOOL, MASK_ADD_F16, MASK_ADD_BF16, MASK_ADD_F32 = 0, 1, 2, 3, 4
+MASK_NONE, MASK_BOOL, MASK_ADD_F16, MASK_ADD_BF16, MASK_ADD_F32, MASK_CAUSAL = 0, 1, 2, 3, 4, 5
 OUT_FINAL, OUT_PARTIAL = 0, 1
 ERR_WORKSPACE = -3  # QSDPA_ERR_WORKSPACE: workspace missing or too small
 KERNEL_AUTO, KERNEL_TCGEN05, KERNEL_MMA, KERNEL_SIMT = 0, 1, 2, 3
-ABI_VERSION = 2
+ABI_VERSION = 3
 
 _c_i32 = ctypes.c_int32
 _c_i64 = ctypes.c_int64
@@ -49,7 +49,7 @@ class DecodeParams(ctypes.Structure):
         ("B", _c_i32), ("Hq", _c_i32), ("Hkv", _c_i32), ("N", _c_i32), ("D", _c_i32),
         ("bits", _c_i32), ("group_size", _c_i32), ("dtype", _c_i32),
         ("scale", ctypes.c_float), ("splits", _c_i32), ("out_mode", _c_i32),
-        ("kernel", _c_i32),
+        ("kernel", _c_i32), ("qL", _c_i32),
     ]
 
 
@@ -246,9 +246,12 @@ def decode(q: torch.Tensor, kp, vp, ks, vs, kb, vb, *, scale: float, bits: int, 
         p.k_biases = kb.data_ptr(); p.kb_sb = kbs[0]; p.kb_sh = kbs[1]
         p.v_biases = vb.data_ptr(); p.vb_sb = vbs[0]; p.vb_sh = vbs[1]
     if mask is not None:
-        p.mask = mask.data_ptr(); p.mask_kind = mask_kind
+        p.mask = mask.data_ptr()
         p.m_sb = mask.stride(0) if mask.shape[0] > 1 else 0
         p.m_sh = mask.stride(1) if mask.shape[1] > 1 else 0
+    p.mask_kind = mask_kind
+    if qL > 1:
+        p.qL = qL  # q rows of a head must be contiguous: q_sh = qL * D (checked by the library)
     if kv_len is not None:
         p.kv_len = kv_len.data_ptr()
         p.kv_start = _ptr(kv_start)
@@ -260,12 +263,12 @@ def decode(q: torch.Tensor, kp, vp, ks, vs, kb, vb, *, scale: float, bits: int, 
     p.kernel = int(kernel)
     if out_mode == OUT_FINAL:
         if out is None:
-            out = torch.empty((B, Hq, 1, D), dtype=q.dtype, device=dev)
+            out = torch.empty((B, Hq, qL, D), dtype=q.dtype, device=dev)
         p.out = out.data_ptr()
     if shard is not None or out_mode != OUT_FINAL:
         if part is None:
-            part = (torch.empty((B * Hq, D), dtype=torch.float32, device=dev),
-                    torch.empty((B * Hq, 2), dtype=torch.float32, device=dev))
+            part = (torch.empty((B * Hq * qL, D), dtype=torch.float32, device=dev),
+                    torch.empty((B * Hq * qL, 2), dtype=torch.float32, device=dev))
         p.part_o, p.part_ml = part[0].data_ptr(), part[1].data_ptr()
     ref = ctypes.byref(p)
     if shard is not None:

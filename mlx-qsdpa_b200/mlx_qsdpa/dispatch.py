@@ -9,9 +9,13 @@ B200 kernels can do more:
   row), a boolean or additive mask of shape (B|1, H_q|1, 1, N), or a
   :class:`KVRanges` key window -> one fused decode launch (the reference
   sends every masked call to the dequantise fallback, dispatch.py:68).
-* qL > 1, other mask shapes, or a head dim outside {32, 64, 128, 256} ->
-  GPU dequantise kernel + ``torch.nn.functional.scaled_dot_product_attention``
-  (the reference's fallback, dispatch.py:68-83).
+* 1 < qL <= 16 with no mask or ``"causal"`` (e.g. speculative decoding's
+  draft tokens) -> the fused path with every query position as a head row of
+  its own (causal: the tcgen05 kernel; the reference takes its fallback).
+* larger qL, other masks with qL > 1, other mask shapes, or a head dim
+  outside {32, 64, 128, 256} -> GPU dequantise kernel +
+  ``torch.nn.functional.scaled_dot_product_attention`` (the reference's
+  fallback, dispatch.py:68-83).
 * ``threshold``: N <= threshold runs the keys of each KV head in a single CTA
   (the reference's single-pass kernel); larger N splits the keys over enough
   CTAs to fill the GPU and merges the partials in the same launch.  The
@@ -109,6 +113,9 @@ def _fused_mask(mask, B, H_q, N, device):
 
 class _NotFusable(Exception):
     pass
+
+
+_MAX_FUSED_QL = 16  # queries per head the fused path takes (qsdpa_decode_params.qL)
 
 
 def _causal_bool(qL: int, N: int, device) -> torch.Tensor:
@@ -212,6 +219,20 @@ def quantized_sdpa(
     if k_biases is None or v_biases is None:
         k_biases = v_biases = None
 
+    if 1 < qL <= _MAX_FUSED_QL and (mask is None or (isinstance(mask, str) and mask == "causal")):
+        # a few queries per head (speculative decoding's draft tokens): every
+        # query position is fused as a head row of its own, on the
+        # tensor-core kernels; other shapes take the reference's fallback
+        try:
+            return _lib.decode(
+                q.contiguous(), _lib.rows_contiguous(packed_k), _lib.rows_contiguous(packed_v),
+                _lib.rows_contiguous(k_scales), _lib.rows_contiguous(v_scales),
+                _lib.rows_contiguous(k_biases) if k_biases is not None else None,
+                _lib.rows_contiguous(v_biases) if v_biases is not None else None,
+                scale=scale, bits=bits, group_size=group_size,
+                mask_kind=_lib.MASK_CAUSAL if mask is not None else _lib.MASK_NONE)
+        except NotImplementedError:
+            pass
     if qL > 1 or D not in (32, 64, 128, 256):
         return dequant_sdpa(q, packed_k, packed_v, k_scales, v_scales, k_biases, v_biases, scale,
                             mask, bits, group_size)

@@ -41,7 +41,7 @@ def test_library_exports_every_declared_symbol(lib_path):
     for fn in declared_functions():
         assert hasattr(lib, fn), f"{fn} missing from {lib_path}"
     lib.qsdpa_abi_version.restype = ctypes.c_int
-    assert lib.qsdpa_abi_version() == 2
+    assert lib.qsdpa_abi_version() == 3
     lib.qsdpa_last_error.restype = ctypes.c_char_p
     assert lib.qsdpa_last_error() == b""
 

@@ -206,3 +206,55 @@ def test_small_gqa_groups(lib, shape, bits, gs):
     check(lib, c, cap=cap)
     check(lib, c, splits=1, cap=cap)
     check(lib, c, kernel=lib.KERNEL_MMA, cap=cap)
+
+
+@pytest.mark.parametrize("qL,causal,N", [(4, True, 3000), (2, True, 129), (8, True, 700), (16, True, 1000),
+                                         (4, False, 2000), (3, True, 2500)])
+@pytest.mark.parametrize("splits", [0, 1])
+def test_multi_query(lib, qL, causal, N, splits):
+    """qL > 1 queries per head (qsdpa_decode_params.qL): each query position
+    is a head row of its own; with QSDPA_MASK_CAUSAL query i of qL sees the
+    keys up to N - qL + i (bottom-right aligned, as MLX's "causal")."""
+    from qsdpa_testlib import normal, to_torch
+    c = Case(1, 16, 2, N, 256, seed=qL * 100 + N)
+    qn = normal(np.random.default_rng(qL + N), (1, 16, qL, 256), c.dtype)
+    ref = O.sdpa(qn, c.k, c.v, mask="causal" if causal else None, dtype=c.dtype)
+    _, pk, pv, ks, vs, kb, vb = c.torch_args()
+    out = lib.decode(to_torch(qn, c.dtype), pk, pv, ks, vs, kb, vb, scale=256 ** -0.5, bits=4, group_size=32,
+                     splits=splits, kernel=lib.KERNEL_TCGEN05,
+                     mask_kind=lib.MASK_CAUSAL if causal else lib.MASK_NONE)
+    torch.cuda.synchronize()
+    assert tuple(out.shape) == (1, 16, qL, 256)
+    assert_close(from_torch(out), ref, what=f"qL={qL} causal={causal}")
+
+
+def test_multi_query_other_kernels(lib):
+    """Without a mask every kernel takes qL > 1 (more head rows); a causal
+    call on the mma.sync kernel is reported as unsupported."""
+    from qsdpa_testlib import normal, to_torch
+    c = Case(2, 8, 2, 900, 128, seed=5)
+    qn = normal(np.random.default_rng(5), (2, 8, 4, 128), c.dtype)
+    _, pk, pv, ks, vs, kb, vb = c.torch_args()
+    q = to_torch(qn, c.dtype)
+    cap = 1024
+    pk, pv, ks, vs, kb, vb = (padded(x, cap) for x in (pk, pv, ks, vs, kb, vb))
+    out = lib.decode(q, pk, pv, ks, vs, kb, vb, scale=128 ** -0.5, bits=4, group_size=32, kernel=lib.KERNEL_MMA)
+    torch.cuda.synchronize()
+    assert_close(from_torch(out), O.sdpa(qn, c.k, c.v, dtype=c.dtype), what="mma qL=4")
+    with pytest.raises(NotImplementedError, match="causal"):
+        lib.decode(q, pk, pv, ks, vs, kb, vb, scale=128 ** -0.5, bits=4, group_size=32, kernel=lib.KERNEL_MMA,
+                   mask_kind=lib.MASK_CAUSAL)
+
+
+def test_multi_query_public_api(lib):
+    """quantized_sdpa with qL > 1 and mask="causal" takes the fused path and
+    matches the oracle (the reference answers through dequantise + SDPA)."""
+    import mlx_qsdpa
+    from qsdpa_testlib import normal, to_torch
+    c = Case(1, 32, 2, 5000, 256, seed=21)
+    qn = normal(np.random.default_rng(21), (1, 32, 4, 256), c.dtype)
+    _, pk, pv, ks, vs, kb, vb = c.torch_args()
+    out = mlx_qsdpa.quantized_sdpa(to_torch(qn, c.dtype), pk, pv, ks, vs, kb, vb, mask="causal", bits=4,
+                                   group_size=32)
+    torch.cuda.synchronize()
+    assert_close(from_torch(out), O.sdpa(qn, c.k, c.v, mask="causal", dtype=c.dtype), what="public qL=4")
