@@ -2,14 +2,16 @@
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
-Workload (BASELINE.json configs 2 and 5): one decode-attention step of a
+Workload (headline configurations 2 and 5): one decode-attention step of a
 B=1, H_q=32, H_kv=2, D=256, 4-bit gs=32 (with biases) quantized KV cache.  Each
 GPU holds a 131,072-token shard of the context (weak scaling: the context is
 N_gpus x 128K; at 8 GPUs that is the 1,048,576-token config), for 12
 independent layers; step i attends over layer i % 12, so consecutive steps
 read 12 x 84 MB of distinct KV (far larger than the 126 MB L2) and no step
 finds its KV in L2.  With N > 1 each rank computes a partial record over its
-shard, the records are all-gathered over NCCL and merged on every rank.
+shard and the ranks' records are merged over NVLink peer memory in the same
+call (qsdpa_decode_shard; --collective nccl: an NCCL all-gather and a merge
+kernel instead).
 
 K/V are synthetic fp16 ~N(0,1) quantized on the GPU by the library's own
 quantize kernel; q ~N(0,1).  The JSON line reports device time per step (max

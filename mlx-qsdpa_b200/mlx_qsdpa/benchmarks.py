@@ -211,7 +211,7 @@ def config4(steps=64, seed=0):
 
 
 def main(argv=None):
-    ap = argparse.ArgumentParser(description="decode benchmarks of BASELINE configs 2-4")
+    ap = argparse.ArgumentParser(description="decode benchmarks of configurations 2-4")
     ap.add_argument("--config", type=int, choices=[2, 3, 4], required=True)
     ap.add_argument("--kernel", choices=list(KERNELS), default="auto")
     ap.add_argument("--peak-gbs", type=float, default=None, help="HBM peak for frac_of_peak")

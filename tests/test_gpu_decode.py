@@ -117,7 +117,7 @@ def test_32k_context(qs):
 
 
 def test_config3_bf16_8bit_non_gqa(qs):
-    # BASELINE config 3 shape at a size the oracle finishes quickly
+    # config-3 shape (non-GQA, 8-bit) at a size the oracle finishes quickly
     c = Case(1, 8, 8, 2048, 128, bits=8, gs=64, dtype=O.BF16, kv_std=0.5, seed=11)
     check(qs, c)
     c = Case(1, 8, 8, 2048, 128, bits=4, gs=128, dtype=O.BF16, kv_std=0.5, symmetric=True, seed=12)
