@@ -62,6 +62,31 @@ def test_invalid_args_rejected_without_gpu(lib_path):
     assert lib.qsdpa_quantize(None, None) == -1
 
 
+def test_multi_query_arguments_checked_without_gpu(lib_path):
+    """qL > 1: at most 16 queries per head, only QSDPA_MASK_NONE / _CAUSAL,
+    each head's query rows contiguous (q_sh = qL * D); checked on the host."""
+    from mlx_qsdpa import _lib
+    lib = _lib.load()
+    p = _lib.DecodeParams()
+    p.B, p.Hq, p.Hkv, p.N, p.D, p.bits, p.group_size = 1, 32, 2, 4096, 256, 4, 32
+    p.q = p.k_packed = p.v_packed = p.k_scales = p.v_scales = p.out = 1
+    p.qL, p.q_sh = 17, 17 * 256
+    assert lib.qsdpa_decode(ctypes.byref(p), None) == -1
+    assert b"qL" in lib.qsdpa_last_error()
+    p.qL, p.q_sh = 4, 256  # rows of a head not contiguous
+    assert lib.qsdpa_decode(ctypes.byref(p), None) == -1
+    assert b"contiguous" in lib.qsdpa_last_error()
+    p.q_sh = 4 * 256
+    p.mask, p.mask_kind = 1, _lib.MASK_BOOL  # mask arrays are for qL = 1
+    assert lib.qsdpa_decode(ctypes.byref(p), None) == -1
+    p.mask, p.mask_kind = None, _lib.MASK_CAUSAL
+    p.kernel = _lib.KERNEL_SIMT  # causal rows run on the tcgen05 kernel only
+    assert lib.qsdpa_decode(ctypes.byref(p), None) == -2
+    assert b"causal" in lib.qsdpa_last_error()
+    p.mask, p.mask_kind = 1, _lib.MASK_CAUSAL  # the causal kind takes no array
+    assert lib.qsdpa_decode(ctypes.byref(p), None) == -1
+
+
 def test_sharded_step_rejects_bad_arguments_without_gpu(lib_path):
     """qsdpa_decode_shard checks its own arguments (params, world / rank, the
     ranks' buffers, out_mode and record buffers) on the host before any launch."""
