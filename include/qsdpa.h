@@ -269,8 +269,8 @@ int qsdpa_shard_merge(const float* rec, float* const* bufs, unsigned int* state,
  * Sequence-sharded decode step in one call (no reference counterpart): this
  * rank's decode over its key shard followed by the merge with the other
  * ranks, over the same buffers and step counter as qsdpa_shard_merge.  `p`
- * is a qsdpa_decode call with out_mode QSDPA_OUT_FINAL whose `out` receives
- * the merged output (B, H_q, 1, D); `part_o` / `part_ml` must point to this
+ * is a qsdpa_decode call (one query per head: qL 0 or 1) with out_mode
+ * QSDPA_OUT_FINAL whose `out` receives the merged output (B, H_q, 1, D); `part_o` / `part_ml` must point to this
  * rank's record buffers (B*H_q x D and B*H_q x 2 fp32), which hold the record
  * when the keys are not split.  When they are split, one kernel merges the
  * split records of each 64-dim slice, stores the slice to every rank and

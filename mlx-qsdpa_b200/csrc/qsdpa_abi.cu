@@ -338,6 +338,8 @@ extern "C" int qsdpa_decode_shard(const qsdpa_decode_params* p, float* const* bu
     if (p->out_mode != QSDPA_OUT_FINAL || !p->out || !p->part_o || !p->part_ml)
         return set_error(QSDPA_ERR_INVALID,
                          "qsdpa_decode_shard: out_mode must be QSDPA_OUT_FINAL with out, part_o and part_ml set");
+    if (p->qL > 1)  // the peer buffers hold B * H_q rows
+        return set_error(QSDPA_ERR_INVALID, "qsdpa_decode_shard: one query per head (qL 0 or 1), got qL %d", p->qL);
     int rc = check_shard_args(bufs, state, rank, world, p->B * p->Hq, p->D, p->dtype, "qsdpa_decode_shard");
     if (rc) return rc;
     // the decode writes this rank's record: split records into the workspace,

@@ -107,6 +107,10 @@ def test_sharded_step_rejects_bad_arguments_without_gpu(lib_path):
     assert lib.qsdpa_decode_shard(ctypes.byref(p), bufs, state, 2, 2, None) == -1  # rank out of range
     assert b"rank" in lib.qsdpa_last_error()
     assert lib.qsdpa_decode_shard(ctypes.byref(p), bufs, state, 0, 9, None) == -1  # world above 8
+    p.qL, p.q_sh = 4, 4 * 256  # the peer buffers hold one query per head
+    assert lib.qsdpa_decode_shard(ctypes.byref(p), bufs, state, 0, 2, None) == -1
+    assert b"qL" in lib.qsdpa_last_error()
+    p.qL, p.q_sh = 0, 0
     bad = (ctypes.c_void_p * 2)(256, 520)  # rank 1's buffer not 16-byte aligned
     assert lib.qsdpa_decode_shard(ctypes.byref(p), bad, state, 0, 2, None) == -1
     assert b"aligned" in lib.qsdpa_last_error()
