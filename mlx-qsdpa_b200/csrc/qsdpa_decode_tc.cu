@@ -622,7 +622,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         tmem_alloc(smem_u32(tmem_slot), kTmemCols);
         tmem_relinquish();
     }
-    if (warp != kProdWarp) grid_dep_wait();  // before any global read or write    tc_fence_before();
+    if (warp != kProdWarp) grid_dep_wait();  // before any global read or write
+    tc_fence_before();
     __syncthreads();
     tc_fence_after();
     const uint32_t tbase = *tmem_slot;

@@ -26,6 +26,7 @@ namespace {
 
 constexpr size_t kScratchBytes = QSDPA_NOALLOC_SCRATCH_BYTES;
 constexpr int kMaxDevices = 64;
+constexpr int kMaxSplits = 1024;  // qsdpa_decode's limit on splits
 
 // The scratch itself.  In host code this name is only a handle for
 // cudaGetSymbolAddress, never a device address.
@@ -74,12 +75,25 @@ extern "C" int qsdpa_decode_noalloc(const qsdpa_decode_params* p, void* stream) 
                                     "qsdpa_decode_noalloc: %d splits need %zu bytes of scratch; the fixed array "
                                     "holds %zu (ask for fewer splits, or 0 for automatic)",
                                     p->splits, need, kScratchBytes);
-        // automatic: the largest split count whose records fit the array
-        const size_t per_split = (size_t)p->B * p->Hq * ((size_t)p->D + 2) * sizeof(float);
-        int s = static_cast<int>((kScratchBytes - 512) / per_split);
+        // automatic: the largest split count whose records fit the array.  Every
+        // query position is a record row of its own (B * H_q * qL rows).
+        const size_t rows = (size_t)p->B * p->Hq * (size_t)(p->qL > 1 ? p->qL : 1);
+        const size_t per_split = rows * ((size_t)p->D + 2) * sizeof(float);
+        size_t guess = (kScratchBytes - 512) / per_split;
+        if (guess > (size_t)(splits - 1)) guess = (size_t)(splits - 1);
+        if (guess > (size_t)kMaxSplits) guess = (size_t)kMaxSplits;
+        int s = static_cast<int>(guess);
         while (s > 1) {
             q.splits = s;
             need = qsdpa_decode_workspace_size(&q);
+            if (need == 0) {
+                // 0 is either a plan that needs no scratch (the chunks rounded
+                // up to whole tiles leave one split) or a rejected call, which
+                // must not pass as a fit
+                const int rc = qsdpa_decode_splits(&q);
+                if (rc < 0) return rc;
+                break;
+            }
             if (need <= kScratchBytes) break;
             --s;
         }

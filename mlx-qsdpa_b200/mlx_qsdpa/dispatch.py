@@ -214,10 +214,18 @@ def quantized_sdpa(
     if scale is None:
         scale = D ** -0.5
 
-    # The reference treats the cache as symmetric unless both biases are given
-    # (dispatch.py:89-94).
-    if k_biases is None or v_biases is None:
-        k_biases = v_biases = None
+    if (k_biases is None) != (v_biases is None):
+        if mask is None and qL == 1:
+            # the reference's decode path treats the cache as symmetric unless
+            # both biases are given (dispatch.py:89-94)
+            k_biases = v_biases = None
+        elif k_biases is None:
+            # every other call takes the reference's fallback, which
+            # dequantises K and V each with its own bias, zero where it is
+            # None (dispatch.py:68-78)
+            k_biases = torch.zeros_like(k_scales)
+        else:
+            v_biases = torch.zeros_like(v_scales)
 
     if 1 < qL <= _MAX_FUSED_QL and (mask is None or (isinstance(mask, str) and mask == "causal")):
         # a few queries per head (speculative decoding's draft tokens): every

@@ -220,14 +220,20 @@ def sdpa(q, k, v, scale: Optional[float] = None, mask=None, mode: str = "exact",
     if scale is None:
         scale = D ** -0.5
     rep = Hq // Hkv
-    kk = np.repeat(k, rep, axis=1)
-    vv = np.repeat(v, rep, axis=1)
+    kt = np.swapaxes(k, -1, -2)
+
+    def qk(qq):
+        # the rep query heads of a KV head share its keys: one (rep*qL, D) x
+        # (D, N) product per (b, kv head), in float64
+        g = qq.reshape(B, Hkv, rep * qL, D) @ kt
+        return g.reshape(B, Hq, qL, N)
+
     if mode == "mlx":
         s_t = float(round_to(np.asarray([scale], np.float32), dtype)[0])
         qs = round_to(q * s_t, dtype).astype(np.float64)
-        scores = round_to(np.einsum("bhqd,bhnd->bhqn", qs, kk), dtype).astype(np.float64)
+        scores = round_to(qk(qs), dtype).astype(np.float64)
     else:
-        scores = np.einsum("bhqd,bhnd->bhqn", q, kk) * float(scale)
+        scores = qk(q) * float(scale)
     keep = np.ones(scores.shape, dtype=bool)
     if isinstance(mask, str):
         if mask != "causal":
@@ -250,7 +256,7 @@ def sdpa(q, k, v, scale: Optional[float] = None, mask=None, mode: str = "exact",
     p = e / np.where(l > 0, l, 1.0)
     if mode == "mlx":
         p = round_to(p, dtype).astype(np.float64)
-    out = np.einsum("bhqn,bhnd->bhqd", p, vv)
+    out = (p.reshape(B, Hkv, rep * qL, N) @ v).reshape(B, Hq, qL, D)
     out = np.where(empty, 0.0, out)
     if mode == "mlx":
         out = round_to(out, dtype).astype(np.float64)

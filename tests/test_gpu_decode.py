@@ -148,6 +148,31 @@ def test_one_bias_none_means_symmetric(qs):
     assert_close(out, O.sdpa(c.q, k0, v0))
 
 
+@pytest.mark.parametrize("missing", ["k", "v"])
+@pytest.mark.parametrize("route", ["bool_mask_qL1", "causal_qL1", "causal_qL4", "no_mask_qL4"])
+def test_one_bias_none_outside_decode_is_per_tensor(qs, missing, route):
+    """Every call the reference sends to its fallback (any mask, or qL > 1)
+    dequantises K and V each with its own bias, zero only for the one that is
+    None (dispatch.py:68-78); only unmasked qL = 1 goes fully symmetric."""
+    c = Case(1, 8, 2, 96, 128, seed=9)
+    qL = 4 if route.endswith("qL4") else 1
+    if qL > 1:
+        c.q = O.round_to(np.random.default_rng(90).standard_normal((1, 8, qL, 128)).astype(np.float32), O.F16)
+    q, pk, pv, ks, vs, kb, vb = c.torch_args()
+    mask_np = None
+    mask_t = None
+    if route == "bool_mask_qL1":
+        mask_np = np.random.default_rng(91).random((1, 1, 1, 96)) < 0.7
+        mask_t = torch.from_numpy(mask_np).cuda()
+    elif route.startswith("causal"):
+        mask_np = mask_t = "causal"
+    kbias, vbias = (None, vb) if missing == "k" else (kb, None)
+    out = from_torch(qs.quantized_sdpa(q, pk, pv, ks, vs, kbias, vbias, bits=4, group_size=32, mask=mask_t))
+    k_ref = O.dequantize(c.pk, c.ks, None if missing == "k" else c.kb, 32, 4, O.F16)
+    v_ref = O.dequantize(c.pv, c.vs, None if missing == "v" else c.vb, 32, 4, O.F16)
+    assert_close(out, O.sdpa(c.q, k_ref, v_ref, mask=mask_np), what=f"{route}, {missing} bias None")
+
+
 # ---- masks ----
 
 def test_bool_mask_per_batch(qs):

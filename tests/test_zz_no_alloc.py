@@ -22,6 +22,8 @@ from qsdpa_testlib import Case, assert_close, from_torch
 torch = pytest.importorskip("torch")
 pytestmark = pytest.mark.gpu
 
+SCRATCH_BYTES = 4 << 20  # QSDPA_NOALLOC_SCRATCH_BYTES in include/qsdpa.h
+
 
 @pytest.fixture(scope="module")
 def lib():
@@ -31,7 +33,7 @@ def lib():
     return _lib
 
 
-def params(_lib, q, pk, pv, ks, vs, kb, vb, out, bits, gs, splits=0):
+def params(_lib, q, pk, pv, ks, vs, kb, vb, out, bits, gs, splits=0, qL=1, mask_kind=0):
     p = _lib.DecodeParams()
     p.q, p.q_sb, p.q_sh = q.data_ptr(), q.stride(0), q.stride(1)
     p.k_packed, p.kp_sb, p.kp_sh = pk.data_ptr(), pk.stride(0), pk.stride(1)
@@ -47,33 +49,76 @@ def params(_lib, q, pk, pv, ks, vs, kb, vb, out, bits, gs, splits=0):
     p.dtype = _lib.dtype_code(q.dtype)
     p.scale = D ** -0.5
     p.splits = splits
+    p.qL = qL
+    p.mask_kind = mask_kind
     return p
 
 
-def noalloc(_lib, c: Case, splits=0):
-    q, pk, pv, ks, vs, kb, vb = c.torch_args()
-    out = torch.full_like(q, float("nan"))
-    p = params(_lib, q, pk, pv, ks, vs, kb, vb, out, c.bits, c.gs, splits)
+def automatic_workspace(_lib, p) -> int:
+    """Bytes qsdpa_decode's automatic split plan would ask for."""
+    return int(_lib.load().qsdpa_decode_workspace_size(ctypes.byref(p)))
+
+
+def call_noalloc(_lib, p):
     stream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
     rc = _lib.load().qsdpa_decode_noalloc(ctypes.byref(p), stream)
     assert rc == 0, _lib.load().qsdpa_last_error().decode()
     torch.cuda.synchronize()
+
+
+def noalloc(_lib, c: Case, splits=0, needs_cap=False):
+    q, pk, pv, ks, vs, kb, vb = c.torch_args()
+    out = torch.full_like(q, float("nan"))
+    p = params(_lib, q, pk, pv, ks, vs, kb, vb, out, c.bits, c.gs, splits)
+    if needs_cap:
+        # the automatic plan's records do not fit the fixed array: the cap runs
+        assert automatic_workspace(_lib, p) > SCRATCH_BYTES
+    call_noalloc(_lib, p)
     with_ws = _lib.decode(q, pk, pv, ks, vs, kb, vb, scale=c.D ** -0.5, bits=c.bits, group_size=c.gs)
     torch.cuda.synchronize()
     return from_torch(out), from_torch(with_ws)
 
 
 def test_noalloc_matches_decode_on_two_calls_in_a_row(lib):
-    # four batch rows of the GQA-16 heads: the default split count would need
-    # more split records than the fixed array holds, so it is capped
-    first = Case(4, 32, 2, 16384, 256, bits=4, gs=32, seed=101)
+    # four batch rows of the GQA-16 heads at 16,000 keys: the automatic split
+    # count needs more split records than the fixed array holds, so it is capped
+    first = Case(4, 32, 2, 16000, 256, bits=4, gs=32, seed=101)
     second = Case(2, 16, 2, 5000, 128, bits=8, gs=64, seed=102)
-    for c in (first, second):
-        got, ref = noalloc(lib, c)
+    for c, cap in ((first, True), (second, False)):
+        got, ref = noalloc(lib, c, needs_cap=cap)
         assert np.all(np.isfinite(got))
         assert_close(got, ref, what="noalloc vs qsdpa_decode")
-    # the second call also against the oracle
-    assert_close(got, second.reference(), what="noalloc vs oracle")
+        assert_close(got, c.reference(), what="noalloc vs oracle")
+
+
+def test_noalloc_multi_query_cap(lib):
+    # 16 causal query positions per head: B * H_q * qL = 1,024 record rows,
+    # whose automatic plan needs more than the array; the capped call must
+    # still match qsdpa_decode, twice in a row
+    B, H, qL, D, N, bits, gs = 8, 8, 16, 128, 65536, 4, 32
+    g = torch.Generator(device="cuda")
+    g.manual_seed(7)
+    pd, G = D * bits // 32, D // gs
+
+    def codes():
+        return torch.randint(0, 2 ** 31 - 1, (B, H, N, pd), generator=g, device="cuda",
+                             dtype=torch.int32).view(torch.uint32)
+
+    def groups(lo, hi):
+        return (torch.rand((B, H, N, G), generator=g, device="cuda") * (hi - lo) + lo).half()
+
+    pk, pv = codes(), codes()
+    ks, vs, kb, vb = groups(0.02, 0.2), groups(0.02, 0.2), groups(-1.5, 0.0), groups(-1.5, 0.0)
+    q = torch.randn((B, H, qL, D), generator=g, device="cuda").half()
+    for _ in range(2):
+        out = torch.full_like(q, float("nan"))
+        p = params(lib, q, pk, pv, ks, vs, kb, vb, out, bits, gs, qL=qL, mask_kind=lib.MASK_CAUSAL)
+        assert automatic_workspace(lib, p) > SCRATCH_BYTES
+        call_noalloc(lib, p)
+        ref = lib.decode(q, pk, pv, ks, vs, kb, vb, scale=D ** -0.5, bits=bits, group_size=gs,
+                         mask_kind=lib.MASK_CAUSAL)
+        torch.cuda.synchronize()
+        assert_close(from_torch(out), from_torch(ref), what="noalloc qL=16 vs qsdpa_decode")
 
 
 def test_noalloc_explicit_split_limits(lib):
