@@ -2,29 +2,34 @@
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
-Workload (headline configurations 2 and 5): one decode-attention step of a
-B=1, H_q=32, H_kv=2, D=256, 4-bit gs=32 (with biases) quantized KV cache.  Each
-GPU holds a 131,072-token shard of the context (weak scaling: the context is
-N_gpus x 128K; at 8 GPUs that is the 1,048,576-token config), for 12
-independent layers; step i attends over layer i % 12, so consecutive steps
-read 12 x 84 MB of distinct KV (far larger than the 126 MB L2) and no step
-finds its KV in L2.  With N > 1 each rank computes a partial record over its
-shard and the ranks' records are merged over NVLink peer memory in the same
-call (qsdpa_decode_shard; --collective nccl: an NCCL all-gather and a merge
-kernel instead).
+Workload (the headline long-context configuration): one decode step of a
+12-layer model whose every attention layer holds a 1,048,576-token quantized
+KV context -- B=1, H_q=32, H_kv=2, D=256, 4-bit gs=32 with biases, fp16 --
+split evenly across the N GPUs (strong scaling: 1M/N tokens of every layer per
+GPU, the same total work at every N).  A step runs the 12 layers' decode
+calls back to back, each with its own query and KV; with N > 1 each call
+computes this rank's partial record and merges it with the other ranks' over
+NVLink peer memory in the same call (qsdpa_decode_shard; --collective nccl: an
+NCCL all-gather and a merge kernel instead).  Consecutive steps read 12 x 671
+MB / N of distinct KV per GPU (far more than the 126 MB L2), so no call finds
+its KV in L2.
 
 K/V are synthetic fp16 ~N(0,1) quantized on the GPU by the library's own
 quantize kernel; q ~N(0,1).  The JSON line reports device time per step (max
 over ranks), the end-to-end time through the public Python API with host
-buffers, the roofline of the decode kernel against the measured HBM peak, the
-CPU baseline (C restatement of the reference's dequantise + SDPA branch) and
-the SM clocks sampled during the timed region.
+buffers, the roofline of the decode call against the measured HBM peak, the
+CPU baseline (C restatement of the reference's dequantise + SDPA branch), the
+SM clocks sampled during the timed region, a correctness check of the timed
+path, and (N=1) the other configurations: the GQA-16 context sweep 1K-128K,
+the non-GQA 8-bit and symmetric 4-bit decode, continuous batching with the
+linear and rotating batch caches, and the CPU-runnable 8K cache_sdpa case.
 """
 
 from __future__ import annotations
 
 import argparse
 import ctypes
+import hashlib
 import json
 import os
 import subprocess
@@ -38,21 +43,24 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, os.path.join(ROOT, "mlx-qsdpa_b200"))
 
 B, HQ, HKV, D, BITS, GS = 1, 32, 2, 256, 4, 32
-CTX_PER_GPU = 131072
+CONTEXT = 1048576
 LAYERS = 12
-METRIC = "decode-attn us/step (GQA-16, D=256, 4-bit gs32, 128K ctx per GPU)"
+METRIC = "decode-attn us/step (12 layers x 1M-token ctx split over the GPUs; GQA-16, D=256, 4-bit gs32)"
+TRAFFIC_RECORD = "profiles/decode_tc_traffic.txt"
 
 
 def parse():
     ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=2000)
-    ap.add_argument("--warmup", type=int, default=50)
+    ap.add_argument("--steps", type=int, default=240)
+    ap.add_argument("--warmup", type=int, default=12)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--ctx", type=int, default=CTX_PER_GPU, help="context tokens per GPU")
+    ap.add_argument("--context", type=int, default=CONTEXT, help="context tokens of every layer (all GPUs)")
     ap.add_argument("--layers", type=int, default=LAYERS)
     ap.add_argument("--no-graph", action="store_true", help="launch eagerly instead of CUDA graphs")
-    ap.add_argument("--cpu-sample-calls", type=int, default=3)
+    ap.add_argument("--cpu-sample-calls", type=int, default=1,
+                    help="layer calls of the CPU baseline sample (0: skip it)")
+    ap.add_argument("--no-extras", action="store_true", help="skip the other configurations (N=1)")
     ap.add_argument("--collective", choices=["p2p", "nccl"], default="p2p",
                     help="N>1: merge the ranks' records over NVLink peer memory or with an NCCL all-gather")
     ap.add_argument("--kernel", choices=list(KERNELS), default="auto",
@@ -61,20 +69,6 @@ def parse():
 
 
 KERNELS = {"auto": 0, "tcgen05": 1, "mma": 2, "simt": 3}
-# kernel the library picks with QSDPA_KERNEL_AUTO for this workload, and the
-# profile summaries (ncu --set full on this workload) giving DRAM traffic
-AUTO_KERNEL = "tcgen05"
-PROFILES = {"mma": "profiles/decode_mma_128k_gqa16.md", "tcgen05": "profiles/decode_tcgen05_128k_gqa16.md"}
-
-
-def profiled_traffic(kernel: str):
-    """DRAM bytes (read + write) of one decode launch from the committed ncu summary."""
-    import re
-    path = os.path.join(ROOT, PROFILES.get(AUTO_KERNEL if kernel == "auto" else kernel, ""))
-    if not os.path.isfile(path):
-        return None, None
-    m = re.search(r"traffic per launch \(dram read \+ write\): ([0-9.]+) MB", open(path).read())
-    return (round(float(m.group(1)) * 1e6), os.path.relpath(path, ROOT)) if m else (None, None)
 
 
 def measured_peaks():
@@ -91,6 +85,34 @@ def algorithmic_bytes(ctx_tokens: int) -> int:
     G = D // GS
     row = D * BITS // 8 + G * 2 * 2
     return 2 * B * HQ * D * 2 + ctx_tokens * B * HKV * 2 * row
+
+
+def lib_md5(path: str) -> str:
+    h = hashlib.md5()
+    with open(path, "rb") as f:
+        for chunk in iter(lambda: f.read(1 << 20), b""):
+            h.update(chunk)
+    return h.hexdigest()
+
+
+def recorded_traffic(lib_path: str, keys: int):
+    """DRAM bytes (read + write) of one decode launch over `keys` keys, from the
+    ncu capture recorded for exactly this build of libqsdpa.so (matched by the
+    library's md5; captured on a smaller context and scaled by the keys per
+    launch, as the kernel's traffic grows in proportion).  None when this
+    build has no capture."""
+    path = os.path.join(ROOT, TRAFFIC_RECORD)
+    if not os.path.isfile(path):
+        return None, "no capture recorded"
+    rec = {}
+    for line in open(path):
+        if ":" in line and not line.startswith("#"):
+            k, v = line.split(":", 1)
+            rec[k.strip()] = v.strip()
+    if rec.get("lib_md5") != lib_md5(lib_path):
+        return None, "no ncu capture of this build"
+    per_key = float(rec["traffic_bytes_per_launch"]) / float(rec["keys_per_launch"])
+    return round(per_key * keys), f"{TRAFFIC_RECORD} (scaled from {rec['keys_per_launch']} keys)"
 
 
 # ------------------------------------------------------------ CPU side ----
@@ -110,7 +132,7 @@ def host_threads() -> int:
 
 
 def cpu_decode_timer(ctx: int, calls: int, seed: int = 0):
-    """Time the C restatement of the reference CPU path on a full-size call.
+    """Time the C restatement of the reference CPU path on one layer's call.
 
     Returns (us per call, threads).  Inputs: quantized codes with random
     scales/biases of the right dtype layout (the branch's cost does not
@@ -231,6 +253,116 @@ def build_layers(torch, dev, ctx, layers, seed):
     return out
 
 
+def gather_layer(torch, dist, layer, world):
+    """Every rank's shard of one layer, concatenated along the tokens (rank order)."""
+    full = []
+    for t in layer[0] + layer[1]:
+        g = torch.empty((world,) + tuple(t.shape[1:]), dtype=t.dtype, device=t.device)
+        src = t.view(torch.int32) if t.dtype == torch.uint32 else t
+        dst = g.view(torch.int32) if g.dtype == torch.uint32 else g
+        dist.all_gather_into_tensor(dst, src.contiguous())
+        # (world, H, n, W) -> (1, H, world * n, W)
+        full.append(g.permute(1, 0, 2, 3).reshape(1, t.shape[1], world * t.shape[2], t.shape[3]))
+    return (full[0], full[1], full[2]), (full[3], full[4], full[5])
+
+
+def extras(torch, peak):
+    """The other configurations on one GPU (rank 0, N=1)."""
+    import mlx_qsdpa
+    from mlx_qsdpa import benchmarks as bm
+    res = {}
+    # configuration 2: the GQA-16 context sweep
+    sweep = []
+    for n in (1024, 4096, 16384, 32768, 65536, 131072):
+        sweep.append(bm.time_decode(1, 32, 2, n, 256, 4, 32, torch.float16, peak_gbs=peak))
+    res["config2_sweep"] = sweep
+    # configuration 3: non-GQA 8-bit bf16 and the symmetric 4-bit gs128 variant
+    c3 = []
+    for n in (16384, 65536, 131072):
+        c3.append({"variant": "8-bit gs64 affine", **bm.time_decode(1, 8, 8, n, 128, 8, 64, torch.bfloat16, std=0.5,
+                                                                     peak_gbs=peak)})
+    for n in (16384, 65536, 131072):
+        c3.append({"variant": "4-bit gs128 symmetric", **bm.time_decode(1, 8, 8, n, 128, 4, 128, torch.bfloat16,
+                                                                         std=0.5, symmetric=True, peak_gbs=peak)})
+    res["config3"] = c3
+    # configuration 4: continuous batching (decode alone, then append + decode steps)
+    res["config4_decode"] = bm.config4_decode("auto", peak, emit=False)
+    res["config4_steps"] = bm.config4(peak=peak, emit=False)
+    torch.cuda.empty_cache()
+    # configuration 1: the 8K cache_sdpa case, on the GPU and with the CPU port
+    dev = torch.device("cuda")
+    g = torch.Generator(device=dev)
+    g.manual_seed(0)
+    cache = mlx_qsdpa.QuantizedSDPACache(bits=4, group_size=32)
+    k = torch.randn((1, 2, 8192, 256), generator=g, device=dev).half()
+    v = torch.randn((1, 2, 8192, 256), generator=g, device=dev).half()
+    kq, vq = cache.update_and_fetch(k, v)
+    q = torch.randn((1, 32, 1, 256), generator=g, device=dev).half()
+    for _ in range(5):
+        mlx_qsdpa.cache_sdpa(q, kq, vq, cache)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(200):
+        mlx_qsdpa.cache_sdpa(q, kq, vq, cache)
+    e1.record()
+    torch.cuda.synchronize()
+    cpu_us, thr = cpu_decode_timer(8192, 20)
+    res["config1"] = {"context": 8192, "gpu_cache_sdpa_us": round(e0.elapsed_time(e1) * 1e3 / 200, 3),
+                      "gpu_note": "eager calls through cache_sdpa (L2-resident: 5.2 MB)",
+                      "cpu_port_us": round(cpu_us, 1), "cpu_cores": thr}
+    return res
+
+
+def batch_sharded(torch, dist, dev, rank, world, steps=64):
+    """Configuration 4 sharded by sequence (N > 1): the 32 sequences of the
+    continuous batch (lengths U[2048, 32768], seed 0) split over the ranks by
+    partition_sequences; each rank appends one token per sequence and decodes
+    its own rows every step, with no collective.  Returns (max over ranks of
+    us per step, this rank's row count)."""
+    import mlx_qsdpa
+    from mlx_qsdpa.sharded import partition_sequences
+    Bc, Hq, Hkv, Dc, bits, gs = 32, 32, 8, 128, 4, 64
+    lens = torch.randint(2048, 32769, (Bc,), generator=torch.Generator().manual_seed(0)).tolist()
+    mine = partition_sequences(lens, world)[rank]
+    g = torch.Generator(device=dev)
+    g.manual_seed(77 + rank)
+    singles = []
+    for i in mine:
+        c = mlx_qsdpa.QuantizedSDPACache(bits=bits, group_size=gs)
+        k = torch.randn((1, Hkv, lens[i], Dc), generator=g, device=dev).half()
+        v = torch.randn((1, Hkv, lens[i], Dc), generator=g, device=dev).half()
+        c.update_and_fetch(k, v)
+        singles.append(c)
+    cache = mlx_qsdpa.BatchQuantizedSDPACache.merge(singles)
+    del singles
+    b = len(mine)
+    news = [(torch.randn((b, Hkv, 1, Dc), generator=g, device=dev).half(),
+             torch.randn((b, Hkv, 1, Dc), generator=g, device=dev).half(),
+             torch.randn((b, Hq, 1, Dc), generator=g, device=dev).half()) for _ in range(steps + 3)]
+
+    def one(i):
+        k, v, q = news[i]
+        kq, vq = cache.update_and_fetch(k, v)
+        mlx_qsdpa.cache_sdpa(q, kq, vq, cache, mask=cache.kv_ranges())
+
+    for i in range(3):
+        one(i)
+    torch.cuda.synchronize(dev)
+    dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for i in range(steps):
+        one(3 + i)
+    e1.record()
+    torch.cuda.synchronize(dev)
+    t = torch.tensor([e0.elapsed_time(e1) * 1e3 / steps], dtype=torch.float64, device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    del cache, news
+    torch.cuda.empty_cache()
+    return float(t.item()), b
+
+
 def main():
     args = parse()
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -252,87 +384,89 @@ def main():
     from mlx_qsdpa import _lib
     from mlx_qsdpa.sharded import PeerExchange, sharded_quantized_sdpa
 
-    ctx = args.ctx
+    if args.context % world:
+        raise SystemExit(f"--context {args.context} is not divisible by {world} GPUs")
+    ctx = args.context // world
     L = args.layers
     layers = build_layers(torch, dev, ctx, L, seed=1234 + rank)
+    # one query per layer, the same on every rank
     gq = torch.Generator(device=dev)
     gq.manual_seed(99)
-    q = torch.randn((B, HQ, 1, D), generator=gq, device=dev).to(torch.float16)
+    qs = [torch.randn((B, HQ, 1, D), generator=gq, device=dev).to(torch.float16) for _ in range(L)]
     scale = D ** -0.5
     stream = torch.cuda.current_stream(dev)
 
     exchange = None
+    rows = B * HQ
     if world > 1:
-        # one packed record per rank, [o (rows x D) | m, l (rows x 2)]: one all-gather per step
-        rows = B * HQ
+        # one packed record per rank, [o (rows x D) | m, l (rows x 2)]
         rec = torch.empty(rows * (D + 2), dtype=torch.float32, device=dev)
         part = (rec[: rows * D].view(rows, D), rec[rows * D:].view(rows, 2))
         gath = torch.empty((world, rows * (D + 2)), dtype=torch.float32, device=dev)
         exchange = PeerExchange(rows, D, device=dev) if args.collective == "p2p" else None
 
     outs = [torch.empty((B, HQ, 1, D), dtype=torch.float16, device=dev) for _ in range(L)]
-
     kern_code = KERNELS[args.kernel]
 
-    def step(i):
-        (pk, ks, kb), (pv, vs, vb) = layers[i % L]
+    def layer_call(l):
+        (pk, ks, kb), (pv, vs, vb) = layers[l]
         if world == 1:
-            _lib.decode(q, pk, pv, ks, vs, kb, vb, scale=scale, bits=BITS, group_size=GS, out=outs[i % L],
+            _lib.decode(qs[l], pk, pv, ks, vs, kb, vb, scale=scale, bits=BITS, group_size=GS, out=outs[l],
                         kernel=kern_code)
         elif exchange is not None:
             # decode + merge with the other ranks over peer memory in one call
-            _lib.decode(q, pk, pv, ks, vs, kb, vb, scale=scale, bits=BITS, group_size=GS, out=outs[i % L],
+            _lib.decode(qs[l], pk, pv, ks, vs, kb, vb, scale=scale, bits=BITS, group_size=GS, out=outs[l],
                         part=part, kernel=kern_code, shard=exchange.shard_args())
         else:
-            _lib.decode(q, pk, pv, ks, vs, kb, vb, scale=scale, bits=BITS, group_size=GS,
+            _lib.decode(qs[l], pk, pv, ks, vs, kb, vb, scale=scale, bits=BITS, group_size=GS,
                         out_mode=_lib.OUT_PARTIAL, part=part, kernel=kern_code)
             dist.all_gather_into_tensor(gath, rec)
-            _lib.combine_packed(gath, rows, D, out=outs[i % L].view(rows, D))
+            _lib.combine_packed(gath, rows, D, out=outs[l].view(rows, D))
+
+    def local_call(l):
+        (pk, ks, kb), (pv, vs, vb) = layers[l]
+        _lib.decode(qs[l], pk, pv, ks, vs, kb, vb, scale=scale, bits=BITS, group_size=GS, out=outs[l],
+                    kernel=kern_code)
+
+    def step(fn=layer_call):
+        for l in range(L):
+            fn(l)
 
     # warm-up (also allocates the decode workspace outside any capture)
-    for i in range(max(args.warmup, 3)):
-        step(i)
+    for _ in range(max(args.warmup, 3)):
+        step()
     torch.cuda.synchronize(dev)
 
-    # every CUDA graph lives only in these lists (no loop variable keeps one):
-    # graphs that hold NCCL work must all be gone before destroy_process_group.
-    # A model captures a decode step's layers in one graph; so does the bench:
-    # graphs[0] runs the L layers' steps back to back, graphs[1 + l] layer l
-    # alone (for step counts that are not a multiple of L).
-    graphs = []
+    # A model captures its decode step's layers in one graph; so does the
+    # bench.  Every graph lives only in `graphs` (graphs that hold NCCL work
+    # must all be gone before destroy_process_group).
+    graphs = {}
     graph_note = "eager"
 
-    def capture(fn, into):
-        into.append(torch.cuda.CUDAGraph())
-        with torch.cuda.graph(into[-1]):
-            for l in range(L):
-                fn(l)
-        for l in range(L):
-            into.append(torch.cuda.CUDAGraph())
-            with torch.cuda.graph(into[-1]):
-                fn(l)
-        for g in into:
-            g.replay()
+    def capture(name, fn):
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            step(fn)
+        graphs[name] = g
+        g.replay()
         torch.cuda.synchronize(dev)
 
     if not args.no_graph:
         try:
-            capture(step, graphs)
-            graph_note = f"one cuda graph over the {L} layers' decode steps"
+            capture("step", layer_call)
+            capture("local", local_call)
+            graph_note = f"one cuda graph per step over the {L} layers' decode calls"
         except Exception as e:  # noqa: BLE001
             graphs.clear()
             graph_note = f"eager (graph capture failed: {type(e).__name__})"
 
-    def replay(gl, fn, K):
-        """K steps: whole L-layer graphs, then single layers for the remainder."""
-        if not gl:
-            for i in range(K):
-                fn(i)
-            return
-        for _ in range(K // L):
-            gl[0].replay()
-        for i in range(K % L):
-            gl[1 + i].replay()
+    def run(name, fn, K):
+        if name in graphs:
+            for _ in range(K):
+                graphs[name].replay()
+        else:
+            for _ in range(K):
+                step(fn)
 
     def barrier():
         if world > 1:
@@ -342,39 +476,32 @@ def main():
     # ---- timed region: K steps back to back ----
     K = args.steps
     barrier()
+    # one untimed step right before the start event: its peer exchanges line
+    # the ranks up on the device, so host launch skew is not timed
+    run("step", layer_call, 1)
     with ClockSampler(local) as clk:
         e0 = torch.cuda.Event(enable_timing=True)
         e1 = torch.cuda.Event(enable_timing=True)
         t_host0 = time.time()
         e0.record(stream)
-        replay(graphs, step, K)
+        run("step", layer_call, K)
         e1.record(stream)
         barrier()
         t_host1 = time.time()
     elapsed_ms = e0.elapsed_time(e1)
     clocks = clk.summary(t_host0, t_host1)
 
-    # ---- device duration of one decode-kernel launch (for the roofline) ----
-    # the local decode alone (no collective), captured like the step and
-    # replayed back to back between one pair of events on the launching stream
-    def local_decode(i):
-        (pk, ks, kb), (pv, vs, vb) = layers[i % L]
-        _lib.decode(q, pk, pv, ks, vs, kb, vb, scale=scale, bits=BITS, group_size=GS, out=outs[i % L],
-                    kernel=kern_code)
-
-    kgraphs = []
-    if world == 1:
-        kgraphs = graphs
-    elif graphs:
-        capture(local_decode, kgraphs)
+    # ---- device duration of one decode call (for the roofline): the local
+    # decode alone (no exchange), captured like the step, back to back ----
     barrier()
     k0 = torch.cuda.Event(enable_timing=True)
     k1 = torch.cuda.Event(enable_timing=True)
+    Kk = max(1, min(K, 120))
     k0.record(stream)
-    replay(kgraphs, local_decode, K)
+    run("local", local_call, Kk)
     k1.record(stream)
     barrier()
-    per_launch_ms = k0.elapsed_time(k1) / K
+    per_launch_ms = k0.elapsed_time(k1) / (Kk * L)
 
     t = torch.tensor([elapsed_ms, per_launch_ms], dtype=torch.float64, device=dev)
     if world > 1:
@@ -382,30 +509,33 @@ def main():
     elapsed_ms, per_launch_ms = t.tolist()
     ms_per_step = elapsed_ms / K
 
-    # ---- end to end through the public API with host buffers ----
-    q_host = torch.empty((B, HQ, 1, D), dtype=torch.float16, pin_memory=True)
-    q_host.copy_(q.cpu())
-    out_host = torch.empty((B, HQ, 1, D), dtype=torch.float16, pin_memory=True)
-    Ke = min(K, 120)
+    # ---- end to end through the public API with host buffers: every step
+    # copies the 12 layers' queries in from pinned host memory and their
+    # outputs back ----
+    q_host = torch.empty((L, B, HQ, 1, D), dtype=torch.float16, pin_memory=True)
+    q_host.copy_(torch.stack(qs).cpu())
+    out_host = torch.empty((L, B, HQ, 1, D), dtype=torch.float16, pin_memory=True)
+    Ke = max(1, min(K, 60))
 
-    def e2e_step(i):
+    def e2e_step():
         qd = q_host.to(dev, non_blocking=True)
-        (pk, ks, kb), (pv, vs, vb) = layers[i % L]
-        if world == 1:
-            o = mlx_qsdpa.quantized_sdpa(qd, pk, pv, ks, vs, kb, vb, scale=scale, bits=BITS, group_size=GS)
-        else:
-            o = sharded_quantized_sdpa(qd, (pk, ks, kb), (pv, vs, vb), bits=BITS, group_size=GS, scale=scale,
-                                       exchange=exchange)
-        out_host.copy_(o, non_blocking=True)
+        for l in range(L):
+            (pk, ks, kb), (pv, vs, vb) = layers[l]
+            if world == 1:
+                o = mlx_qsdpa.quantized_sdpa(qd[l], pk, pv, ks, vs, kb, vb, scale=scale, bits=BITS, group_size=GS)
+            else:
+                o = sharded_quantized_sdpa(qd[l], (pk, ks, kb), (pv, vs, vb), bits=BITS, group_size=GS,
+                                           scale=scale, exchange=exchange)
+            out_host[l].copy_(o, non_blocking=True)
 
-    for i in range(3):
-        e2e_step(i)
+    for _ in range(3):
+        e2e_step()
     barrier()
     f0 = torch.cuda.Event(enable_timing=True)
     f1 = torch.cuda.Event(enable_timing=True)
     f0.record(stream)
-    for i in range(Ke):
-        e2e_step(i)
+    for _ in range(Ke):
+        e2e_step()
     f1.record(stream)
     barrier()
     te = torch.tensor([f0.elapsed_time(f1) / Ke], dtype=torch.float64, device=dev)
@@ -413,28 +543,52 @@ def main():
         dist.all_reduce(te, op=dist.ReduceOp.MAX)
     e2e_ms = float(te.item())
 
-    # ---- correctness spot check of the timed path (vs the unsplit single-GPU path) ----
-    check = None
+    # ---- correctness of the timed path (outside the timed region) ----
+    checks = {}
+    ok = True
+    (pk, ks, kb), (pv, vs, vb) = layers[0]
     if world == 1:
-        (pk, ks, kb), (pv, vs, vb) = layers[0]
-        a = _lib.decode(q, pk, pv, ks, vs, kb, vb, scale=scale, bits=BITS, group_size=GS)
-        b = _lib.decode(q, pk, pv, ks, vs, kb, vb, scale=scale, bits=BITS, group_size=GS, splits=7)
-        check = float((a.float() - b.float()).abs().max().item())
+        a = _lib.decode(qs[0], pk, pv, ks, vs, kb, vb, scale=scale, bits=BITS, group_size=GS, kernel=kern_code)
+        b = _lib.decode(qs[0], pk, pv, ks, vs, kb, vb, scale=scale, bits=BITS, group_size=GS, splits=7,
+                        kernel=kern_code)
+        c = _lib.decode(qs[0], pk, pv, ks, vs, kb, vb, scale=scale, bits=BITS, group_size=GS,
+                        kernel=KERNELS["mma"])
+        checks["split_check_max_abs"] = float((a.float() - b.float()).abs().max().item())
+        checks["kernel_check_max_abs"] = float((a.float() - c.float()).abs().max().item())
+        checks["kernel_check"] = "timed kernel vs the mma.sync kernel on layer 0's full context"
+        ok = checks["split_check_max_abs"] <= 2e-3 and checks["kernel_check_max_abs"] <= 2e-3
+    else:
+        # the sharded output of layer 0 (the timed call, run again: the
+        # local-only timing above reused the output buffers) against the
+        # unsharded decode of the whole context (every rank's shard gathered)
+        layer_call(0)
+        sharded = outs[0].clone()
+        kfull, vfull = gather_layer(torch, dist, layers[0], world)
+        ref = _lib.decode(qs[0], kfull[0], vfull[0], kfull[1], vfull[1], kfull[2], vfull[2], scale=scale,
+                          bits=BITS, group_size=GS)
+        err = torch.tensor([float((sharded.float() - ref.float()).abs().max().item())], dtype=torch.float64,
+                           device=dev)
+        dist.all_reduce(err, op=dist.ReduceOp.MAX)
+        checks["shard_check_max_abs"] = float(err.item())
+        checks["shard_check"] = "layer 0: sharded output (max over ranks) vs the unsharded decode of the full context"
+        ok = checks["shard_check_max_abs"] <= 2e-3
+        del kfull, vfull, ref
+
+    batch_us = None
+    if world > 1 and not args.no_extras:
+        batch_us, batch_rows = batch_sharded(torch, dist, dev, rank, world)
 
     if rank == 0:
         peak, peak_kind = measured_peaks()
-        bytes_local = algorithmic_bytes(ctx)
-        achieved = bytes_local / (per_launch_ms * 1e-3) / 1e9
-        (pk0, ks0, kb0), (pv0, vs0, vb0) = layers[0]
-        splits = _lib.plan_splits(q, pk0, pv0, ks0, vs0, kb0, vb0, BITS, GS, kernel=kern_code)
-        traffic, traffic_src = profiled_traffic(args.kernel)
-        # decode (+ split merge); N>1 over peer memory: decode + the fused split merge / exchange /
-        # rank merge (or, keys not split, the exchange-and-merge kernel); over NCCL: + the record
-        # merge after NCCL's all-gather
+        bytes_call = algorithmic_bytes(ctx)
+        achieved = bytes_call / (per_launch_ms * 1e-3) / 1e9
+        splits = _lib.plan_splits(qs[0], pk, pv, ks, vs, kb, vb, BITS, GS, kernel=kern_code)
+        traffic, traffic_src = recorded_traffic(_lib.LIB_PATH, ctx)
+        # per layer call: the decode kernel and the split merge (N>1: the fused
+        # split merge + exchange + rank merge kernel; over NCCL: the record merge)
+        launches_per_call = (1 if splits == 1 else 2) + (1 if (world > 1 and exchange is None) else 0)
         if world > 1 and exchange is not None:
-            launches_per_step = 2
-        else:
-            launches_per_step = (1 if splits == 1 else 2) + (1 if world > 1 else 0)
+            launches_per_call = 2
         line = {
             "metric": METRIC,
             "value": round(ms_per_step * 1e3, 3),
@@ -444,90 +598,104 @@ def main():
             "warmup": args.warmup,
             "ms_per_step": round(ms_per_step, 6),
             "higher_is_better": False,
-            "scaling": "weak",
+            "scaling": "strong",
             "vs_baseline": None,
             "dtype": "f16",
             "data": "synthetic (K/V fp16 ~N(0,1) quantized on device, q ~N(0,1))",
             "config": {
-                "workload": "BASELINE configs 2+5: quantized_sdpa decode, 128K-token KV shard per GPU, "
-                            "context = n_gpus x 128K (1M at 8 GPUs), 12 layers rotated",
+                "workload": f"decode step of {L} attention layers, each over a {args.context:,}-token quantized KV "
+                            f"context split evenly across the GPUs ({ctx:,} tokens per GPU)",
                 "B": B, "H_q": HQ, "H_kv": HKV, "D": D, "bits": BITS, "group_size": GS, "biases": True,
-                "context_per_gpu": ctx, "context_total": ctx * world, "layers": L,
-                "l2": "inputs larger than L2: 12 layers x %.1f MB rotated" % (bytes_local / 1e6),
+                "context_total": args.context, "context_per_gpu": ctx, "layers": L,
+                "l2": "inputs larger than L2: %d layers x %.1f MB distinct KV per GPU per step" % (L, bytes_call / 1e6),
                 "launch": graph_note, "splits": splits,
-                "kernel": AUTO_KERNEL if args.kernel == "auto" else args.kernel,
-                "parallelism": (f"sequence-sharded, records merged over {'NVLink peer memory' if args.collective == 'p2p' else 'NCCL all-gather'}"
+                "kernel": {0: "auto", 1: "tcgen05", 2: "mma", 3: "simt"}[_lib.plan_kernel(
+                    qs[0], pk, pv, ks, vs, kb, vb, BITS, GS, kernel=kern_code)],
+                "parallelism": (f"sequence-sharded over {world} GPUs, records merged over "
+                                f"{'NVLink peer memory' if args.collective == 'p2p' else 'NCCL all-gather'}"
                                 if world > 1 else "single GPU"),
             },
+            "per_layer_us": round(ms_per_step * 1e3 / L, 3),
             "gbs_per_gpu": round(achieved, 1),
             "roofline": {
                 "bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                 "frac": round(achieved / peak, 4), "peak_kind": peak_kind,
                 "traffic": traffic, "traffic_source": traffic_src,
-                "launch": "one qsdpa_decode call: decode kernel + split merge",
-                "bytes_per_launch": bytes_local,
+                "launch": "one qsdpa_decode call over this GPU's keys: decode kernel + split merge",
+                "bytes_per_launch": bytes_call,
                 "launch_us": round(per_launch_ms * 1e3, 3),
             },
             "e2e": {"value": round(e2e_ms * 1e3, 3), "unit": "us/step",
-                    "h2d_bytes_per_step": B * HQ * D * 2, "d2h_bytes_per_step": B * HQ * D * 2},
-            "gpu_launches": K * launches_per_step,  # decode, split merge, (cross-GPU merge) per step
+                    "h2d_bytes_per_step": L * B * HQ * D * 2, "d2h_bytes_per_step": L * B * HQ * D * 2},
+            "gpu_launches": K * L * launches_per_call,
             "clocks": clocks,
-            "split_check_max_abs": check,
+            "checks": checks,
         }
-        if world == 1:
+        if world == 1 and args.cpu_sample_calls > 0:
             us, thr = cpu_decode_timer(ctx, args.cpu_sample_calls)
             line["cpu_baseline"] = {
-                "value": round(us, 1), "unit": "us/step", "cores": thr, "kind": "port",
-                "sample": f"{args.cpu_sample_calls} full {ctx}-token decode calls of the C restatement "
-                          "(dequantise K/V to fp16, fp32 SDPA) on all host threads",
+                "value": round(us * L, 1), "unit": "us/step", "cores": thr, "kind": "port",
+                "sample": f"{args.cpu_sample_calls} layer call(s) over the full {ctx:,}-token context of the C "
+                          f"restatement (dequantise K/V to fp16, fp32 SDPA) on all host threads, times {L} layers",
             }
+        if world == 1 and not args.no_extras:
+            line["extras"] = extras(torch, peak)
+        if batch_us is not None:
+            line["extras"] = {"config4_batch_sharded": {
+                "us_per_step": round(batch_us, 3), "ranks": world, "rows_rank0": batch_rows,
+                "what": "configuration 4 (B=32, lengths U[2048, 32768], H_q=32, H_kv=8, D=128, 4-bit gs64) "
+                        "sharded by sequence: each rank appends one token per sequence and decodes its own "
+                        "rows through BatchQuantizedSDPACache + cache_sdpa, max over ranks; no collective"}}
         print(json.dumps(line), flush=True)
 
     if world > 1:
         # graphs holding NCCL work must be released before the process group
         torch.cuda.synchronize(dev)
-        kgraphs = None
         graphs.clear()
         exchange = None
         import gc
         gc.collect()
         torch.cuda.synchronize(dev)
         dist.destroy_process_group()
+    if not ok:
+        print(f"rank {rank}: correctness check failed: {checks}", file=sys.stderr, flush=True)
+        sys.exit(3)
 
 
 def run_reference(args, world, rank):
     """Reference arm: the reference's CPU path (C restatement) on the host cores."""
     if rank != 0:
         return
-    ctx = args.ctx * world
-    K = max(1, min(args.steps, 10))
+    ctx = args.context
+    L = args.layers
+    K = max(1, min(args.steps, 5))
     W = max(0, min(args.warmup, 1))
-    lib = oracle_lib()
-    del lib
     for _ in range(W):
         cpu_decode_timer(ctx, 1)
     us, thr = cpu_decode_timer(ctx, K)
     line = {
         "impl": "reference",
         "metric": METRIC,
-        "value": round(us, 1),
+        "value": round(us * L, 1),
         "unit": "us/step",
         "n_gpus": world,
         "steps": K,
         "warmup": W,
-        "ms_per_step": round(us / 1e3, 3),
+        "ms_per_step": round(us * L / 1e3, 3),
         "higher_is_better": False,
-        "scaling": "weak",
+        "scaling": "strong",
         "vs_baseline": None,
         "dtype": "f16",
         "data": "synthetic",
-        "config": {"workload": "same decode step, context = n_gpus x 128K tokens, on the host CPU",
+        "config": {"workload": f"decode step of {L} attention layers, each over a {ctx:,}-token quantized KV "
+                               "context, on the host CPU",
                    "B": B, "H_q": HQ, "H_kv": HKV, "D": D, "bits": BITS, "group_size": GS,
-                   "context_total": ctx},
-        "cpu_baseline": {"value": round(us, 1), "unit": "us/step", "cores": thr, "kind": "port",
-                         "sample": f"{K} full {ctx}-token decode calls of the C restatement of "
-                                   "cache_sdpa's dequantise + SDPA branch (MLX not installable here)"},
-        "e2e": {"value": round(us, 1), "unit": "us/step", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+                   "context_total": ctx, "layers": L},
+        "cpu_baseline": {"value": round(us * L, 1), "unit": "us/step", "cores": thr, "kind": "port",
+                         "sample": f"each step one layer call over the full {ctx:,}-token context of the C "
+                                   "restatement of cache_sdpa's dequantise + SDPA branch (MLX not installable "
+                                   f"here) on all host threads, times {L} layers"},
+        "e2e": {"value": round(us * L, 1), "unit": "us/step", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
 

@@ -158,6 +158,11 @@ int qsdpa_decode(const qsdpa_decode_params* p, void* stream);
  * splits == 0 with the device's SM count). */
 int qsdpa_decode_splits(const qsdpa_decode_params* p);
 
+/* Kernel qsdpa_decode runs for these parameters (QSDPA_KERNEL_TCGEN05,
+ * _MMA or _SIMT; resolves QSDPA_KERNEL_AUTO), or a negative error code.  No
+ * counterpart in the reference, whose dispatch has one kernel per path. */
+int qsdpa_decode_kernel(const qsdpa_decode_params* p);
+
 /* Workspace bytes qsdpa_decode needs for these parameters. */
 size_t qsdpa_decode_workspace_size(const qsdpa_decode_params* p);
 
@@ -296,6 +301,39 @@ const char* qsdpa_last_error(void);
 
 /* QSDPA_ABI_VERSION of the loaded library. */
 int qsdpa_abi_version(void);
+
+/*
+ * Token-row gather between quantized cache planes: the device side of the
+ * caches' management operations (merge, extend, filter, extract, the
+ * right-padding roll of finalize, the ring buffer's temporal order, buffer
+ * growth) -- mlx_qsdpa/cache.py:199-231, 324-348, 378-492, 662-711, 868-1010
+ * restate each of those as array slicing and concatenation.
+ *
+ * Destination plane q is (B, H, T, W[q]) elements of elem_bytes[q] bytes with
+ * batch / head strides dst_sb[q] / dst_sh[q] (elements; token rows
+ * contiguous).  Destination row b copies, for every destination token j in
+ * [lo_b, hi_b), source token s = (j - shift_b) mod mod_b (mod_b == 0: s = j -
+ * shift_b, which must be >= 0) of its own source, and writes zeros for every
+ * other token.  Device tables (int64 / uint64, one row per destination row b):
+ *   src[b * planes + q]     address of the source row's (head 0, token 0) in plane q
+ *   src_sh[b * planes + q]  that source's head stride (elements; token rows contiguous)
+ *   rowinfo[4 b .. 4 b + 3] shift_b, lo_b, hi_b, mod_b
+ * Destination and sources must not overlap.
+ */
+#define QSDPA_GATHER_MAX_PLANES 6
+typedef struct qsdpa_gather_params {
+    int32_t planes;
+    void* dst[QSDPA_GATHER_MAX_PLANES];
+    int64_t dst_sb[QSDPA_GATHER_MAX_PLANES], dst_sh[QSDPA_GATHER_MAX_PLANES];
+    int32_t W[QSDPA_GATHER_MAX_PLANES];
+    int32_t elem_bytes[QSDPA_GATHER_MAX_PLANES];
+    const uint64_t* src;
+    const int64_t* src_sh;
+    const int64_t* rowinfo;
+    int32_t B, H, T;
+} qsdpa_gather_params;
+
+int qsdpa_gather_rows(const qsdpa_gather_params* p, void* stream);
 
 #ifdef __cplusplus
 }

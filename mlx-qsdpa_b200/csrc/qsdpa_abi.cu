@@ -26,7 +26,6 @@ constexpr int kMinChunk = 64;  // keys per CTA below which splitting stops payin
 constexpr int kLongChunk = 256;  // keys per CTA from which a second CTA per SM pays off
 constexpr int kMinChunkTc = 128;  // one tile of the tcgen05 kernel
 constexpr int kMaxQL = 16;        // queries per head of one call
-constexpr int kTcMaxChunk = 8192;   // keys per CTA above which the keys are split further
 constexpr int kMmaMaxChunk = 4096;
 // QSDPA_KERNEL_AUTO takes the tcgen05 kernel from this many keys per KV head
 // and GQA groups of at least kAutoTcMinGqa heads; below either the mma.sync
@@ -217,12 +216,11 @@ int make_plan(const qsdpa_decode_params* p, const DecodeArgs& a, Plan& pl) {
         // chunk holds kLongChunk keys; CUDA-core kernel: two waves of 4 per SM.
         // No chunk below kMinChunk.
         if (pl.kern == Kern::Tc) {
-            // one CTA per SM (its shared memory fills the SM): one wave, or
-            // more when the units alone fill the GPU, with no CTA walking more
-            // than kTcMaxChunk keys (long chunks leave a ragged last wave)
+            // one CTA per SM (its shared memory fills the SM) and exactly one
+            // wave, however long the chunks get: a second, ragged wave costs
+            // more than the longer walk (measured at 1M keys, GQA-16 D=256:
+            // 148 CTAs 171.8 us, 256 CTAs 197.5 us, 294 CTAs 179.2 us)
             splits = (sm_count() + units - 1) / units;
-            const int by_max = (p->N + kTcMaxChunk - 1) / kTcMaxChunk;
-            if (splits < by_max) splits = by_max;
         } else if (pl.use_mma) {
             const int lo = (sm_count() + units - 1) / units, hi = (2 * sm_count() + units - 1) / units;
             const int by_long = (p->N + kLongChunk - 1) / kLongChunk;
@@ -269,6 +267,17 @@ extern "C" int qsdpa_decode_splits(const qsdpa_decode_params* p) {
     Plan pl;
     rc = make_plan(p, a, pl);
     return rc ? rc : pl.splits;
+}
+
+extern "C" int qsdpa_decode_kernel(const qsdpa_decode_params* p) {
+    int rc = validate(p);
+    if (rc) return rc;
+    DecodeArgs a;
+    fill_args(p, a);
+    Plan pl;
+    rc = make_plan(p, a, pl);
+    if (rc) return rc;
+    return pl.kern == Kern::Tc ? QSDPA_KERNEL_TCGEN05 : pl.kern == Kern::Mma ? QSDPA_KERNEL_MMA : QSDPA_KERNEL_SIMT;
 }
 
 extern "C" size_t qsdpa_decode_workspace_size(const qsdpa_decode_params* p) {

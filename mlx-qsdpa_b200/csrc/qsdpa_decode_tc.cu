@@ -126,6 +126,9 @@ constexpr int kTmemS = 0;       // S^T: two buffers of 16 columns
 constexpr int kTmemO = 32;      // O^T: 16 columns per 128 head dims
 constexpr int kTmemK = 64;      // K operand: two buffers of D/2 columns
 constexpr float kRescaleTc = 8.f;
+// running maximum before the first key: finite, far below any score, so
+// s - m_run is never NaN (a head that saw no key reports m = -inf)
+constexpr float kNoMax = -3.0e38f;
 constexpr unsigned long long kWaitNs = 1000000000ull;
 constexpr int kSmemLimit = 227 * 1024;
 // launch as a programmatic dependent of the previous kernel on the stream
@@ -135,6 +138,9 @@ constexpr int kSmemLimit = 227 * 1024;
 constexpr bool kTcPdl = QSDPA_TC_PDL != 0;
 #ifndef QSDPA_TC_VREG
 #define QSDPA_TC_VREG 1
+#endif
+#ifndef QSDPA_TC_VHALF
+#define QSDPA_TC_VHALF 0
 #endif
 
 template <int BITS, int D, int GS, bool SPLITP>
@@ -149,8 +155,13 @@ struct TcCfg {
     static constexpr int SC_BYTES = kTcTile * SROWB;
     static constexpr int SC_CHUNKS = SC_BYTES / 16;
     static constexpr int STAGE_BYTES = 2 * PACK_BYTES + 4 * SC_BYTES;
-    static constexpr int V_BYTES = kTcTile * D * 2;       // one V^T operand
-    static constexpr int V_LBO = (kTcTile / 8) * 1024;    // V^T: between 64-dim blocks
+    // V^T operands hold half a tile (64 tokens) each: two of them take the
+    // shared memory of one whole-tile operand and leave room for another ring
+    // stage; the P V MMA of a tile runs as two halves
+    static constexpr bool VHALF = QSDPA_TC_VHALF != 0;
+    static constexpr int VT = VHALF ? kTcTile / 2 : kTcTile;  // tokens per V^T operand
+    static constexpr int V_BYTES = VT * D * 2;            // one V^T operand
+    static constexpr int V_LBO = (VT / 8) * 1024;         // V^T: between 64-dim blocks
     static constexpr int Q_BYTES = kTcHeads * D * 2;      // Q operand
     static constexpr int P_BYTES = kTcTile * kTcHeads * 2;  // one P^T operand
     static constexpr int P_BUF = (SPLITP ? 2 : 1) * P_BYTES;  // hi (+ lo) of one of two P buffers
@@ -161,8 +172,8 @@ struct TcCfg {
     }
     // two P^T buffers (softmax of tile j overlaps the P V MMA of tile j-1) and
     // two V^T buffers (values run a tile ahead) where they fit
-    static constexpr int PBUFS = fits(2, 1) ? 2 : 1;
-    static constexpr int VBUFS = fits(PBUFS, 2) ? 2 : 1;
+    static constexpr int PBUFS = fits(2, VHALF ? 2 : 1) ? 2 : 1;
+    static constexpr int VBUFS = VHALF ? 2 : (fits(PBUFS, 2) ? 2 : 1);
     static constexpr int FIXED = BASE + PBUFS * P_BUF;
     static constexpr int STAGES_FIT = (kSmemLimit - FIXED - VBUFS * V_BYTES) / STAGE_BYTES;
     static constexpr int STAGES = STAGES_FIT > 4 ? 4 : STAGES_FIT;
@@ -174,6 +185,9 @@ struct TcCfg {
     // box of 128-byte rows is exactly the ring's chunk swizzle); 64-byte rows by
     // the producer lanes' cp.async
     static constexpr bool TMA_ROWS = ROWB == 128 || ROWB == 256;
+    // scale / bias rows of 16 bytes (8 groups) arrive by TMA as well: one
+    // instruction per array and tile instead of a loop of 16-byte copies
+    static constexpr bool TMA_SCALES = TMA_ROWS && SROWB == 16;
     // value rows of up to 128 bytes are copied to registers and the stage
     // released before they are dequantised (the key warps finish a stage
     // first, so the value warps decide when the producer may refill it)
@@ -455,9 +469,26 @@ __device__ __forceinline__ void dequant_chunk(const uint4 w4, uint32_t s2, uint3
     }
 }
 
+// Tensor maps of one call: packed K and V rows, and the scale / bias arrays
+// (k scales, k biases, v scales, v biases) when their rows are 16 bytes.
+struct TcMaps {
+    CUtensorMap k, v;
+    CUtensorMap sc[4];
+};
+
+// One tile of scale / bias rows (128 rows of 8 halves starting at token p0).
+__device__ __forceinline__ void tma_scale_rows(uint32_t dst, const CUtensorMap* map, int p0, int kvh, int b,
+                                               uint32_t mbar) {
+    asm volatile(
+        "cp.async.bulk.tensor.4d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4, %5}], "
+        "[%6];\n" ::"r"(dst),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(0), "r"(p0), "r"(kvh), "r"(b), "r"(mbar)
+        : "memory");
+}
+
 template <typename T, int BITS, int D, int GS, bool CAUSAL>
 __global__ void __launch_bounds__(kTcThreads, 1)
-    decode_tc_kernel(const DecodeArgs a, const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v) {
+    decode_tc_kernel(const DecodeArgs a, const __grid_constant__ TcMaps maps) {
     using C = TcCfg<BITS, D, GS, Ops<T>::kSplitP>;
     constexpr bool kBf16 = !std::is_same<T, __half>::value;
     constexpr uint32_t IDESC_QK = make_idesc(kBf16, false, false, 128, kTcHeads);
@@ -541,9 +572,19 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         if constexpr (C::TMA_ROWS) {
             // rows past N arrive zero-filled; rows of the next chunk are masked later
             if (lane == 0) {
-                mbar_expect_tx(full_bar(s), 2 * C::PACK_BYTES);
-                tma_rows<C::ROWB>(smem_u32(st), &tm_k, p0, kvh, b, full_bar(s));
-                tma_rows<C::ROWB>(smem_u32(st + C::PACK_BYTES), &tm_v, p0, kvh, b, full_bar(s));
+                const uint32_t sc_bytes = C::TMA_SCALES ? (has_bias ? 4 : 2) * C::SC_BYTES : 0;
+                mbar_expect_tx(full_bar(s), 2 * C::PACK_BYTES + sc_bytes);
+                tma_rows<C::ROWB>(smem_u32(st), &maps.k, p0, kvh, b, full_bar(s));
+                tma_rows<C::ROWB>(smem_u32(st + C::PACK_BYTES), &maps.v, p0, kvh, b, full_bar(s));
+                if constexpr (C::TMA_SCALES) {
+                    const uint32_t s0 = smem_u32(st + 2 * C::PACK_BYTES);
+                    tma_scale_rows(s0, &maps.sc[0], p0, kvh, b, full_bar(s));
+                    tma_scale_rows(s0 + 2 * C::SC_BYTES, &maps.sc[2], p0, kvh, b, full_bar(s));
+                    if (has_bias) {
+                        tma_scale_rows(s0 + C::SC_BYTES, &maps.sc[1], p0, kvh, b, full_bar(s));
+                        tma_scale_rows(s0 + 3 * C::SC_BYTES, &maps.sc[3], p0, kvh, b, full_bar(s));
+                    }
+                }
             }
         } else {
             const char* ksrc = kp_b + (int64_t)p0 * C::ROWB + lane * 16;
@@ -573,7 +614,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         }
         const int sbytes = rows_valid * C::SROWB;
         char* s0 = st + 2 * C::PACK_BYTES;
-        for (int k = lane; k < C::SC_CHUNKS; k += 32) {
+        for (int k = lane; k < C::SC_CHUNKS && !C::TMA_SCALES; k += 32) {
             const int off = k * 16;
             const int nb = max(0, min(16, sbytes - off));
             const int64_t goff = (int64_t)p0 * C::SROWB + (nb > 0 ? off : 0);
@@ -632,7 +673,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 
     float m_run[kTcHeads], l_run[kTcHeads];
 #pragma unroll
-    for (int h = 0; h < kTcHeads; ++h) m_run[h] = -INFINITY, l_run[h] = 0.f;
+    for (int h = 0; h < kTcHeads; ++h) m_run[h] = kNoMax, l_run[h] = 0.f;
     int n_active = 0;
 
     if (warp == kProdWarp) {
@@ -682,6 +723,36 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         for (int i = advance(0); i < ntiles; i = advance(i + 1)) ++n;
         for (int jp = 0; jp < n && !dead; ++jp) {
             mbar_wait(pready_bar(jp % PB), (jp / PB) & 1, dead);
+            if constexpr (C::VHALF) {
+                // half h of the tile: tokens 64h.. in V^T buffer h, rows 64h.. of P^T
+                const int pbuf = jp % PB;
+                const uint64_t pb0 = pbase + (uint64_t)((pbuf * C::P_BUF) >> 4);
+#pragma unroll 1
+                for (int h = 0; h < 2 && !dead; ++h) {
+                    mbar_wait(vready_bar(h), jp & 1, dead);
+                    if (dead) break;
+                    tc_fence_after();
+                    if (elect_one()) {
+                        const uint64_t vb0 = vbase + (uint64_t)((h * C::V_BYTES) >> 4);
+#pragma unroll
+                        for (int mb = 0; mb < C::MB; ++mb) {
+#pragma unroll
+                            for (int ks_ = 0; ks_ < C::VT / 16; ++ks_) {
+                                const uint64_t vd = vb0 + (uint64_t)(((2 * mb) * C::V_LBO + (2 * ks_) * 1024) >> 4);
+                                const uint64_t pd = pb0 + (uint64_t)(((h * (C::VT / 16) + ks_) * 512) >> 4);
+                                mma_ss(tbase + kTmemO + mb * 16, vd, pd, IDESC_PV, (jp > 0 || h > 0 || ks_ > 0) ? 1u : 0u);
+                                if constexpr (Ops<T>::kSplitP)
+                                    mma_ss(tbase + kTmemO + mb * 16, vd, pd + (uint64_t)(C::P_BYTES >> 4), IDESC_PV, 1u);
+                            }
+                        }
+                        mma_commit(vfree_bar(h));
+                        if (h == 1) mma_commit(pfree_bar(pbuf));
+                    }
+                    __syncwarp();
+                }
+                TC_TRACE(kEvMmaPV, jp);
+                continue;
+            }
             mbar_wait(vready_bar(jp % VB), (jp / VB) & 1, dead);
             if (dead) break;
             const int vbuf = jp % VB, pbuf = jp % PB;
@@ -808,11 +879,20 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             }
 
             // ---------------- online softmax for token p0 + t ----------------
+            // log2-domain scores; m_run starts at kNoMax (finite), so s - m_run
+            // is never NaN: +huge for a first finite score, -inf for a masked key
             const int p0 = p_lo + i * kTcTile;
             const int tok = p0 + t;
-            const bool valid = tok < p_hi && win.contains(tok);
 #pragma unroll
-            for (int h = 0; h < kTcHeads; ++h) s[h] = valid ? s[h] * a.scale_log2 : -INFINITY;
+            for (int h = 0; h < kTcHeads; ++h) s[h] *= a.scale_log2;
+            bool valid = true;
+            if (!(win.full && p0 + kTcTile <= p_hi)) {  // a tile cut by the chunk end or the window
+                valid = tok < p_hi && win.contains(tok);
+                if (!valid) {
+#pragma unroll
+                    for (int h = 0; h < kTcHeads; ++h) s[h] = -INFINITY;
+                }
+            }
             if (a.mask && valid) {
 #pragma unroll
                 for (int h = 0; h < kTcHeads; ++h)
@@ -828,10 +908,15 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 for (int h = 0; h < kTcHeads; ++h)
                     if (rel > lim0 + (h0 + h) % a.causal_qL) s[h] = -INFINITY;
             }
-            bool up = false;
+            // p[h] holds the exponent s - m_run until the 2^ below
+            float p[kTcHeads];
+            float dmax = -INFINITY;
 #pragma unroll
-            for (int h = 0; h < kTcHeads; ++h) up |= s[h] > m_run[h] + kRescaleTc;
-            const bool wup = __any_sync(0xffffffffu, up);
+            for (int h = 0; h < kTcHeads; ++h) {
+                p[h] = s[h] - m_run[h];
+                dmax = fmaxf(dmax, p[h]);
+            }
+            const bool wup = __any_sync(0xffffffffu, dmax > kRescaleTc);
             if (lane == 0) flags[qw] = wup ? 1 : 0;
             named_barrier(1, kSmWarps * 32);
             const bool tile_up = (flags[0] | flags[1] | flags[2] | flags[3]) != 0;
@@ -859,6 +944,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                     alpha[h] = u ? ex2(m_run[h] - v) : 1.f;
                     if (u) m_run[h] = v;
                     l_run[h] *= alpha[h];
+                    p[h] = s[h] - m_run[h];
                 }
                 named_barrier(1, kSmWarps * 32);  // red read before it is written again
                 if (js > 0) {
@@ -878,11 +964,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                     tmem_wait_st();
                 }
             }
-            float p[kTcHeads];
 #pragma unroll
             for (int h = 0; h < kTcHeads; ++h) {
-                const float mu = m_run[h] == -INFINITY ? 0.f : m_run[h];
-                p[h] = ex2(s[h] - mu);
+                p[h] = ex2(p[h]);
                 l_run[h] += p[h];
             }
             // row t of P^T: 32 bytes, halves swapped on rows 4-7 of each 8 (32-byte swizzle)
@@ -918,9 +1002,101 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         }
     } else {
         // ================= value warps: V -> V^T operand =================
+        if constexpr (C::VHALF) {
+            // thread t: the tokens th and 64 + th of the tile (one per half),
+            // head dims [dh * D/2, (dh + 1) * D/2) of each
+            constexpr int HC = C::CPR / 2;                  // chunks per half row
+            constexpr int GH = C::G >= 2 ? C::G / 2 : 1;    // groups of a half row
+            const int th = t & 63, dh = t >> 6;
+            const int g0 = C::G >= 2 ? dh * GH : 0;
+            const RowChunks<C::CPR> rows0(th), rows1(64 + th);
+            const uint32_t vx = (uint32_t)(th & 7) << 4;
+            char* const vrow0 = sV + (th >> 3) * 1024 + (th & 7) * 128;
+            // every 4 pairs are 8 consecutive head dims: one 16-byte store into
+            // token th's row of the 1024-byte atom (8 tokens x 64 dims) of
+            // 64-dim block w8 / 8, 16-byte slot (w8 % 8) ^ (th % 8)
+            auto store_chunk = [&](int h, int cg, const uint32_t* o) {
+                char* vrow = vrow0 + h * C::V_BYTES;
+#pragma unroll
+                for (int e = 0; e < PPC / 4; ++e) {
+                    const int w8 = cg * (PPC / 4) + e;
+                    *reinterpret_cast<uint4*>(vrow + (w8 >> 3) * C::V_LBO + (((uint32_t)(w8 & 7) << 4) ^ vx)) =
+                        make_uint4(o[4 * e], o[4 * e + 1], o[4 * e + 2], o[4 * e + 3]);
+                }
+            };
+            int j = 0;
+            for (int i = advance(0); i < ntiles; i = advance(i + 1), ++j) {
+                const int s = j % ST;
+                mbar_wait(full_bar(s), (j / ST) & 1, dead);
+                const char* st = ring + s * C::STAGE_BYTES;
+                const char* vsc0 = st + 2 * C::PACK_BYTES + 2 * C::SC_BYTES + th * C::SROWB + g0 * 2;
+                const char* vsc1 = vsc0 + 64 * C::SROWB;
+                if constexpr (C::VAL_REGS) {
+                    // both half rows and their scale / bias pairs into registers,
+                    // the stage released, then one half at a time into its buffer
+                    uint4 w[2][HC];
+#pragma unroll
+                    for (int c = 0; c < HC; ++c) {
+                        w[0][c] = lds128(st + C::PACK_BYTES + rows0.off(dh * HC + c));
+                        w[1][c] = lds128(st + C::PACK_BYTES + rows1.off(dh * HC + c));
+                    }
+                    uint32_t sc2[2][GH], bi2[2][GH];
+                    load_pairs<GH>(vsc0, sc2[0]);
+                    load_pairs<GH>(vsc1, sc2[1]);
+                    if (has_bias) {
+                        load_pairs<GH>(vsc0 + C::SC_BYTES, bi2[0]);
+                        load_pairs<GH>(vsc1 + C::SC_BYTES, bi2[1]);
+                    } else {
+#pragma unroll
+                        for (int g = 0; g < GH; ++g) bi2[0][g] = bi2[1][g] = 0u;
+                    }
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(empty_bar(s));
+                    if (warp == kKeyWarps) TC_TRACE(kEvValGo, j);
+#pragma unroll
+                    for (int h = 0; h < 2; ++h) {
+                        if (j >= 1) mbar_wait(vfree_bar(h), (j - 1) & 1, dead);
+#pragma unroll
+                        for (int c = 0; c < HC; ++c) {
+                            const int cg = dh * HC + c;
+                            const int g = (cg * EPC) / GS - g0;
+                            uint32_t o[PPC];
+                            dequant_chunk<T, BITS>(w[h][c], sc2[h][g], bi2[h][g], o);
+                            store_chunk(h, cg, o);
+                        }
+                        fence_proxy_async();
+                        __syncwarp();
+                        if (lane == 0) mbar_arrive(vready_bar(h));
+                    }
+                } else {
+#pragma unroll 1
+                    for (int h = 0; h < 2; ++h) {
+                        if (j >= 1) mbar_wait(vfree_bar(h), (j - 1) & 1, dead);
+                        const RowChunks<C::CPR>& rw = h ? rows1 : rows0;
+                        const char* vsc = h ? vsc1 : vsc0;
+#pragma unroll 2
+                        for (int c = 0; c < HC; ++c) {
+                            const int cg = dh * HC + c;
+                            const int g = (cg * EPC) / GS - g0;
+                            const uint32_t s2 = pair_at(vsc + g * 2);
+                            const uint32_t b2 = has_bias ? pair_at(vsc + C::SC_BYTES + g * 2) : 0u;
+                            uint32_t o[PPC];
+                            dequant_chunk<T, BITS>(lds128(st + C::PACK_BYTES + rw.off(cg)), s2, b2, o);
+                            store_chunk(h, cg, o);
+                        }
+                        fence_proxy_async();
+                        __syncwarp();
+                        if (lane == 0) mbar_arrive(vready_bar(h));
+                    }
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(empty_bar(s));
+                }
+                if (warp == kKeyWarps) TC_TRACE(kEvValEnd, j);
+            }
+        }
         const RowChunks<C::CPR> rows(t);
         int j = 0;
-        for (int i = advance(0); i < ntiles; i = advance(i + 1), ++j) {
+        for (int i = advance(0); i < ntiles && !C::VHALF; i = advance(i + 1), ++j) {
             const int s = j % ST;
             const int vbuf = j % VB;
             mbar_wait(full_bar(s), (j / ST) & 1, dead);
@@ -1018,7 +1194,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         }
         if (warp == kSmWarp0 && lane == 0) {
 #pragma unroll
-            for (int h = 0; h < kTcHeads; ++h) mm[h] = m_run[h];
+            for (int h = 0; h < kTcHeads; ++h) mm[h] = m_run[h] == kNoMax ? -INFINITY : m_run[h];
         }
     }
     tc_fence_before();
@@ -1081,6 +1257,67 @@ int encode_rows(CUtensorMap* m, const void* base, int64_t sb_words, int64_t sh_w
     return QSDPA_OK;
 }
 
+// Tensor map over one scale / bias array (B, Hkv, N, 8) of 16-bit values:
+// 128-token boxes of whole 16-byte rows, no swizzle.
+int encode_scales(CUtensorMap* m, const void* base, int64_t sb, int64_t sh, int N, int Hkv, int B) {
+    EncodeTiledFn enc = encode_tiled();
+    if (!enc) return set_error(QSDPA_ERR_CUDA, "cuTensorMapEncodeTiled is not available from the driver");
+    uint64_t shb = (uint64_t)sh * 2, sbb = (uint64_t)sb * 2;
+    const uint64_t head_bytes = (uint64_t)N * 16;
+    if (Hkv == 1 || shb < head_bytes) shb = Hkv == 1 ? head_bytes : shb;  // a size-1 dim's stride is free
+    if (B == 1 || sbb == 0) sbb = B == 1 ? shb * (uint64_t)Hkv : sbb;
+    cuuint64_t dims[4] = {8, (cuuint64_t)N, (cuuint64_t)Hkv, (cuuint64_t)B};
+    cuuint64_t strides[3] = {16, shb, sbb};
+    cuuint32_t box[4] = {8, kTcTile, 1, 1}, estr[4] = {1, 1, 1, 1};
+    const CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_UINT16, 4, const_cast<void*>(base), dims, strides, box, estr,
+                           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+                           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return set_error(QSDPA_ERR_CUDA, "cuTensorMapEncodeTiled (scales) failed (%d)", (int)r);
+    return QSDPA_OK;
+}
+
+// Encoded maps of recent calls, keyed by everything an encoding depends on:
+// a decode step calls the same layers' caches over and over, so the host
+// encodes each map once.  A small direct-mapped table per process.
+struct MapKey {
+    const void* base;
+    int64_t sb, sh;
+    int N, Hkv, B, kind;  // kind: packed row bytes, or 0 for a scale / bias array
+    bool operator==(const MapKey& o) const {
+        return base == o.base && sb == o.sb && sh == o.sh && N == o.N && Hkv == o.Hkv && B == o.B && kind == o.kind;
+    }
+};
+struct MapSlot {
+    MapKey key;
+    CUtensorMap map;
+    bool used;
+};
+constexpr int kMapSlots = 256;
+MapSlot g_map_cache[kMapSlots];
+std::mutex g_map_mutex;
+
+template <typename Encode>
+int cached_map(CUtensorMap* out, const MapKey& key, Encode encode) {
+    uint64_t h = reinterpret_cast<uintptr_t>(key.base) * 0x9E3779B97F4A7C15ull;
+    h ^= (uint64_t)key.sh * 31 + (uint64_t)key.sb * 131 + (uint64_t)key.N * 7 + (uint64_t)key.kind * 17 +
+         (uint64_t)key.Hkv * 3 + (uint64_t)key.B;
+    MapSlot& slot = g_map_cache[(h >> 17) % kMapSlots];
+    {
+        std::lock_guard<std::mutex> lock(g_map_mutex);
+        if (slot.used && slot.key == key) {
+            *out = slot.map;
+            return QSDPA_OK;
+        }
+    }
+    const int rc = encode(out);
+    if (rc) return rc;
+    std::lock_guard<std::mutex> lock(g_map_mutex);
+    slot.key = key;
+    slot.map = *out;
+    slot.used = true;
+    return QSDPA_OK;
+}
+
 template <typename T, int BITS, int D, int GS>
 int launch_tc4(const DecodeArgs& a, cudaStream_t st) {
     using C = TcCfg<BITS, D, GS, Ops<T>::kSplitP>;
@@ -1096,14 +1333,29 @@ int launch_tc4(const DecodeArgs& a, cudaStream_t st) {
         if (e != cudaSuccess) return set_error(QSDPA_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
         attr_set[causal][dev] = true;
     }
-    CUtensorMap tm_k, tm_v;
-    memset(&tm_k, 0, sizeof(tm_k));
-    memset(&tm_v, 0, sizeof(tm_v));
+    TcMaps maps;
+    memset(&maps, 0, sizeof(maps));
     if constexpr (C::TMA_ROWS) {
         if (a.N > 0) {
-            int rc = encode_rows<C::ROWB>(&tm_k, a.kp, a.kp_sb, a.kp_sh, a.N, a.Hkv, a.B);
-            if (rc == QSDPA_OK) rc = encode_rows<C::ROWB>(&tm_v, a.vp, a.vp_sb, a.vp_sh, a.N, a.Hkv, a.B);
+            auto rows_map = [&](CUtensorMap* m, const void* base, int64_t sb, int64_t sh) {
+                return cached_map(m, MapKey{base, sb, sh, a.N, a.Hkv, a.B, C::ROWB}, [&](CUtensorMap* o) {
+                    return encode_rows<C::ROWB>(o, base, sb, sh, a.N, a.Hkv, a.B);
+                });
+            };
+            int rc = rows_map(&maps.k, a.kp, a.kp_sb, a.kp_sh);
+            if (rc == QSDPA_OK) rc = rows_map(&maps.v, a.vp, a.vp_sb, a.vp_sh);
             if (rc) return rc;
+            if constexpr (C::TMA_SCALES) {
+                const void* base[4] = {a.ks, a.kb, a.vs, a.vb};
+                const int64_t sb[4] = {a.ks_sb, a.kb_sb, a.vs_sb, a.vb_sb};
+                const int64_t sh[4] = {a.ks_sh, a.kb_sh, a.vs_sh, a.vb_sh};
+                for (int i = 0; i < 4 && rc == QSDPA_OK; ++i) {
+                    if (!base[i]) continue;  // symmetric: no bias maps
+                    rc = cached_map(&maps.sc[i], MapKey{base[i], sb[i], sh[i], a.N, a.Hkv, a.B, 0},
+                                    [&](CUtensorMap* o) { return encode_scales(o, base[i], sb[i], sh[i], a.N, a.Hkv, a.B); });
+                }
+                if (rc) return rc;
+            }
         }
     }
     // a programmatic dependent launch: the CTAs may start (barriers, tensor
@@ -1119,7 +1371,7 @@ int launch_tc4(const DecodeArgs& a, cudaStream_t st) {
     attr[0].val.programmaticStreamSerializationAllowed = kTcPdl ? 1 : 0;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, a, tm_k, tm_v);
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, a, maps);
     if (e != cudaSuccess) return set_error(QSDPA_ERR_CUDA, "qsdpa_decode (tcgen05) launch: %s", cudaGetErrorString(e));
     return check_launch("qsdpa_decode (tcgen05)");
 }

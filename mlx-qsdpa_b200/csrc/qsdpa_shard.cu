@@ -5,16 +5,18 @@
 // The record of a rank is [o: rows x D | (m, l): rows x 2] (fp32, log2
 // domain), cut into slices of 64 dims of one query row (slice c = s * rows +
 // row holds dims [64 s, 64 s + 64) of row `row`).  Every value travels as one
-// 8-byte word {value bits, step}: a single 8-byte store is seen whole, so the
-// step number in a word says that its value is that step's, and a reader
-// needs no fence and no separate flag.  Every rank owns a buffer that all
-// ranks can address (symmetric memory, zeroed before the first step):
-//   uint2 words[2][world][ncta][kWords]   (64 o values, m, l, padding)
+// aligned 64-bit word (value bits | step << 32), stored and loaded as a single
+// relaxed system-scope 64-bit scalar: a 64-bit access is single-copy atomic,
+// so a word that carries step e carries that step's value, and a reader needs
+// no fence and no separate flag.  Every rank owns a buffer that all ranks can
+// address (symmetric memory, zeroed before the first step):
+//   uint64 words[2][world][ncta][kWords]   (64 o values, m, l, padding)
 // Step e (a device-side counter in `state`, so CUDA-graph replays advance it):
 // for each slice c it handles, thread t of a CTA stores dim t of the slice
 // (threads 0 and 1 also m and l) into words[e & 1][rank][c] of every rank's
-// buffer, then polls (at most about a second) its words of every rank in its
-// own buffer until they carry step e and merges them into the output.  The
+// buffer, then loads its words of every rank from its own buffer all at once,
+// loads again only the ones that do not carry step e yet (for at most about a
+// second) and merges them into the output in rank order.  The
 // last CTA to finish publishes e in state[0].  No thread waits for another
 // CTA of its own grid, only for the CTA of the other ranks' grids (on other
 // GPUs) that handles the same slice.  Double buffering makes the reuse safe:
@@ -44,56 +46,84 @@ constexpr unsigned long long kShardWaitNs = 1000000000ull;
 constexpr int kMaxCtas = 1024;  // 64-thread CTAs: always resident together on 148 SMs
 
 struct PeerBufs {
-    uint2* buf[kMaxWorld];
+    uint64_t* buf[kMaxWorld];
 };
 
-__device__ __forceinline__ void st_word(uint2* p, float v, unsigned int e) {
-    asm volatile("st.volatile.global.v2.u32 [%0], {%1, %2};\n" ::"l"(p), "r"(__float_as_uint(v)), "r"(e) : "memory");
+__device__ __forceinline__ void st_word(uint64_t* p, float v, unsigned int e) {
+    const uint64_t w = (uint64_t)__float_as_uint(v) | ((uint64_t)e << 32);
+    asm volatile("st.relaxed.sys.global.b64 [%0], %1;\n" ::"l"(p), "l"(w) : "memory");
 }
-__device__ __forceinline__ uint2 ld_word(const uint2* p) {
-    uint2 w;
-    asm volatile("ld.volatile.global.v2.u32 {%0, %1}, [%2];\n" : "=r"(w.x), "=r"(w.y) : "l"(p) : "memory");
+__device__ __forceinline__ uint64_t ld_word(const uint64_t* p) {
+    uint64_t w;
+    asm volatile("ld.relaxed.sys.global.b64 %0, [%1];\n" : "=l"(w) : "l"(p) : "memory");
     return w;
 }
+__device__ __forceinline__ unsigned int word_step(uint64_t w) { return (unsigned int)(w >> 32); }
+__device__ __forceinline__ float word_value(uint64_t w) { return __uint_as_float((unsigned int)w); }
 __device__ __forceinline__ uint64_t now_ns() {
     uint64_t t;
     asm volatile("mov.u64 %0, %%globaltimer;\n" : "=l"(t));
     return t;
 }
-// The value of word p once it carries step e; false when that took too long.
-__device__ __forceinline__ bool wait_word(const uint2* p, unsigned int e, uint64_t t0, float& v) {
-    uint2 w = ld_word(p);
-    while (w.y != e) {
-        if (now_ns() - t0 > kShardWaitNs) return false;
-        __nanosleep(20);
-        w = ld_word(p);
-    }
-    v = __uint_as_float(w.x);
-    return true;
-}
 
 // Thread t < kDims: merge dim t of slice c of the world ranks' records of step
 // e (words in this rank's buffer `own`, one rank's slices every `slab` words)
-// into *o_out / *l_out; false when a rank's word did not arrive in time.
-__device__ __forceinline__ bool merge_ranks(const uint2* own, int64_t slab, int c, int world, unsigned int e, int t,
-                                           float& o_out, float& l_out) {
-    const uint64_t t0 = now_ns();
-    float mt = -INFINITY, lt = 0.f, ot = 0.f;
-    for (int r = 0; r < world; ++r) {
-        const uint2* src = own + r * slab + (int64_t)c * kWords;
-        float o, m, l;
-        if (!(wait_word(src + t, e, t0, o) && wait_word(src + kDims, e, t0, m) && wait_word(src + kDims + 1, e, t0, l)))
+// into *o_out / *l_out; false when a rank's word did not arrive in time.  The
+// 3 * world words are loaded at once and only the stale ones again, so once
+// the peers' stores have landed a merge costs one round trip to memory.
+__device__ __forceinline__ bool merge_ranks(const uint64_t* own, int64_t slab, int c, int world, unsigned int e,
+                                           int t, float& o_out, float& l_out) {
+    uint64_t wo[kMaxWorld], wm[kMaxWorld], wl[kMaxWorld];
+    const uint64_t* base = own + (int64_t)c * kWords;
+#pragma unroll
+    for (int r = 0; r < kMaxWorld; ++r) {
+        wo[r] = wm[r] = wl[r] = (uint64_t)e << 32;  // ranks >= world: never stale, never merged
+        if (r < world) {
+            const uint64_t* src = base + r * slab;
+            wo[r] = ld_word(src + t);
+            wm[r] = ld_word(src + kDims);
+            wl[r] = ld_word(src + kDims + 1);
+        }
+    }
+    uint64_t t0 = 0;
+    for (;;) {
+        bool stale = false;
+#pragma unroll
+        for (int r = 0; r < kMaxWorld; ++r)
+            stale |= word_step(wo[r]) != e || word_step(wm[r]) != e || word_step(wl[r]) != e;
+        if (!stale) break;
+        const uint64_t now = now_ns();
+        if (t0 == 0) {
+            t0 = now;
+        } else if (now - t0 > kShardWaitNs) {
             return false;
-        if (m == -INFINITY) continue;
-        if (m > mt) {  // running maximum: no per-rank arrays
-            const float sc = mt == -INFINITY ? 0.f : exp2f(mt - m);
-            lt = lt * sc + l;
-            ot = ot * sc + o;
-            mt = m;
-        } else {
-            const float w = exp2f(m - mt);
-            lt += w * l;
-            ot += w * o;
+        }
+        __nanosleep(32);
+#pragma unroll
+        for (int r = 0; r < kMaxWorld; ++r) {
+            if (r < world) {
+                const uint64_t* src = base + r * slab;
+                if (word_step(wo[r]) != e) wo[r] = ld_word(src + t);
+                if (word_step(wm[r]) != e) wm[r] = ld_word(src + kDims);
+                if (word_step(wl[r]) != e) wl[r] = ld_word(src + kDims + 1);
+            }
+        }
+    }
+    // merge in rank order, so every rank computes the same sums
+    float mt = -INFINITY;
+#pragma unroll
+    for (int r = 0; r < kMaxWorld; ++r)
+        if (r < world) mt = fmaxf(mt, word_value(wm[r]));
+    float lt = 0.f, ot = 0.f;
+    if (mt != -INFINITY) {
+#pragma unroll
+        for (int r = 0; r < kMaxWorld; ++r) {
+            if (r < world) {
+                const float m = word_value(wm[r]);
+                const float w = m == -INFINITY ? 0.f : exp2f(m - mt);
+                lt += w * word_value(wl[r]);
+                ot += w * word_value(wo[r]);
+            }
         }
     }
     o_out = ot;
@@ -121,7 +151,7 @@ __global__ void __launch_bounds__(kDims) shard_merge_kernel(const float* __restr
     const int tid = threadIdx.x;
     const int ncta = rows * ((D + kDims - 1) / kDims);
     const int64_t slab = (int64_t)ncta * kWords;  // one rank's slices of one parity
-    const uint2* own = peers.buf[rank] + (int64_t)(e & 1u) * world * slab;
+    const uint64_t* own = peers.buf[rank] + (int64_t)(e & 1u) * world * slab;
     // Every rank walks the slices in the same order with the same grid, and
     // the grid is small enough to be resident at once, so the CTA a wait
     // depends on is always running.
@@ -130,7 +160,7 @@ __global__ void __launch_bounds__(kDims) shard_merge_kernel(const float* __restr
         const float ov = d < D ? rec_o[(int64_t)row * D + d] : 0.f;
         const float mlv = tid < 2 ? rec_ml[2 * row + tid] : 0.f;
         for (int r = 0; r < world; ++r) {
-            uint2* dst = peers.buf[r] + ((int64_t)(e & 1u) * world + rank) * slab + (int64_t)c * kWords;
+            uint64_t* dst = peers.buf[r] + ((int64_t)(e & 1u) * world + rank) * slab + (int64_t)c * kWords;
             st_word(dst + tid, ov, e);
             if (tid < 2) st_word(dst + kDims + tid, mlv, e);
         }
@@ -165,7 +195,7 @@ __global__ void __launch_bounds__(merge::kThreads)
     const int tid = threadIdx.x;
     const int ncta = rows * ((D + kDims - 1) / kDims);
     const int64_t slab = (int64_t)ncta * kWords;
-    const uint2* own = peers.buf[rank] + (int64_t)(e & 1u) * world * slab;
+    const uint64_t* own = peers.buf[rank] + (int64_t)(e & 1u) * world * slab;
     // every rank walks the slices in the same order with the same (resident) grid
     for (int c = blockIdx.x; c < ncta; c += gridDim.x) {
         const int row = c % rows, sl = c / rows, d = sl * kDims + tid;
@@ -173,7 +203,7 @@ __global__ void __launch_bounds__(merge::kThreads)
         const float o_loc = merge::slice_merge(po, pml, so, sml, ro, rml, parts, D, row, sl, sm, m_loc, l_loc);
         if (tid < kDims) {
             for (int r = 0; r < world; ++r) {
-                uint2* dst = peers.buf[r] + ((int64_t)(e & 1u) * world + rank) * slab + (int64_t)c * kWords;
+                uint64_t* dst = peers.buf[r] + ((int64_t)(e & 1u) * world + rank) * slab + (int64_t)c * kWords;
                 st_word(dst + tid, d < D ? o_loc : 0.f, e);
                 if (tid < 2) st_word(dst + kDims + tid, tid == 0 ? m_loc : l_loc, e);
             }
@@ -226,7 +256,7 @@ namespace {
 
 PeerBufs peer_bufs(float* const* bufs, int world) {
     PeerBufs peers = {};
-    for (int r = 0; r < world; ++r) peers.buf[r] = reinterpret_cast<uint2*>(bufs[r]);
+    for (int r = 0; r < world; ++r) peers.buf[r] = reinterpret_cast<uint64_t*>(bufs[r]);
     return peers;
 }
 
@@ -289,7 +319,7 @@ int launch_shard_combine(const float* po, const float* pml, int64_t so, int64_t 
 extern "C" size_t qsdpa_shard_buffer_bytes(int world, int rows, int D) {
     if (world < 1 || world > kMaxWorld || rows <= 0 || D <= 0) return 0;
     const size_t ncta = (size_t)rows * ((D + kDims - 1) / kDims);
-    return 2 * (size_t)world * ncta * kWords * sizeof(uint2);
+    return 2 * (size_t)world * ncta * kWords * sizeof(uint64_t);
 }
 
 extern "C" int qsdpa_shard_merge(const float* rec, float* const* bufs, unsigned int* state, int rank, int world,

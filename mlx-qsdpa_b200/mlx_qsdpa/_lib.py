@@ -81,11 +81,28 @@ class DequantizeParams(ctypes.Structure):
     ]
 
 
+GATHER_MAX_PLANES = 6
+
+
+class GatherParams(ctypes.Structure):
+    """Mirror of ``qsdpa_gather_params``."""
+
+    _fields_ = [
+        ("planes", _c_i32),
+        ("dst", _c_vp * GATHER_MAX_PLANES),
+        ("dst_sb", _c_i64 * GATHER_MAX_PLANES), ("dst_sh", _c_i64 * GATHER_MAX_PLANES),
+        ("W", _c_i32 * GATHER_MAX_PLANES), ("elem_bytes", _c_i32 * GATHER_MAX_PLANES),
+        ("src", _c_vp), ("src_sh", _c_vp), ("rowinfo", _c_vp),
+        ("B", _c_i32), ("H", _c_i32), ("T", _c_i32),
+    ]
+
+
 # Every function the C header declares (checked by the CPU test suite).
 EXPORTS = (
-    "qsdpa_decode", "qsdpa_decode_noalloc", "qsdpa_decode_splits", "qsdpa_decode_workspace_size",
+    "qsdpa_decode", "qsdpa_decode_noalloc", "qsdpa_decode_splits", "qsdpa_decode_kernel",
+    "qsdpa_decode_workspace_size",
     "qsdpa_combine", "qsdpa_quantize", "qsdpa_dequantize", "qsdpa_device_status", "qsdpa_shard_buffer_bytes",
-    "qsdpa_shard_merge", "qsdpa_decode_shard", "qsdpa_last_error", "qsdpa_abi_version",
+    "qsdpa_shard_merge", "qsdpa_decode_shard", "qsdpa_last_error", "qsdpa_abi_version", "qsdpa_gather_rows",
 )
 
 _lib = None
@@ -112,6 +129,8 @@ def load() -> ctypes.CDLL:
         lib.qsdpa_decode_noalloc.restype = ctypes.c_int
         lib.qsdpa_decode_splits.argtypes = [P(DecodeParams)]
         lib.qsdpa_decode_splits.restype = ctypes.c_int
+        lib.qsdpa_decode_kernel.argtypes = [P(DecodeParams)]
+        lib.qsdpa_decode_kernel.restype = ctypes.c_int
         lib.qsdpa_decode_workspace_size.argtypes = [P(DecodeParams)]
         lib.qsdpa_decode_workspace_size.restype = ctypes.c_size_t
         lib.qsdpa_combine.argtypes = [_c_vp, _c_vp, _c_i64, _c_i64, ctypes.c_int, ctypes.c_int,
@@ -129,6 +148,8 @@ def load() -> ctypes.CDLL:
         lib.qsdpa_decode_shard.argtypes = [P(DecodeParams), ctypes.POINTER(_c_vp), _c_vp, ctypes.c_int, ctypes.c_int,
                                            _c_vp]
         lib.qsdpa_decode_shard.restype = ctypes.c_int
+        lib.qsdpa_gather_rows.argtypes = [P(GatherParams), _c_vp]
+        lib.qsdpa_gather_rows.restype = ctypes.c_int
         lib.qsdpa_device_status.argtypes = [ctypes.c_int]
         lib.qsdpa_device_status.restype = ctypes.c_int
         lib.qsdpa_last_error.argtypes = []
@@ -297,10 +318,7 @@ def decode(q: torch.Tensor, kp, vp, ks, vs, kb, vb, *, scale: float, bits: int, 
     return out if (out_mode == OUT_FINAL or shard is not None) else part
 
 
-def plan_splits(q, kp, vp, ks, vs, kb, vb, bits: int, group_size: int, splits: int = 0,
-                kernel: int = KERNEL_AUTO) -> int:
-    """Split count qsdpa_decode will use for these tensors (host-only query)."""
-    lib = load()
+def _plan_params(q, kp, vp, ks, vs, kb, vb, bits: int, group_size: int, splits: int, kernel: int) -> DecodeParams:
     B, Hq, _, D = q.shape
     p = DecodeParams()
     p.q, p.q_sb, p.q_sh = q.data_ptr(), q.stride(0), q.stride(1)
@@ -316,8 +334,24 @@ def plan_splits(q, kp, vp, ks, vs, kb, vb, bits: int, group_size: int, splits: i
     p.bits, p.group_size, p.dtype, p.splits = bits, group_size, dtype_code(q.dtype), splits
     p.kernel = int(kernel)
     p.scale = 1.0
-    rc = lib.qsdpa_decode_splits(ctypes.byref(p))
+    return p
+
+
+def plan_splits(q, kp, vp, ks, vs, kb, vb, bits: int, group_size: int, splits: int = 0,
+                kernel: int = KERNEL_AUTO) -> int:
+    """Split count qsdpa_decode will use for these tensors (host-only query)."""
+    p = _plan_params(q, kp, vp, ks, vs, kb, vb, bits, group_size, splits, kernel)
+    rc = load().qsdpa_decode_splits(ctypes.byref(p))
     _check(rc if rc < 0 else 0, "qsdpa_decode_splits")
+    return rc
+
+
+def plan_kernel(q, kp, vp, ks, vs, kb, vb, bits: int, group_size: int, splits: int = 0,
+                kernel: int = KERNEL_AUTO) -> int:
+    """Kernel (KERNEL_TCGEN05 / _MMA / _SIMT) qsdpa_decode runs for these tensors."""
+    p = _plan_params(q, kp, vp, ks, vs, kb, vb, bits, group_size, splits, kernel)
+    rc = load().qsdpa_decode_kernel(ctypes.byref(p))
+    _check(rc if rc < 0 else 0, "qsdpa_decode_kernel")
     return rc
 
 
@@ -436,3 +470,51 @@ def combine(part_o: torch.Tensor, part_ml: torch.Tensor, dtype: torch.dtype) -> 
                            out.data_ptr(), dtype_code(dtype), _stream(part_o.device))
     _check(rc, "qsdpa_combine")
     return out
+
+
+def gather_rows(dst, sources, rowinfo, T: int):
+    """Token-row gather (``qsdpa_gather_rows``) into the destination planes.
+
+    dst:      list of up to 6 (B, H, >=T, W) tensors (token rows contiguous)
+    sources:  per destination row b, ``(planes, row)``: the source's planes (in
+              the order of ``dst``) and its batch row
+    rowinfo:  per destination row b, ``(shift, lo, hi, mod)``: destination token
+              j in [lo, hi) takes source token (j - shift) mod mod (mod 0: no
+              wrap); every other token of [0, T) becomes zero
+    """
+    lib = load()
+    B, H = dst[0].shape[0], dst[0].shape[1]
+    if B == 0 or T == 0:
+        return
+    n = len(dst)
+    if len(sources) != B or len(rowinfo) != B:
+        raise ValueError("gather_rows: one source and one row entry per destination row")
+    table = []
+    for planes, row in sources:
+        for q in range(n):
+            t = planes[q]
+            if t.stride(-1) != 1 or (t.shape[2] > 1 and t.stride(2) != t.shape[3]):
+                raise ValueError("gather_rows: source token rows must be contiguous")
+            table.append(t.data_ptr() + row * t.stride(0) * t.element_size())
+    table += [planes[q].stride(1) for planes, _ in sources for q in range(n)]
+    for r in rowinfo:
+        table += [int(x) for x in r]
+    dev = dst[0].device
+    tab = torch.tensor(table, dtype=torch.int64).to(dev)
+    p = GatherParams()
+    p.planes = n
+    for q, t in enumerate(dst):
+        if t.stride(-1) != 1 or (t.shape[2] > 1 and t.stride(2) != t.shape[3]):
+            raise ValueError("gather_rows: destination token rows must be contiguous")
+        if t.shape[2] < T:
+            raise ValueError(f"gather_rows: destination plane {q} holds {t.shape[2]} < {T} tokens")
+        p.dst[q] = t.data_ptr()
+        p.dst_sb[q], p.dst_sh[q] = t.stride(0), t.stride(1)
+        p.W[q], p.elem_bytes[q] = t.shape[3], t.element_size()
+    base = tab.data_ptr()
+    p.src = base
+    p.src_sh = base + B * n * 8
+    p.rowinfo = base + 2 * B * n * 8
+    p.B, p.H, p.T = B, H, int(T)
+    # (the caching allocator hands `tab` out again only to work queued after this launch)
+    _check(lib.qsdpa_gather_rows(ctypes.byref(p), _stream(dev)), "qsdpa_gather_rows")

@@ -1,5 +1,5 @@
-"""Benchmarks of the decode path on a CUDA device (the reference's
-benchmarks/bench_comparison.py and benchmarks/bench_cache_sdpa.py workloads).
+"""Benchmarks of the decode path on a CUDA device (the workloads of the
+reference's mlx_qsdpa/bench.py:84-97 sweep and mlx_qsdpa/bench_comparison.py).
 
     python -m mlx_qsdpa.benchmarks --config 2 [--kernel auto|tcgen05|mma|simt]
     python -m mlx_qsdpa.benchmarks --config 3 [--kernel ...]
@@ -125,7 +125,7 @@ def config3(kernel, peak, ns=(16384, 65536, 131072)):
         print(json.dumps({"config": 3, "shape": "B1 Hq8 Hkv8 D128 4-bit gs128 symmetric bf16", **r}), flush=True)
 
 
-def config4_decode(kernel, peak, seed=0):
+def config4_decode(kernel, peak, seed=0, emit=True):
     """The config-4 decode alone (B=32 rows, lengths 2K-32K in a 32K-slot
     cache, each row's window given as KVRanges), for one kernel."""
     dev = torch.device("cuda")
@@ -165,10 +165,13 @@ def config4_decode(kernel, peak, seed=0):
             "splits": _lib.plan_splits(q, k[0], v[0], k[1], v[1], k[2], v[2], bits, gs, kernel=code)}
     if peak:
         line["frac_of_peak"] = round(line["gbs"] / peak, 4)
-    print(json.dumps(line), flush=True)
+    if emit:
+        print(json.dumps(line), flush=True)
+    return line
 
 
-def config4(steps=64, seed=0):
+def config4(steps=64, seed=0, peak=None, emit=True):
+    """Append + decode steps through both batch caches; returns the two lines."""
     dev = torch.device("cuda")
     gen = torch.Generator(device=dev)
     gen.manual_seed(seed)
@@ -176,6 +179,7 @@ def config4(steps=64, seed=0):
     lens = torch.randint(2048, 32769, (B,), generator=torch.Generator().manual_seed(seed)).tolist()
     T = max(lens)
     pad = [T - n for n in lens]
+    lines = []
     for name in ("BatchQuantizedSDPACache", "BatchQuantizedRotatingSDPACache"):
         cache = (BatchQuantizedSDPACache(pad, bits=bits, group_size=gs) if name == "BatchQuantizedSDPACache"
                  else BatchQuantizedRotatingSDPACache(pad, max_size=4096, bits=bits, group_size=gs))
@@ -203,11 +207,26 @@ def config4(steps=64, seed=0):
         e1.record()
         torch.cuda.synchronize()
         us = e0.elapsed_time(e1) * 1e3 / steps
-        print(json.dumps({"config": 4, "cache": name, "B": B, "H_q": Hq, "H_kv": Hkv, "D": D, "bits": bits,
-                          "group_size": gs, "lengths": [min(lens), max(lens)], "steps": steps,
-                          "us_per_step": round(us, 3), "tokens_per_s": round(B / (us * 1e-6), 1)}), flush=True)
+        # algorithmic bytes of a step: the append (fp16 K/V in, codes + scales +
+        # biases out) and the decode over every row's valid keys (padding excluded)
+        # (the visible keys of a row grow by one per step: 3 warm-up steps, then the
+        # timed ones; the rotating cache shows at most max_size of them)
+        grown = [n + 3 + steps // 2 for n in lens]
+        visible = grown if name == "BatchQuantizedSDPACache" else [min(n, 4096) for n in grown]
+        row = D * bits // 8 + (D // gs) * 4
+        nbytes = (2 * B * Hkv * D * 2 + 2 * B * Hkv * row + 2 * B * Hq * D * 2 + 2 * Hkv * sum(visible) * row)
+        line = {"config": 4, "cache": name, "B": B, "H_q": Hq, "H_kv": Hkv, "D": D, "bits": bits,
+                "group_size": gs, "lengths": [min(lens), max(lens)], "steps": steps,
+                "us_per_step": round(us, 3), "tokens_per_s": round(B / (us * 1e-6), 1),
+                "bytes_per_step": nbytes, "gbs": round(nbytes / (us * 1e-6) / 1e9, 1)}
+        if peak:
+            line["frac_of_peak"] = round(line["gbs"] / peak, 4)
+        lines.append(line)
+        if emit:
+            print(json.dumps(line), flush=True)
         del cache, news
         torch.cuda.empty_cache()
+    return lines
 
 
 def main(argv=None):
@@ -222,7 +241,7 @@ def main(argv=None):
         config3(args.kernel, args.peak_gbs)
     else:
         config4_decode(args.kernel, args.peak_gbs)
-        config4()
+        config4(peak=args.peak_gbs)
 
 
 if __name__ == "__main__":

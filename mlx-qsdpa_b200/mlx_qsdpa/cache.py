@@ -5,27 +5,33 @@ the reference (mlx_qsdpa/cache.py:54-1010).  ``update_and_fetch`` returns
 ``((packed_uint32, scales, biases), (packed_uint32, scales, biases))`` views
 covering the visible tokens, exactly like the reference.
 
-What changes is where the work happens:
+How the caches are built here:
 
-* quantize-on-append is one kernel launch per K and V (``qsdpa_quantize``)
-  that quantises the new tokens and writes codes, scales and biases straight
-  into their cache slots -- linear offset or ring slot -- instead of
-  ``mx.quantize`` followed by three slice assignments;
-* dequantisation for rotating-cache prefill and temporal reordering runs on
-  the GPU (``qsdpa_dequantize`` with a ring offset);
-* metadata (offsets, left padding) stays on the host as int64 tensors, so the
-  protocol methods never synchronise with the GPU;
-* the batch caches additionally expose ``kv_ranges()``: the physically valid
-  key window of every row (left padding excluded), which the fused decode
-  kernel consumes directly.  ``make_mask`` reproduces the reference's mask
-  bit for bit (including its use of the logical offset, pinned by the
-  reference tests test_cache.py:291-333 and
-  test_batch_rotating_cache.py:406-450).
+* storage is six planes of shape (B, H_kv, slots, width) -- packed K codes,
+  K scales, K biases, then the same for V -- whose slot count is a multiple of
+  8 tokens (linear buffers: of ``step``), so every plane's head stride is
+  16-byte aligned and the
+  fused decode kernels read the cache in place; a linear buffer grows by at
+  least a quarter of its size at a time (amortised O(1) per token instead of a
+  full copy every ``step`` tokens);
+* quantize-on-append is one kernel per K and V (``qsdpa_quantize``) writing
+  codes, scales and biases straight into their slots (linear offset or ring
+  slot);
+* every management operation -- growth, merge, extend, filter, extract, the
+  right-padding roll of ``finalize``, a ring buffer's temporal order -- is one
+  launch of the token-row gather kernel (``qsdpa_gather_rows``), which gives
+  each destination row its own source, shift, window and ring modulus;
+* metadata (offsets, left padding) stays on the host as int64 tensors;
+* the batch caches also expose ``kv_ranges()``: each row's physically valid
+  key window, which the fused decode kernel consumes without reading padding.
+  ``make_mask`` reproduces the reference's mask bit for bit, including its use
+  of the logical offset (pinned by the reference tests test_cache.py:291-333
+  and test_batch_rotating_cache.py:73-117).
 """
 
 from __future__ import annotations
 
-from typing import List, Optional, Sequence
+from typing import List
 
 import torch
 
@@ -39,91 +45,77 @@ __all__ = [
     "BatchQuantizedRotatingSDPACache",
 ]
 
+# slot granularity of every buffer: 8 tokens keep any plane's rows 16-byte
+# aligned; linear buffers round up to whole growth steps
+_ALIGN = 8
 
-# ------------------------------------------------------------- helpers ----
+
+def _round_up(n: int, m: int) -> int:
+    return (n + m - 1) // m * m
+
+
+def _i64(x) -> torch.Tensor:
+    return torch.as_tensor(x if not isinstance(x, torch.Tensor) else x.cpu(), dtype=torch.int64).reshape(-1)
+
+
+# ------------------------------------------------------------- masks ----
 
 def _create_causal_mask(N, offset, window_size=None, left_padding=None, device=None):
-    """Causal mask (restates mlx_qsdpa/cache.py:15-43).
+    """Boolean attention mask, True where query i may see key j.
 
-    ``offset`` int -> (N, offset+N); 1-D tensor -> (B, 1, N, max(offset)+N).
+    Same arrays as the reference's ``_create_causal_mask``
+    (mlx_qsdpa/cache.py:15-43).  ``offset`` an int: one sequence whose N
+    queries sit at positions offset..offset+N-1 -> (N, offset + N).  ``offset``
+    a 1-D tensor: one offset per batch row -> (B, 1, N, max(offset) + N), with
+    keys before a row's ``left_padding`` masked out.  ``window_size`` limits
+    how far back a query sees.
     """
-    if isinstance(offset, torch.Tensor) and offset.dim() > 0:
-        off = offset.to(torch.int64).cpu()
-        max_off = int(off.max().item())
-        total = max_off + N
-        q_pos = torch.arange(N)[None, :] + off[:, None]
-        k_pos = torch.arange(total)[None, :]
-        mask = q_pos[:, :, None] >= k_pos[:, None, :]
-        if left_padding is not None:
-            lp = left_padding.to(torch.int64).cpu()
-            mask = mask & (k_pos[:, None, :] >= lp[:, None, None])
-        if window_size is not None:
-            mask = mask & (q_pos[:, :, None] - k_pos[:, None, :] < window_size)
-        mask = mask[:, None, :, :]
-    else:
-        off = int(offset)
-        q_idx = torch.arange(off, off + N)
-        k_idx = torch.arange(off + N)
-        mask = q_idx[:, None] >= k_idx[None]
-        if window_size is not None:
-            mask = mask & (q_idx[:, None] - k_idx[None] < window_size)
+    per_row = isinstance(offset, torch.Tensor) and offset.dim() > 0
+    rows = _i64(offset) if per_row else torch.tensor([int(offset)])
+    n_keys = int(rows.max().item()) + N
+    q_pos = rows[:, None, None] + torch.arange(N)[None, :, None]  # (R, N, 1)
+    k_pos = torch.arange(n_keys)[None, None, :]                    # (1, 1, K)
+    keep = k_pos <= q_pos
+    if window_size is not None:
+        keep = keep & (q_pos - k_pos < window_size)
+    if per_row and left_padding is not None:
+        keep = keep & (k_pos >= _i64(left_padding)[:, None, None])
+    mask = keep[:, None] if per_row else keep[0]
     return mask.to(device) if device is not None else mask
 
 
-def _i32(t: torch.Tensor) -> torch.Tensor:
-    """uint32 buffers are handled through an int32 view for torch ops."""
-    return t.view(torch.int32) if t.dtype == torch.uint32 else t
+# ------------------------------------------------------------ storage ----
+
+def _alloc_planes(B, H, slots, k_dim, v_dim, bits, group_size, dtype, device, zero=True):
+    """((k_packed, k_scales, k_biases), (v_packed, v_scales, v_biases)) of `slots` tokens."""
+    make = torch.zeros if zero else torch.empty
+
+    def three(dim):
+        return (make((B, H, slots, dim * bits // 32), dtype=torch.uint32, device=device),
+                make((B, H, slots, dim // group_size), dtype=dtype, device=device),
+                make((B, H, slots, dim // group_size), dtype=dtype, device=device))
+
+    return three(k_dim), three(v_dim)
 
 
-def _u32(t: torch.Tensor) -> torch.Tensor:
-    return t.view(torch.uint32) if t.dtype == torch.int32 else t
+def _alloc_like(planes_k, planes_v, B, slots, zero=False):
+    """New (K, V) plane tuples shaped like the given ones, with B rows and `slots` tokens."""
+    def three(src):
+        make = torch.zeros if zero else torch.empty
+        return tuple(make((B, t.shape[1], slots, t.shape[3]), dtype=t.dtype, device=t.device) for t in src)
+
+    return three(planes_k), three(planes_v)
 
 
-def _cat(ts: Sequence[torch.Tensor], dim: int) -> torch.Tensor:
-    is_u32 = ts[0].dtype == torch.uint32
-    out = torch.cat([_i32(t) for t in ts], dim=dim)
-    return _u32(out) if is_u32 else out
-
-
-def _pad_tokens(t: torch.Tensor, left: int, right: int) -> torch.Tensor:
-    """Zero-pad the token axis (dim 2)."""
-    if left == 0 and right == 0:
-        return t
-    B, H, _, W = t.shape
-    parts = []
-    if left:
-        parts.append(torch.zeros((B, H, left, W), dtype=t.dtype, device=t.device))
-    parts.append(t)
-    if right:
-        parts.append(torch.zeros((B, H, right, W), dtype=t.dtype, device=t.device))
-    return _cat(parts, 2)
-
-
-def _index_batch(t: torch.Tensor, idx) -> torch.Tensor:
-    if isinstance(idx, torch.Tensor):
-        idx = idx.to(t.device)
-    return _u32(_i32(t)[idx]) if t.dtype == torch.uint32 else t[idx]
-
-
-def _alloc_quant(B, H, slots, dim, bits, group_size, dtype, device):
-    el_per_int = 32 // bits
-    return (
-        torch.zeros((B, H, slots, dim // el_per_int), dtype=torch.uint32, device=device),
-        torch.zeros((B, H, slots, dim // group_size), dtype=dtype, device=device),
-        torch.zeros((B, H, slots, dim // group_size), dtype=dtype, device=device),
-    )
+def _gather_into(dst_k, dst_v, sources, rows, T):
+    """One gather launch: destination row b takes its tokens from
+    ``sources[b] = (cache_k, cache_v, row)`` as described by ``rows[b] =
+    (shift, lo, hi, mod)``; tokens [0, T) outside [lo, hi) become zero."""
+    _lib.gather_rows(list(dst_k) + list(dst_v), [(list(k) + list(v), r) for k, v, r in sources], rows, T)
 
 
 def _tuple_nbytes(tuples) -> int:
     return sum(t.numel() * t.element_size() for t in tuples)
-
-
-def _dynamic_roll(t: torch.Tensor, shifts: torch.Tensor) -> torch.Tensor:
-    """Roll each batch row of t along the token axis by shifts[b] (cache.py:46-51)."""
-    n = t.shape[2]
-    idx = (torch.arange(n)[None, :] - shifts.to(torch.int64).cpu()[:, None]) % n  # (B, n)
-    idx = idx.to(t.device)[:, None, :, None].expand(t.shape[0], t.shape[1], n, t.shape[3])
-    return _u32(torch.gather(_i32(t), 2, idx))
 
 
 def _quantize(cache, x: torch.Tensor, bufs, slot0: int, ring: bool = False):
@@ -132,8 +124,37 @@ def _quantize(cache, x: torch.Tensor, bufs, slot0: int, ring: bool = False):
 
 def _dequant(cache, bufs, n_visible: int, start: int = 0, mod: int = 0) -> torch.Tensor:
     p, s, b = (t[:, :, :n_visible] for t in bufs)
-    return _lib.dequantize(p, s, b, cache.bits, cache.group_size, n_out=n_visible,
-                           src_start=start, src_mod=mod)
+    return _lib.dequantize(p, s, b, cache.bits, cache.group_size, n_out=n_visible, src_start=start, src_mod=mod)
+
+
+def _view(tuples, n):
+    return tuple(t[..., :n, :] for t in tuples)
+
+
+class _LinearStore:
+    """Growth of a linear (append-only) buffer of token slots."""
+
+    @staticmethod
+    def grain(step: int) -> int:
+        return _round_up(max(int(step), 1), _ALIGN)
+
+    @staticmethod
+    def ensure(cache, used: int, needed: int, like: torch.Tensor, k_dim: int, v_dim: int, B: int, H: int):
+        """Make room for `needed` tokens, keeping the first `used` in place."""
+        grain = _LinearStore.grain(cache.step)
+        if cache._keys is None:
+            slots = _round_up(max(needed, 1), grain)
+            cache._keys, cache._values = _alloc_planes(B, H, slots, k_dim, v_dim, cache.bits, cache.group_size,
+                                                       like.dtype, like.device)
+            return
+        slots = cache._keys[0].shape[2]
+        if needed <= slots:
+            return
+        new_slots = _round_up(max(needed, slots + slots // 4), grain)
+        nk, nv = _alloc_like(cache._keys, cache._values, cache._keys[0].shape[0], new_slots)
+        n = cache._keys[0].shape[0]
+        _gather_into(nk, nv, [(cache._keys, cache._values, b) for b in range(n)], [(0, 0, used, 0)] * n, new_slots)
+        cache._keys, cache._values = nk, nv
 
 
 # ------------------------------------------------------ linear cache ----
@@ -143,13 +164,13 @@ class QuantizedSDPACache:
 
     ``update_and_fetch`` returns quantized tuples
     ``(packed_uint32, scales, biases)`` for keys and values covering tokens
-    ``[0, offset)``.  Buffers grow by ``step`` tokens exactly as the
-    reference's ``_grow`` does, so ``nbytes`` and the returned shapes match.
+    ``[0, offset)``.  The buffer grows in multiples of ``step`` tokens, by at
+    least a quarter of its size each time.
 
     Args:
         bits: 4 or 8.
         group_size: 32, 64 or 128.
-        step: buffer growth step in tokens.
+        step: growth granularity in tokens.
     """
 
     _use_fused_sdpa = True
@@ -195,26 +216,31 @@ class QuantizedSDPACache:
     def make_mask(self, N, return_array=False, window_size=None):
         if window_size is not None:
             return _create_causal_mask(N, self.offset, window_size=window_size, device=self._device())
-        elif N == 1:
+        if N == 1:
             return None
-        elif return_array:
+        if return_array:
             return _create_causal_mask(N, self.offset, device=self._device())
-        else:
-            return "causal"
+        return "causal"
 
     @property
     def state(self):
         if self._keys is None:
             return None, None
-        k = tuple(t[..., : self.offset, :] for t in self._keys)
-        v = tuple(t[..., : self.offset, :] for t in self._values)
-        return k, v
+        return _view(self._keys, self.offset), _view(self._values, self.offset)
 
     @state.setter
     def state(self, v):
         keys, values = v
-        self._keys = keys
-        self._values = values
+        if keys is None:
+            self._keys = self._values = None
+            return
+        # restored buffers move into aligned slots (the fused kernels read them in place)
+        n = keys[0].shape[2]
+        slots = _round_up(max(n, 1), _LinearStore.grain(getattr(self, "step", 256)))
+        nk, nv = _alloc_like(keys, values, keys[0].shape[0], slots)
+        _gather_into(nk, nv, [(keys, values, b) for b in range(keys[0].shape[0])],
+                     [(0, 0, n, 0)] * keys[0].shape[0], slots)
+        self._keys, self._values = nk, nv
 
     @property
     def meta_state(self):
@@ -238,32 +264,13 @@ class QuantizedSDPACache:
 
     def update_and_fetch(self, keys, values):
         """Quantize and append keys/values (B, H_kv, S, D); return views [0, offset)."""
-        B, n_kv_heads, num_steps, k_head_dim = keys.shape
-        v_head_dim = values.shape[-1]
+        B, H, S, k_dim = keys.shape
         prev = self.offset
-        if self._keys is None or (prev + num_steps) > self._keys[0].shape[2]:
-            self._grow(B, n_kv_heads, num_steps, k_head_dim, v_head_dim, keys.dtype, prev, keys.device)
-        self.offset += num_steps
+        _LinearStore.ensure(self, prev, prev + S, keys, k_dim, values.shape[-1], B, H)
+        self.offset += S
         _quantize(self, keys, self._keys, prev)
         _quantize(self, values, self._values, prev)
-        k_out = tuple(t[..., : self.offset, :] for t in self._keys)
-        v_out = tuple(t[..., : self.offset, :] for t in self._values)
-        return k_out, v_out
-
-    def _grow(self, B, n_kv_heads, num_steps, k_head_dim, v_head_dim, dtype, prev, device):
-        """Grow by ceil(S/step)*step slots (cache.py:199-231)."""
-        new_alloc = ((self.step + num_steps - 1) // self.step) * self.step
-        new_k = _alloc_quant(B, n_kv_heads, new_alloc, k_head_dim, self.bits, self.group_size, dtype, device)
-        new_v = _alloc_quant(B, n_kv_heads, new_alloc, v_head_dim, self.bits, self.group_size, dtype, device)
-        if self._keys is not None:
-            if prev % self.step != 0:
-                self._keys = tuple(t[..., :prev, :] for t in self._keys)
-                self._values = tuple(t[..., :prev, :] for t in self._values)
-            self._keys = tuple(_cat([o, n], 2) for o, n in zip(self._keys, new_k))
-            self._values = tuple(_cat([o, n], 2) for o, n in zip(self._values, new_v))
-        else:
-            self._keys = new_k
-            self._values = new_v
+        return _view(self._keys, self.offset), _view(self._values, self.offset)
 
 
 # ------------------------------------------------------- batch cache ----
@@ -277,7 +284,7 @@ class BatchQuantizedSDPACache:
     def __init__(self, left_padding: List[int], bits: int = 4, group_size: int = 32):
         self.bits = bits
         self.group_size = group_size
-        self.left_padding = torch.as_tensor(list(left_padding), dtype=torch.int64)
+        self.left_padding = _i64(left_padding)
         self.offset = -self.left_padding.clone()
         self._idx = 0
         self._keys = None
@@ -308,66 +315,71 @@ class BatchQuantizedSDPACache:
     def _device(self):
         return self._keys[0].device if self._keys is not None else None
 
+    def _rows(self):
+        return self._keys[0].shape[0]
+
     def update_and_fetch(self, keys, values):
-        B, n_kv_heads, num_steps, k_head_dim = keys.shape
-        v_head_dim = values.shape[-1]
+        B, H, S, k_dim = keys.shape
         prev = self._idx
-        if self._keys is None or (prev + num_steps) > self._keys[0].shape[2]:
-            new_alloc = ((self.step + num_steps - 1) // self.step) * self.step
-            new_k = _alloc_quant(B, n_kv_heads, new_alloc, k_head_dim, self.bits, self.group_size,
-                                 keys.dtype, keys.device)
-            new_v = _alloc_quant(B, n_kv_heads, new_alloc, v_head_dim, self.bits, self.group_size,
-                                 keys.dtype, keys.device)
-            if self._keys is not None:
-                if prev % self.step != 0:
-                    self._keys = tuple(t[..., :prev, :] for t in self._keys)
-                    self._values = tuple(t[..., :prev, :] for t in self._values)
-                self._keys = tuple(_cat([o, n], 2) for o, n in zip(self._keys, new_k))
-                self._values = tuple(_cat([o, n], 2) for o, n in zip(self._values, new_v))
-            else:
-                self._keys = new_k
-                self._values = new_v
-        self.offset = self.offset + num_steps
-        self._idx += num_steps
+        _LinearStore.ensure(self, prev, prev + S, keys, k_dim, values.shape[-1], B, H)
+        self.offset = self.offset + S
+        self._idx += S
         _quantize(self, keys, self._keys, prev)
         _quantize(self, values, self._values, prev)
-        k_out = tuple(t[..., : self._idx, :] for t in self._keys)
-        v_out = tuple(t[..., : self._idx, :] for t in self._values)
-        return k_out, v_out
+        return _view(self._keys, self._idx), _view(self._values, self._idx)
 
     def prepare(self, *, left_padding=None, lengths=None, right_padding=None):
         if left_padding is not None:
             if self._keys is not None:
                 raise ValueError("Left padding can only be added to an empty BatchQuantizedSDPACache")
-            left_padding = torch.as_tensor(list(left_padding), dtype=torch.int64)
-            self.left_padding = self.left_padding + left_padding
-            self.offset = self.offset - left_padding
+            extra = _i64(left_padding)
+            self.left_padding = self.left_padding + extra
+            self.offset = self.offset - extra
         if right_padding is not None and max(right_padding) > 0:
-            self._right_padding = torch.as_tensor(list(right_padding), dtype=torch.int64)
+            self._right_padding = _i64(right_padding)
 
     def finalize(self):
-        if self._right_padding is not None:
-            padding = self._right_padding
-            self._keys = tuple(_dynamic_roll(t, padding) for t in self._keys)
-            self._values = tuple(_dynamic_roll(t, padding) for t in self._values)
-            self.offset = self.offset - padding
-            self.left_padding = self.left_padding + padding
-            self._right_padding = None
+        """Move each row's right padding in front of its tokens (cache.py:337-348).
+
+        Row b's written tokens [0, _idx) rotate right by its right padding, so
+        the padding becomes left padding; the reference rotates the whole
+        buffer, which differs only in the slots that turn into padding (every
+        mask excludes them).
+        """
+        if self._right_padding is None:
+            return
+        pad = self._right_padding
+        if self._keys is not None and self._idx > 0:
+            n = self._rows()
+            nk, nv = _alloc_like(self._keys, self._values, n, self._keys[0].shape[2])
+            _gather_into(nk, nv, [(self._keys, self._values, b) for b in range(n)],
+                         [(int(pad[b]), 0, self._idx, self._idx) for b in range(n)], self._keys[0].shape[2])
+            self._keys, self._values = nk, nv
+        self.offset = self.offset - pad
+        self.left_padding = self.left_padding + pad
+        self._right_padding = None
 
     @property
     def state(self):
         if self._keys is None:
             return None, None, self.offset, self.left_padding
-        keys, values = self._keys, self._values
-        if self._idx < keys[0].shape[2]:
-            keys = tuple(t[..., : self._idx, :] for t in keys)
-            values = tuple(t[..., : self._idx, :] for t in values)
-        return keys, values, self.offset, self.left_padding
+        return _view(self._keys, self._idx), _view(self._values, self._idx), self.offset, self.left_padding
 
     @state.setter
     def state(self, v):
-        self._keys, self._values, self.offset, self.left_padding = v
-        self._idx = 0 if self._keys is None else self._keys[0].shape[2]
+        keys, values, self.offset, self.left_padding = v
+        self.offset = _i64(self.offset)
+        self.left_padding = _i64(self.left_padding)
+        if keys is None:
+            self._keys = self._values = None
+            self._idx = 0
+            return
+        self._idx = keys[0].shape[2]
+        n = keys[0].shape[0]
+        slots = _round_up(max(self._idx, 1), _LinearStore.grain(self.step))
+        nk, nv = _alloc_like(keys, values, n, slots)
+        _gather_into(nk, nv, [(keys, values, b) for b in range(n)], [(0, 0, self._idx, 0)] * n, slots)
+        self._keys, self._values = nk, nv
 
     def make_mask(self, N, return_array=False, **kwargs):
         """Causal mask with left-padding awareness (cache.py:369-376)."""
@@ -382,94 +394,96 @@ class BatchQuantizedSDPACache:
         return r.to(self._device()) if self._device() is not None else r
 
     def filter(self, batch_indices):
+        """Keep the given rows (cache.py:378-391); slots every kept row pads drop."""
+        idx = _i64(batch_indices)
+        keep_lp = self.left_padding[idx]
+        drop = int(keep_lp.min().item()) if idx.numel() else 0
         if self._keys is not None:
-            self._keys = tuple(_index_batch(t, batch_indices) for t in self._keys)
-            self._values = tuple(_index_batch(t, batch_indices) for t in self._values)
-        idx = torch.as_tensor(batch_indices).cpu()
+            n = idx.numel()
+            new_idx = self._idx - drop
+            slots = _round_up(max(new_idx, 1), _LinearStore.grain(self.step))
+            nk, nv = _alloc_like(self._keys, self._values, n, slots)
+            _gather_into(nk, nv, [(self._keys, self._values, int(i)) for i in idx],
+                         [(-drop, 0, new_idx, 0)] * n, slots)
+            self._keys, self._values = nk, nv
+            self._idx = new_idx
         self.offset = self.offset[idx]
-        self.left_padding = self.left_padding[idx]
-        min_pad = int(self.left_padding.min().item())
-        if min_pad > 0:
-            self._keys = tuple(t[..., min_pad:, :] for t in self._keys)
-            self._values = tuple(t[..., min_pad:, :] for t in self._values)
-            self._idx -= min_pad
-            self.left_padding = self.left_padding - min_pad
+        self.left_padding = keep_lp - drop
 
     def extend(self, other):
-        max_idx = max(self._idx, other._idx)
-        max_size = max(self._keys[0].shape[2], other._keys[0].shape[2])
-
-        def pad_quant(c_idx, tuples):
-            left = max_idx - c_idx
-            right = max_size - tuples[0].shape[2] - left
-            result = []
-            for t in tuples:
-                tr = t
-                if right < 0:
-                    tr = tr[..., :right, :]
-                    right_actual = 0
-                else:
-                    right_actual = right
-                result.append(_pad_tokens(tr, left, right_actual))
-            return tuple(result), left
-
-        sk, s_left = pad_quant(self._idx, self._keys)
-        sv, _ = pad_quant(self._idx, self._values)
-        ok, o_left = pad_quant(other._idx, other._keys)
-        ov, _ = pad_quant(other._idx, other._values)
-        self._keys = tuple(_cat([s, o], 0) for s, o in zip(sk, ok))
-        self._values = tuple(_cat([s, o], 0) for s, o in zip(sv, ov))
+        """Append the rows of another batch cache (cache.py:393-428): the
+        shorter side's tokens move right so both end at the same slot."""
+        end = max(self._idx, other._idx)
+        shift_self, shift_other = end - self._idx, end - other._idx
+        sides = [(c, s) for c, s in ((self, shift_self), (other, shift_other)) if c._keys is not None]
+        if sides:
+            ref = sides[0][0]
+            n = sum(c._rows() for c, _ in sides)
+            slots = _round_up(max(end, 1), _LinearStore.grain(self.step))
+            nk, nv = _alloc_like(ref._keys, ref._values, n, slots)
+            sources, rows = [], []
+            for c, s in sides:
+                for b in range(c._rows()):
+                    sources.append((c._keys, c._values, b))
+                    rows.append((s, s, end, 0))
+            _gather_into(nk, nv, sources, rows, slots)
+            self._keys, self._values = nk, nv
         self.offset = torch.cat([self.offset, other.offset])
-        self.left_padding = torch.cat([self.left_padding + s_left, other.left_padding + o_left])
-        self._idx = max_idx
+        self.left_padding = torch.cat([self.left_padding + shift_self, other.left_padding + shift_other])
+        self._idx = end
 
     def extract(self, idx):
+        """Row `idx` as a QuantizedSDPACache (cache.py:429-445)."""
         cache = QuantizedSDPACache(bits=self.bits, group_size=self.group_size)
         if self._keys is None:
             return cache
-        padding = int(self.left_padding[idx].item())
-        cache._keys = tuple(t[idx:idx + 1, :, padding:self._idx].contiguous() for t in self._keys)
-        cache._values = tuple(t[idx:idx + 1, :, padding:self._idx].contiguous() for t in self._values)
-        cache.offset = self._idx - padding
+        pad = int(self.left_padding[idx].item())
+        n = max(self._idx - pad, 0)
+        slots = _round_up(max(n, 1), _LinearStore.grain(cache.step))
+        nk, nv = _alloc_like(self._keys, self._values, 1, slots)
+        _gather_into(nk, nv, [(self._keys, self._values, int(idx))], [(-pad, 0, n, 0)], slots)
+        cache._keys, cache._values = nk, nv
+        cache.offset = n
         return cache
 
     @classmethod
     def merge(cls, caches):
-        """Right-align single-request caches into one batch (cache.py:446-492)."""
+        """Right-align single-request caches into one batch (cache.py:446-492).
+
+        Row i holds cache i's tokens in slots [max_len - len_i, max_len); one
+        gather launch fills every row.  The slots leave room for the next
+        append.
+        """
         if not caches:
             return cls([0])
-        bits = caches[0].bits
-        gs = caches[0].group_size
         lengths = [c.offset for c in caches]
         max_len = max(lengths)
-        padding = [max_len - l for l in lengths]
-        batch = cls(padding, bits=bits, group_size=gs)
-        if all(c.empty() for c in caches):
+        padding = [max_len - n for n in lengths]
+        batch = cls(padding, bits=caches[0].bits, group_size=caches[0].group_size)
+        filled = [c for c in caches if not c.empty()]
+        if not filled:
             return batch
-        B = len(caches)
-        ref = next(c for c in caches if not c.empty())
-        H = ref._keys[0].shape[1]
-        dev = ref._keys[0].device
-        dtype = ref._keys[1].dtype
-
-        def alloc(src):
-            return tuple(torch.zeros((B, H, max_len, t.shape[3]), dtype=t.dtype, device=dev) for t in src)
-
-        batch._keys = alloc(ref._keys)
-        batch._values = alloc(ref._values)
-        for i, (p, c) in enumerate(zip(padding, caches)):
-            if c.empty():
-                continue
-            for j in range(3):
-                _i32(batch._keys[j])[i:i + 1, :, p:p + c.offset] = _i32(c._keys[j][..., : c.offset, :])
-                _i32(batch._values[j])[i:i + 1, :, p:p + c.offset] = _i32(c._values[j][..., : c.offset, :])
+        ref = filled[0]
+        slots = _round_up(max_len + 1, _LinearStore.grain(cls.step))
+        nk, nv = _alloc_like(ref._keys, ref._values, len(caches), slots)
+        sources, rows = [], []
+        for p, c in zip(padding, caches):
+            src = c if not c.empty() else ref
+            sources.append((src._keys, src._values, 0))
+            rows.append((p, p, max_len, 0) if not c.empty() else (0, 0, 0, 0))
+        _gather_into(nk, nv, sources, rows, slots)
+        batch._keys, batch._values = nk, nv
         batch.offset = batch.offset + max_len
         batch._idx = max_len
-        del dtype
         return batch
 
 
 # ----------------------------------------------------- rotating cache ----
+
+def _ring_slots(max_size: int) -> int:
+    """Physical slots of a ring of `max_size` tokens (rows stay aligned)."""
+    return _round_up(max(max_size, 1), _ALIGN)
+
 
 class QuantizedRotatingSDPACache:
     """Fixed-size circular quantized cache (mlx_qsdpa/cache.py:495-711).
@@ -514,74 +528,62 @@ class QuantizedRotatingSDPACache:
     def _device(self):
         return self._keys[0].device if self._keys is not None else None
 
-    def _alloc(self, B, n_kv_heads, k_head_dim, v_head_dim, dtype, device):
-        self._keys = _alloc_quant(B, n_kv_heads, self.max_size, k_head_dim, self.bits, self.group_size, dtype,
-                                  device)
-        self._values = _alloc_quant(B, n_kv_heads, self.max_size, v_head_dim, self.bits, self.group_size, dtype,
-                                    device)
-
     def update_and_fetch(self, keys, values):
-        B, n_kv_heads, S, k_head_dim = keys.shape
-        v_head_dim = values.shape[-1]
+        B, H, S, k_dim = keys.shape
         if self._keys is None:
-            self._alloc(B, n_kv_heads, k_head_dim, v_head_dim, keys.dtype, keys.device)
+            self._keys, self._values = _alloc_planes(B, H, _ring_slots(self.max_size), k_dim, values.shape[-1],
+                                                     self.bits, self.group_size, keys.dtype, keys.device)
         if S == 1:
             return self._update_decode(keys, values)
         return self._update_prefill(keys, values)
 
     def _update_decode(self, keys, values):
         """cache.py:574-591."""
-        write_pos = self._idx % self.max_size
-        _quantize(self, keys, self._keys, write_pos)
-        _quantize(self, values, self._values, write_pos)
+        slot = self._idx % self.max_size
+        _quantize(self, keys, self._keys, slot)
+        _quantize(self, values, self._values, slot)
         self._idx += 1
         self.offset += 1
         if self._idx > self.max_size:
-            self._idx = self._idx % self.max_size
-        n_visible = min(self.offset, self.max_size)
-        k_out = tuple(t[..., :n_visible, :] for t in self._keys)
-        v_out = tuple(t[..., :n_visible, :] for t in self._values)
-        return k_out, v_out
+            self._idx %= self.max_size
+        n = min(self.offset, self.max_size)
+        return _view(self._keys, n), _view(self._values, n)
 
     def _update_prefill(self, keys, values):
-        """cache.py:593-620."""
+        """cache.py:593-620: window in temporal order + new tokens, last
+        max_size kept, re-quantised from slot 0."""
         S = keys.shape[2]
         if self.offset > 0:
-            existing_k = self._dequant_temporal(self._keys)
-            existing_v = self._dequant_temporal(self._values)
-            all_k = torch.cat([existing_k, keys.to(existing_k.dtype)], dim=2)
-            all_v = torch.cat([existing_v, values.to(existing_v.dtype)], dim=2)
-        else:
-            all_k, all_v = keys, values
-        total = all_k.shape[2]
+            old_k = self._dequant_temporal(self._keys)
+            old_v = self._dequant_temporal(self._values)
+            keys = torch.cat([old_k, keys.to(old_k.dtype)], dim=2)
+            values = torch.cat([old_v, values.to(old_v.dtype)], dim=2)
+        total = keys.shape[2]
         if total > self.max_size:
-            all_k = all_k[..., total - self.max_size:, :]
-            all_v = all_v[..., total - self.max_size:, :]
+            keys = keys[..., total - self.max_size:, :]
+            values = values[..., total - self.max_size:, :]
             total = self.max_size
-        _quantize(self, all_k, self._keys, 0)
-        _quantize(self, all_v, self._values, 0)
+        _quantize(self, keys, self._keys, 0)
+        _quantize(self, values, self._values, 0)
         self.offset += S
         self._idx = total % self.max_size
-        n_visible = min(self.offset, self.max_size)
-        k_out = tuple(t[..., :n_visible, :] for t in self._keys)
-        v_out = tuple(t[..., :n_visible, :] for t in self._values)
-        return k_out, v_out
+        n = min(self.offset, self.max_size)
+        return _view(self._keys, n), _view(self._values, n)
 
     def _dequant_temporal(self, quant_tuple):
         """Dequantise the visible window in temporal order (cache.py:622-634)."""
-        n_visible = min(self.offset, self.max_size)
+        n = min(self.offset, self.max_size)
         if self.offset > self.max_size and self._idx > 0:
-            return _dequant(self, quant_tuple, n_visible, start=self._idx, mod=n_visible)
-        return _dequant(self, quant_tuple, n_visible)
+            return _dequant(self, quant_tuple, n, start=self._idx, mod=n)
+        return _dequant(self, quant_tuple, n)
 
     def make_mask(self, N, return_array=False, window_size=None):
         effective = min(self.offset, self.max_size)
         if N == 1:
             return None
-        elif return_array or window_size is not None:
+        if return_array or window_size is not None:
             return _create_causal_mask(N, effective, window_size=window_size, device=self._device())
-        else:
-            return "causal"
+        return "causal"
 
     def trim(self, n):
         n = min(self.offset, n)
@@ -602,32 +604,29 @@ class QuantizedRotatingSDPACache:
         """Cached tensors in temporal order (cache.py:662-678)."""
         if self._keys is None:
             return None, None
-        n_visible = min(self.offset, self.max_size)
+        n = min(self.offset, self.max_size)
         if self.offset > self.max_size and self._idx > 0:
-            def reorder(tuples):
-                return tuple(_cat([t[..., self._idx:n_visible, :], t[..., : self._idx, :]], 2) for t in tuples)
-
-            return reorder(self._keys), reorder(self._values)
-        k = tuple(t[..., :n_visible, :] for t in self._keys)
-        v = tuple(t[..., :n_visible, :] for t in self._values)
-        return k, v
+            # the oldest token sits at slot _idx
+            nk, nv = _alloc_like(self._keys, self._values, self._keys[0].shape[0], _round_up(max(n, 1), _ALIGN))
+            rows = self._keys[0].shape[0]
+            _gather_into(nk, nv, [(self._keys, self._values, b) for b in range(rows)],
+                         [(-self._idx, 0, n, n)] * rows, n)
+            return _view(nk, n), _view(nv, n)
+        return _view(self._keys, n), _view(self._values, n)
 
     @state.setter
     def state(self, v):
-        """Restore from a temporal-order snapshot, re-expanded to max_size (cache.py:680-711)."""
+        """Restore a temporal-order snapshot into a ring of max_size slots (cache.py:680-711)."""
         keys, values = v
         if keys is None:
-            self._keys = None
-            self._values = None
+            self._keys = self._values = None
             return
-        n_visible = keys[0].shape[2]
-        pad_len = self.max_size - n_visible
-        if pad_len <= 0:
-            self._keys = keys
-            self._values = values
-            return
-        self._keys = tuple(_pad_tokens(t, 0, pad_len) for t in keys)
-        self._values = tuple(_pad_tokens(t, 0, pad_len) for t in values)
+        n = keys[0].shape[2]
+        rows = keys[0].shape[0]
+        slots = max(_ring_slots(self.max_size), _round_up(n, _ALIGN))
+        nk, nv = _alloc_like(keys, values, rows, slots)
+        _gather_into(nk, nv, [(keys, values, b) for b in range(rows)], [(0, 0, n, 0)] * rows, slots)
+        self._keys, self._values = nk, nv
 
 
 # ----------------------------------------------- batch rotating cache ----
@@ -650,7 +649,7 @@ class BatchQuantizedRotatingSDPACache:
         self.keep = keep
         self.bits = bits
         self.group_size = group_size
-        self.left_padding = torch.as_tensor(list(left_padding), dtype=torch.int64)
+        self.left_padding = _i64(left_padding)
         self.offset = -self.left_padding.clone()
         self._idx = 0
         self._keys = None
@@ -682,67 +681,57 @@ class BatchQuantizedRotatingSDPACache:
         return self._keys[0].device if self._keys is not None else None
 
     def update_and_fetch(self, keys, values):
-        B, n_kv_heads, S, k_head_dim = keys.shape
-        v_head_dim = values.shape[-1]
+        B, H, S, k_dim = keys.shape
         if self._keys is None:
-            self._keys = _alloc_quant(B, n_kv_heads, self.max_size, k_head_dim, self.bits, self.group_size,
-                                      keys.dtype, keys.device)
-            self._values = _alloc_quant(B, n_kv_heads, self.max_size, v_head_dim, self.bits, self.group_size,
-                                        keys.dtype, keys.device)
+            self._keys, self._values = _alloc_planes(B, H, _ring_slots(self.max_size), k_dim, values.shape[-1],
+                                                     self.bits, self.group_size, keys.dtype, keys.device)
         if S == 1:
             return self._update_decode(keys, values)
         return self._update_prefill(keys, values)
 
     def _update_decode(self, keys, values):
         """cache.py:796-811."""
-        write_pos = self._idx % self.max_size
+        slot = self._idx % self.max_size
         if self._idx >= self.max_size:
             # the write replaces each row's oldest visible slot
             self._pad = (self._pad - 1).clamp(min=0)
-        _quantize(self, keys, self._keys, write_pos)
-        _quantize(self, values, self._values, write_pos)
+        _quantize(self, keys, self._keys, slot)
+        _quantize(self, values, self._values, slot)
         self.offset = self.offset + 1
         self._idx += 1
-        n_visible = min(self._idx, self.max_size)
-        k_out = tuple(t[..., :n_visible, :] for t in self._keys)
-        v_out = tuple(t[..., :n_visible, :] for t in self._values)
-        return k_out, v_out
+        n = min(self._idx, self.max_size)
+        return _view(self._keys, n), _view(self._values, n)
 
     def _update_prefill(self, keys, values):
         """cache.py:813-840."""
-        n_vis = min(self._idx, self.max_size)
         if self._idx > 0:
-            existing_k = self._dequant_temporal(self._keys)
-            existing_v = self._dequant_temporal(self._values)
-            all_k = torch.cat([existing_k, keys.to(existing_k.dtype)], dim=2)
-            all_v = torch.cat([existing_v, values.to(existing_v.dtype)], dim=2)
+            old_k = self._dequant_temporal(self._keys)
+            old_v = self._dequant_temporal(self._values)
+            all_k = torch.cat([old_k, keys.to(old_k.dtype)], dim=2)
+            all_v = torch.cat([old_v, values.to(old_v.dtype)], dim=2)
         else:
             all_k, all_v = keys, values
-            n_vis = 0
         total = all_k.shape[2]
         if total > self.max_size:
             dropped = total - self.max_size
-            all_k = all_k[..., total - self.max_size:, :]
-            all_v = all_v[..., total - self.max_size:, :]
+            all_k = all_k[..., dropped:, :]
+            all_v = all_v[..., dropped:, :]
             total = self.max_size
             self._pad = (self._pad - dropped).clamp(min=0)
         _quantize(self, all_k, self._keys, 0)
         _quantize(self, all_v, self._values, 0)
         self.offset = self.offset + keys.shape[2]
         self._idx = total
-        del n_vis
-        k_out = tuple(t[..., :total, :] for t in self._keys)
-        v_out = tuple(t[..., :total, :] for t in self._values)
-        return k_out, v_out
+        return _view(self._keys, total), _view(self._values, total)
 
     def _dequant_temporal(self, quant_tuple):
         """Visible tokens in chronological order (cache.py:842-857)."""
-        n_visible = min(self._idx, self.max_size)
+        n = min(self._idx, self.max_size)
         if self._idx > self.max_size:
             write_pos = self._idx % self.max_size
             if write_pos > 0:
-                return _dequant(self, quant_tuple, n_visible, start=write_pos, mod=n_visible)
-        return _dequant(self, quant_tuple, n_visible)
+                return _dequant(self, quant_tuple, n, start=write_pos, mod=n)
+        return _dequant(self, quant_tuple, n)
 
     def make_mask(self, N, return_array=False, **kwargs):
         """cache.py:859-866."""
@@ -752,56 +741,53 @@ class BatchQuantizedRotatingSDPACache:
 
     def kv_ranges(self) -> KVRanges:
         """Each row's valid ring window over the visible slots (padding excluded)."""
-        n_vis = min(self._idx, self.max_size)
+        n = min(self._idx, self.max_size)
         oldest = self._idx % self.max_size if self._idx >= self.max_size else 0
-        pad = self._pad.clamp(min=0, max=n_vis)
-        start = (oldest + pad) % max(n_vis, 1)
-        length = n_vis - pad
+        pad = self._pad.clamp(min=0, max=n)
+        start = (oldest + pad) % max(n, 1)
+        length = n - pad
         r = KVRanges(start, length)
         return r.to(self._device()) if self._device() is not None else r
 
     def filter(self, batch_indices):
+        """Keep the given rows (cache.py:868-876)."""
+        idx = _i64(batch_indices)
         if self._keys is not None:
-            self._keys = tuple(_index_batch(t, batch_indices) for t in self._keys)
-            self._values = tuple(_index_batch(t, batch_indices) for t in self._values)
-        idx = torch.as_tensor(batch_indices).cpu()
+            slots = self._keys[0].shape[2]
+            nk, nv = _alloc_like(self._keys, self._values, idx.numel(), slots)
+            _gather_into(nk, nv, [(self._keys, self._values, int(i)) for i in idx],
+                         [(0, 0, slots, 0)] * idx.numel(), slots)
+            self._keys, self._values = nk, nv
         self.offset = self.offset[idx]
         self.left_padding = self.left_padding[idx]
         self._pad = self._pad[idx]
 
     def extend(self, other):
-        if self._keys is None and other._keys is None:
-            self.offset = torch.cat([self.offset, other.offset])
-            self.left_padding = torch.cat([self.left_padding, other.left_padding])
-            self._pad = torch.cat([self._pad, other._pad])
-            return
-        max_idx = max(self._idx, other._idx)
-
-        def pad_quant(tuples, c_idx):
-            left = max_idx - c_idx
-            if left == 0:
-                return tuples
-            return tuple(_pad_tokens(t, left, 0) for t in tuples)
-
-        sk = pad_quant(self._keys, self._idx) if self._keys is not None else None
-        sv = pad_quant(self._values, self._idx) if self._values is not None else None
-        ok = pad_quant(other._keys, other._idx) if other._keys is not None else None
-        ov = pad_quant(other._values, other._idx) if other._values is not None else None
-        if sk is not None and ok is not None:
-            self._keys = tuple(_cat([s, o], 0) for s, o in zip(sk, ok))
-            self._values = tuple(_cat([s, o], 0) for s, o in zip(sv, ov))
-        elif ok is not None:
-            self._keys = ok
-            self._values = ov
-        s_left = max_idx - self._idx
-        o_left = max_idx - other._idx
+        """Append the rows of another batch rotating cache (cache.py:878-912):
+        the side with fewer writes moves right by the difference (slots past
+        the ring are never visible and are dropped)."""
+        end = max(self._idx, other._idx)
+        shift_self, shift_other = end - self._idx, end - other._idx
+        sides = [(c, s) for c, s in ((self, shift_self), (other, shift_other)) if c._keys is not None]
+        if sides:
+            ref = sides[0][0]
+            n = sum(c._keys[0].shape[0] for c, _ in sides)
+            slots = max(c._keys[0].shape[2] for c, _ in sides)
+            nk, nv = _alloc_like(ref._keys, ref._values, n, slots)
+            sources, rows = [], []
+            for c, s in sides:
+                for b in range(c._keys[0].shape[0]):
+                    sources.append((c._keys, c._values, b))
+                    rows.append((s, s, min(slots, c._keys[0].shape[2] + s), 0))
+            _gather_into(nk, nv, sources, rows, slots)
+            self._keys, self._values = nk, nv
         self.offset = torch.cat([self.offset, other.offset])
-        self.left_padding = torch.cat([self.left_padding + s_left, other.left_padding + o_left])
-        self._pad = torch.cat([self._pad + s_left, other._pad + o_left])
-        self._idx = max_idx
+        self.left_padding = torch.cat([self.left_padding + shift_self, other.left_padding + shift_other])
+        self._pad = torch.cat([self._pad + shift_self, other._pad + shift_other])
+        self._idx = end
 
     def extract(self, idx):
-        """One row as a QuantizedRotatingSDPACache in temporal order (cache.py:914-961)."""
+        """Row `idx` as a QuantizedRotatingSDPACache in temporal order (cache.py:914-961)."""
         cache = QuantizedRotatingSDPACache(max_size=self.max_size, bits=self.bits, group_size=self.group_size)
         if self._keys is None:
             return cache
@@ -809,67 +795,55 @@ class BatchQuantizedRotatingSDPACache:
         n_tokens = max(0, min(int(self.offset[idx].item()), self.max_size))
         if n_tokens == 0:
             return cache
-
-        def extract_temporal(tuples):
-            result = tuple(t[idx:idx + 1, :, :visible, :].contiguous() for t in tuples)
-            if self._idx > self.max_size:
-                write_pos = self._idx % self.max_size
-                if write_pos > 0:
-                    result = tuple(_cat([t[..., write_pos:, :], t[..., :write_pos, :]], 2) for t in result)
-            padding = visible - n_tokens
-            if padding > 0:
-                result = tuple(t[..., padding:visible, :].contiguous() for t in result)
-            return result
-
-        cache._keys = extract_temporal(self._keys)
-        cache._values = extract_temporal(self._values)
+        # temporal order (oldest slot first), then the row's padding dropped
+        wrapped = self._idx > self.max_size
+        oldest = self._idx % self.max_size if wrapped else 0
+        skip = visible - n_tokens
+        slots = _ring_slots(self.max_size)
+        nk, nv = _alloc_like(self._keys, self._values, 1, slots)
+        _gather_into(nk, nv, [(self._keys, self._values, int(idx))],
+                     [(-(oldest + skip), 0, n_tokens, visible if oldest else 0)], slots)
+        cache._keys, cache._values = nk, nv
         cache.offset = n_tokens
         cache._idx = n_tokens
-        if n_tokens < self.max_size:
-            pad_len = self.max_size - n_tokens
-            cache._keys = tuple(_pad_tokens(t, 0, pad_len) for t in cache._keys)
-            cache._values = tuple(_pad_tokens(t, 0, pad_len) for t in cache._values)
         return cache
 
     @classmethod
     def merge(cls, caches):
         """Right-align rotating caches into one batch (cache.py:963-1010).
 
-        The reference allocates ``max_len`` slots here, which leaves no room
-        for the next decode write at ``_idx % max_size`` whenever
-        ``max_len < max_size``; this cache allocates ``max_size`` slots so the
-        ring stays a ring.  Visible views have the same shapes.
+        Each cache's window, in temporal order, lands in slots
+        [max_len - len_i, max_len) of its row.  The reference allocates
+        ``max_len`` slots, which leaves no room for the next decode write at
+        ``_idx % max_size`` whenever ``max_len < max_size``; this cache keeps a
+        full ring of ``max_size`` slots.  Visible views have the same shapes.
         """
         if not caches:
             return cls([0], max_size=4096)
         max_size = caches[0].max_size
-        bits = caches[0].bits
-        gs = caches[0].group_size
         lengths = [c.size() for c in caches]
         max_len = max(lengths)
-        padding = [max_len - l for l in lengths]
-        batch = cls(padding, max_size=max_size, bits=bits, group_size=gs)
-        if all(c.empty() for c in caches):
+        padding = [max_len - n for n in lengths]
+        batch = cls(padding, max_size=max_size, bits=caches[0].bits, group_size=caches[0].group_size)
+        filled = [c for c in caches if not c.empty()]
+        if not filled:
             return batch
-        B = len(caches)
-        ref = next(c for c in caches if not c.empty())
-        H = ref._keys[0].shape[1]
-        dev = ref._keys[0].device
-        k_state_ref, v_state_ref = ref.state
-        slots = max(max_size, max_len)
-        batch._keys = tuple(torch.zeros((B, H, slots, t.shape[3]), dtype=t.dtype, device=dev)
-                            for t in k_state_ref)
-        batch._values = tuple(torch.zeros((B, H, slots, t.shape[3]), dtype=t.dtype, device=dev)
-                              for t in v_state_ref)
-        for i, (p, c) in enumerate(zip(padding, caches)):
-            if c.empty():
+        ref = filled[0]
+        slots = max(_ring_slots(max_size), _round_up(max_len, _ALIGN))
+        nk, nv = _alloc_like(ref._keys, ref._values, len(caches), slots)
+        sources, rows = [], []
+        for p, c, n in zip(padding, caches, lengths):
+            if c.empty() or n == 0:
+                sources.append((ref._keys, ref._values, 0))
+                rows.append((0, 0, 0, 0))
                 continue
-            k_state, v_state = c.state
-            n = k_state[0].shape[2]
-            for j in range(3):
-                _i32(batch._keys[j])[i:i + 1, :, p:p + n] = _i32(k_state[j])
-                _i32(batch._values[j])[i:i + 1, :, p:p + n] = _i32(v_state[j])
+            # slot p + t takes the cache's t-th oldest token: ring slot (oldest + t) mod n
+            oldest = c._idx % c.max_size if c.offset > c.max_size else 0
+            sources.append((c._keys, c._values, 0))
+            rows.append((p - oldest, p, p + n, n if oldest else 0) if oldest else (p, p, p + n, 0))
+        _gather_into(nk, nv, sources, rows, slots)
+        batch._keys, batch._values = nk, nv
         batch.offset = batch.offset + max_len
         batch._idx = max_len
-        batch._pad = torch.as_tensor(padding, dtype=torch.int64)
+        batch._pad = _i64(padding)
         return batch

@@ -16,8 +16,10 @@ step have arrived -- two kernels, no NCCL call.  The all-gather path remains
 for process groups without peer access (gloo, tests).
 
 Appends go to the rank that owns the tail of the sequence
-(:class:`SequenceShardedCache`).  Batches shard by sequence instead and need no
-collective at all (each rank runs the unsharded decode on its own rows).
+(:class:`SequenceShardedCache`).  Batches shard by sequence instead
+(:func:`partition_sequences` balances the rows' KV bytes over the ranks) and
+need no collective on the data path: each rank runs the unsharded decode on its
+own rows.
 """
 
 from __future__ import annotations
@@ -32,7 +34,47 @@ import torch.distributed as dist
 from . import _lib
 from .cache import QuantizedSDPACache
 
-__all__ = ["sharded_quantized_sdpa", "merge_partials", "SequenceShardedCache", "PeerExchange"]
+__all__ = ["sharded_quantized_sdpa", "merge_partials", "SequenceShardedCache", "PeerExchange",
+           "partition_sequences", "gather_rows"]
+
+
+def partition_sequences(lengths, world: int):
+    """Batch sharding by sequence: split the rows of a continuous batch over
+    ``world`` ranks so each rank's decode reads about the same number of KV
+    bytes (the decode is bound by them).  Greedy longest-first onto the
+    least-loaded rank; ties go to the lower rank, so every rank computes the
+    same partition.  Returns one sorted list of row indices per rank.  The
+    ranks then decode their own rows independently -- no collective on the
+    data path; the outputs stay on their ranks (``gather_rows`` reassembles
+    them where one rank needs the whole batch).
+    """
+    if world < 1:
+        raise ValueError(f"world must be >= 1, got {world}")
+    lens = [int(n) for n in lengths]
+    load = [0] * world
+    parts = [[] for _ in range(world)]
+    for i in sorted(range(len(lens)), key=lambda i: (-lens[i], i)):
+        r = min(range(world), key=lambda r: (load[r], r))
+        parts[r].append(i)
+        load[r] += lens[i]
+    return [sorted(p) for p in parts]
+
+
+def gather_rows(local_out: torch.Tensor, parts, group=None) -> torch.Tensor:
+    """Reassemble a batch from the ranks' outputs: rank r holds the rows
+    ``parts[r]`` of the batch (in that order) along dim 0.  Every rank gets
+    the whole batch (collective over ``group``)."""
+    world = dist.get_world_size(group)
+    n_max = max(len(p) for p in parts)
+    pad = torch.zeros((n_max,) + tuple(local_out.shape[1:]), dtype=local_out.dtype, device=local_out.device)
+    pad[: local_out.shape[0]] = local_out
+    gath = _gather(pad, group)
+    B = sum(len(p) for p in parts)
+    out = torch.empty((B,) + tuple(local_out.shape[1:]), dtype=local_out.dtype, device=local_out.device)
+    for r in range(world):
+        for j, row in enumerate(parts[r]):
+            out[row] = gath[r, j]
+    return out
 
 
 class PeerExchange:

@@ -90,3 +90,23 @@ def assert_close(out: np.ndarray, ref: np.ndarray, atol=ATOL, rtol=RTOL, what=""
         raise AssertionError(f"{what}: {bad.sum()} elements outside tolerance; max abs err "
                              f"{err.max():.3e} at {i} (out {out[i]:.6f} ref {ref[i]:.6f})")
     return float(err.max())
+
+
+def cpu_gather(dst_k, dst_v, sources, rows, T):
+    """CPU statement of qsdpa_gather_rows (include/qsdpa.h): destination row b
+    takes, for tokens j in [lo, hi), source token (j - shift) mod mod (mod 0:
+    j - shift) of its own source row; every other token of [0, T) is zero."""
+    dst = list(dst_k) + list(dst_v)
+    import torch
+    as_i = lambda t: t.view(torch.int32) if t.dtype == torch.uint32 else t
+    for b, ((sk, sv, r), (shift, lo, hi, mod)) in enumerate(zip(sources, rows)):
+        src = list(sk) + list(sv)
+        for d, s in zip(dst, src):
+            d, s = as_i(d), as_i(s)
+            d[b, :, :T] = 0
+            for j in range(max(lo, 0), min(hi, T)):
+                sj = j - shift
+                if mod:
+                    sj %= mod
+                if sj >= 0:
+                    d[b, :, j] = s[r, :, sj]

@@ -123,7 +123,8 @@ def test_struct_layout_matches_c(tmp_path):
     lines = ['#include <stdio.h>', '#include <stddef.h>', '#include "qsdpa.h"', 'int main(void){']
     for cname, py in (("qsdpa_decode_params", _lib.DecodeParams),
                       ("qsdpa_quantize_params", _lib.QuantizeParams),
-                      ("qsdpa_dequantize_params", _lib.DequantizeParams)):
+                      ("qsdpa_dequantize_params", _lib.DequantizeParams),
+                      ("qsdpa_gather_params", _lib.GatherParams)):
         lines.append(f'printf("{cname} %zu\\n", sizeof({cname}));')
         for f, _ in py._fields_:
             lines.append(f'printf("{cname}.{f} %zu\\n", offsetof({cname}, {f}));')
@@ -135,7 +136,8 @@ def test_struct_layout_matches_c(tmp_path):
                                                          check=True).stdout.split("\n") if l)
     for cname, py in (("qsdpa_decode_params", _lib.DecodeParams),
                       ("qsdpa_quantize_params", _lib.QuantizeParams),
-                      ("qsdpa_dequantize_params", _lib.DequantizeParams)):
+                      ("qsdpa_dequantize_params", _lib.DequantizeParams),
+                      ("qsdpa_gather_params", _lib.GatherParams)):
         assert int(got[cname]) == ctypes.sizeof(py), cname
         for f, _ in py._fields_:
             assert int(got[f"{cname}.{f}"]) == getattr(py, f).offset, f"{cname}.{f}"

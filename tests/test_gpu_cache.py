@@ -56,7 +56,8 @@ def test_linear_cache_matches_model(qs, bits, gs):
         same_tuple(kq, mk, O.F16)
         same_tuple(vq, mv, O.F16)
         assert cache.offset == model.offset
-        assert cache._keys[0].shape[2] == model.cap
+        # slots: a multiple of 8 tokens (aligned rows) holding every token
+        assert cache._keys[0].shape[2] >= cache.offset and cache._keys[0].shape[2] % 8 == 0
     assert cache.offset == 145
     assert cache.nbytes == sum(t.numel() * t.element_size() for t in cache._keys + cache._values)
 
@@ -111,7 +112,7 @@ def test_merge_and_batch_mask_pinned(qs):
     ma.update_and_fetch(ka, va)
     mb.update_and_fetch(kb_, vb_)
     mm = O.BatchCacheModel.merge([ma, mb])
-    same_tuple(batch._keys, mm.K.tup(), O.F16)
+    same_tuple(tuple(t[:, :, :batch._idx] for t in batch._keys), mm.K.tup(slice(0, batch._idx)), O.F16)
     r = batch.kv_ranges()
     assert r.start.tolist() == [0, 2] and r.length.tolist() == [4, 2]
 
@@ -349,3 +350,50 @@ def test_batch_decode_with_ranges_matches_masked_oracle(qs):
     # the reference's own mask (bit-exact make_mask) through the fused path
     out2 = from_torch(qs.cache_sdpa(q, kq, vq, batch, mask=mref))
     assert_close(out2, O.sdpa(qn, kd, vd, mask=mref.cpu().numpy()))
+
+
+# ------------------------------------------------------ row gather ----
+
+@pytest.mark.parametrize("G", [1, 2, 8])
+def test_gather_rows_matches_cpu_statement(qs, G):
+    """qsdpa_gather_rows against its CPU statement (tests/qsdpa_testlib.py):
+    rows from different sources, shifts both ways, a ring modulus, windows that
+    leave zeros, and scale rows of 2, 4 and 16 bytes (every copy width)."""
+    from qsdpa_testlib import cpu_gather
+    g = torch.Generator(device="cuda")
+    g.manual_seed(G)
+    H, pd, T = 2, 16, 40
+
+    def planes(B, n):
+        k = (torch.randint(-2 ** 31, 2 ** 31 - 1, (B, H, n, pd), generator=g, device="cuda",
+                           dtype=torch.int32).view(torch.uint32),
+             torch.randn((B, H, n, G), generator=g, device="cuda").half(),
+             torch.randn((B, H, n, G), generator=g, device="cuda").half())
+        v = (torch.randint(-2 ** 31, 2 ** 31 - 1, (B, H, n, pd), generator=g, device="cuda",
+                           dtype=torch.int32).view(torch.uint32),
+             torch.randn((B, H, n, G), generator=g, device="cuda").half(),
+             torch.randn((B, H, n, G), generator=g, device="cuda").half())
+        return k, v
+
+    a, b = planes(3, 33), planes(2, 50)
+    sources = [(a[0], a[1], 2), (b[0], b[1], 0), (a[0], a[1], 0), (b[0], b[1], 1)]
+    rows = [(5, 5, 38, 0), (-7, 0, 30, 0), (11, 0, 33, 33), (0, 3, 3, 0)]
+    def sevens(t):  # destination plane of 4 rows, T + 3 tokens, every element 7 (tokens >= T stay so)
+        if t.dtype == torch.uint32:
+            return torch.full((4, H, T + 3, t.shape[3]), 7, dtype=torch.int32, device="cuda").view(torch.uint32)
+        return torch.full((4, H, T + 3, t.shape[3]), 7, dtype=t.dtype, device="cuda")
+
+    dk, dv = (tuple(sevens(t) for t in three) for three in a)
+    from mlx_qsdpa import cache as C
+    C._gather_into(dk, dv, sources, rows, T)
+    torch.cuda.synchronize()
+    ck = tuple(t.cpu() for t in dk)
+    cv = tuple(t.cpu() for t in dv)
+    cpu_src = [((tuple(t.cpu() for t in sk), tuple(t.cpu() for t in sv), r)) for sk, sv, r in sources]
+    ref_k = tuple(sevens(t).cpu() for t in a[0])
+    ref_v = tuple(sevens(t).cpu() for t in a[1])
+    cpu_gather(ref_k, ref_v, cpu_src, rows, T)
+    for got, want in zip(ck + cv, ref_k + ref_v):
+        gi = got.view(torch.int32) if got.dtype == torch.uint32 else got.view(torch.int16)
+        wi = want.view(torch.int32) if want.dtype == torch.uint32 else want.view(torch.int16)
+        assert torch.equal(gi, wi)

@@ -60,7 +60,7 @@ def _worker(rank, world, port, q_list):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("world", [2, 4])
+@pytest.mark.parametrize("world", [2, 4, 8])
 def test_peer_merge_matches_single_gpu(world):
     if not torch.cuda.is_available() or torch.cuda.device_count() < world:
         pytest.skip(f"needs {world} GPUs")
@@ -131,3 +131,76 @@ def test_decode_shard_single_rank_matches_decode(kernel, N, splits):
         assert (out.float() - ref.float()).abs().max().item() < 2e-3, f"step {step}"
     assert_close(from_torch(out), c.reference(), what=f"decode_shard {kernel}")
     assert _lib.device_status(reset=True) == 0
+
+
+def _batch_worker(rank, world, port, q_list):
+    """One rank of a batch sharded by sequence: configuration 4's 32 sequences
+    (lengths U[2048, 32768], seed 0), this rank's share merged into its own
+    BatchQuantizedSDPACache, one decode step, every row against the oracle."""
+    import datetime
+    import torch.distributed as dist
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dev = torch.device("cuda", rank % torch.cuda.device_count())
+    torch.cuda.set_device(dev)
+    # the host collective (gloo) reassembles the batch; the data path has none
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=120))
+    try:
+        import mlx_qsdpa
+        from mlx_qsdpa.sharded import gather_rows, partition_sequences
+        from qsdpa_testlib import normal, to_torch, u32_from_torch
+        B, Hq, Hkv, D, bits, gs = 32, 32, 8, 128, 4, 64
+        lengths = np.random.default_rng(0).integers(2048, 32769, size=B)
+        parts = partition_sequences(lengths, world)
+        mine = parts[rank]
+        qn = normal(np.random.default_rng(5), (B, Hq, 1, D), O.F16)
+        singles = []
+        for i in mine:
+            g = torch.Generator(device=dev)
+            g.manual_seed(1000 + i)  # sequence i's K/V, whichever rank holds it
+            c = mlx_qsdpa.QuantizedSDPACache(bits=bits, group_size=gs)
+            k = torch.randn((1, Hkv, int(lengths[i]), D), generator=g, device=dev).half()
+            v = torch.randn((1, Hkv, int(lengths[i]), D), generator=g, device=dev).half()
+            c.update_and_fetch(k, v)
+            singles.append(c)
+        batch = mlx_qsdpa.BatchQuantizedSDPACache.merge(singles)
+        kq, vq = batch.state[0], batch.state[1]
+        q = to_torch(qn[mine], O.F16, device=dev)
+        out = mlx_qsdpa.cache_sdpa(q, kq, vq, batch, mask=batch.kv_ranges())
+        local = from_torch(out)
+        errs = []
+        lp = batch.left_padding.tolist()
+        for j, i in enumerate(mine):
+            kd = O.dequantize(u32_from_torch(kq[0][j:j + 1]), from_torch(kq[1][j:j + 1]), from_torch(kq[2][j:j + 1]),
+                              gs, bits, O.F16)[:, :, lp[j]:]
+            vd = O.dequantize(u32_from_torch(vq[0][j:j + 1]), from_torch(vq[1][j:j + 1]), from_torch(vq[2][j:j + 1]),
+                              gs, bits, O.F16)[:, :, lp[j]:]
+            ref = O.sdpa(qn[i:i + 1], kd, vd)
+            err = np.abs(local[j:j + 1] - ref)
+            errs.append(bool(np.all((err <= 2e-3) | (err <= 1e-2 * np.abs(ref)))))
+        full = gather_rows(torch.from_numpy(local), parts)
+        q_list.put((rank, mine, errs, full.numpy()[mine].tolist() == local.tolist()))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_batch_sharding_two_ranks():
+    """Batch sharding by sequence over two ranks (one process each; on a
+    one-GPU box both run on it -- they never wait for each other on the GPU)."""
+    if not torch.cuda.is_available():
+        pytest.skip("needs a GPU")
+    import torch.multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    q_list = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_batch_worker, args=(r, 2, port, q_list)) for r in range(2)]
+    for p in procs:
+        p.start()
+    results = [q_list.get(timeout=600) for _ in procs]
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    assert sorted(i for _, mine, _, _ in results for i in mine) == list(range(32))
+    for rank, mine, errs, gathered_ok in results:
+        assert all(errs), f"rank {rank}: rows {[i for i, e in zip(mine, errs) if not e]} outside tolerance"
+        assert gathered_ok

@@ -11,6 +11,7 @@ import numpy as np
 import pytest
 
 import qsdpa_oracle as O
+from qsdpa_testlib import cpu_gather
 
 torch = pytest.importorskip("torch")
 
@@ -49,6 +50,7 @@ def _oracle_dequant(cache, bufs, n_visible, start=0, mod=0):
 def cpu_kernels(monkeypatch):
     monkeypatch.setattr(C, "_quantize", _oracle_quantize)
     monkeypatch.setattr(C, "_dequant", _oracle_dequant)
+    monkeypatch.setattr(C, "_gather_into", cpu_gather)
 
 
 def kv(rng, B, H, S, D):
@@ -144,7 +146,9 @@ def test_linear_cache_growth_and_state(cpu_kernels):
         k, v = kv(rng, 1, 2, S, 64)
         kq, _ = c.update_and_fetch(k, v)
         mk, _ = m.update_and_fetch(_np(k), _np(v))
-        assert kq[0].shape == mk[0].shape and c._keys[0].shape[2] == m.cap
+        assert kq[0].shape == mk[0].shape
+        slots = c._keys[0].shape[2]
+        assert slots >= c.offset and slots % 64 == 0  # whole steps, grown by at least a quarter
         assert np.array_equal(kq[0].view(torch.int32).numpy().view(np.uint32), mk[0])
     st, meta = c.state, c.meta_state
     assert meta == ("199", "4", "32")
@@ -190,11 +194,14 @@ def test_batch_cache_merge_filter_extend_extract(cpu_kernels):
     for i, n in enumerate((4, 7, 2)):
         e = b.extract(i)
         assert e.offset == n
-        assert torch.equal(e._keys[0].view(torch.int32), singles[i]._keys[0][:, :, :n].view(torch.int32))
+        assert torch.equal(e.state[0][0].view(torch.int32), singles[i]._keys[0][:, :, :n].view(torch.int32))
     b.update_and_fetch(*kv(rng, 3, 2, 1, 64))
     assert b.offset.tolist() == [5, 8, 3] and b._idx == 8
+    before = b._keys[0][:, :, :8].clone()
     b.filter([0, 2])
-    assert b.left_padding.tolist() == [0, 2] and b._idx == 5 and b._keys[0].shape[2] == 260
+    assert b.left_padding.tolist() == [0, 2] and b._idx == 5
+    # the slots every kept row pads (3) are dropped
+    assert torch.equal(b._keys[0][:, :, :5].view(torch.int32), before[[0, 2], :, 3:8].view(torch.int32))
     other = mlx_qsdpa.QuantizedSDPACache.merge([singles[1]])
     b.extend(other)
     assert b._keys[0].shape[0] == 3 and b._idx == 7 and b.left_padding.tolist() == [2, 4, 0]
@@ -209,11 +216,12 @@ def test_batch_prepare_finalize(cpu_kernels):
     assert b.left_padding.tolist() == [1, 0] and b.offset.tolist() == [-1, 0]
     k, v = kv(rng, 2, 2, 5, 64)
     b.update_and_fetch(k, v)
-    before = b._keys[0].clone()
+    before = b._keys[0][:, :, :5].clone()
     b.finalize()
     assert b.left_padding.tolist() == [1, 2] and b.offset.tolist() == [4, 3]
-    # row 1 rolled right by 2 along the token axis
-    assert torch.equal(b._keys[0][1].view(torch.int32).roll(-2, dims=1), before[1].view(torch.int32))
+    # row 1's written tokens rolled right by 2: its right padding is now in front
+    assert torch.equal(b._keys[0][1, :, :5].view(torch.int32).roll(-2, dims=1), before[1].view(torch.int32))
+    assert torch.equal(b._keys[0][0, :, :5].view(torch.int32), before[0].view(torch.int32))
     with pytest.raises(ValueError, match="Left padding can only be added"):
         b.prepare(left_padding=[1, 1])
 

@@ -137,3 +137,69 @@ def test_two_rank_sequence_sharding():
         assert own_ok, f"rank {rank} stored the wrong tokens"
         assert offset == 300
         assert max(errs) < 1e-5, (rank, errs)
+
+
+# ---- batch sharding by sequence (continuous batching, no data-path collective) ----
+
+def test_partition_sequences_balances_and_covers():
+    from mlx_qsdpa.sharded import partition_sequences
+    lengths = np.random.default_rng(0).integers(2048, 32769, size=32)
+    for world in (1, 2, 3, 4, 8):
+        parts = partition_sequences(lengths, world)
+        assert len(parts) == world
+        flat = sorted(i for p in parts for i in p)
+        assert flat == list(range(32))  # a disjoint cover of the batch
+        loads = [int(lengths[p].sum()) for p in parts]
+        # greedy longest-first: no rank exceeds the mean by more than one sequence
+        assert max(loads) - min(loads) <= int(lengths.max())
+        assert parts == partition_sequences(lengths.tolist(), world)  # deterministic
+    with pytest.raises(ValueError):
+        partition_sequences([1, 2], 0)
+
+
+def _batch_worker(rank, world, port, q_list):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        from mlx_qsdpa.sharded import gather_rows, partition_sequences
+        rng = np.random.default_rng(11)
+        B, Hq, Hkv, D, bits, gs = 6, 8, 2, 128, 4, 64
+        lengths = [40, 7, 25, 63, 12, 30]
+        q = O.round_to(rng.standard_normal((B, Hq, 1, D)).astype(np.float32), O.F16)
+        seqs = []
+        for n in lengths:
+            k = O.round_to(rng.standard_normal((1, Hkv, n, D)).astype(np.float32), O.F16)
+            v = O.round_to(rng.standard_normal((1, Hkv, n, D)).astype(np.float32), O.F16)
+            pk, ks, kb = O.quantize(k, gs, bits, O.F16)
+            pv, vs, vb = O.quantize(v, gs, bits, O.F16)
+            seqs.append((O.dequantize(pk, ks, kb, gs, bits, O.F16), O.dequantize(pv, vs, vb, gs, bits, O.F16)))
+        parts = partition_sequences(lengths, world)
+        mine = parts[rank]
+        # this rank attends only over its own sequences (the oracle stands in
+        # for the CUDA decode): no exchange of keys or records
+        local = np.concatenate([O.sdpa(q[i:i + 1], *seqs[i]) for i in mine], axis=0) if mine else \
+            np.zeros((0, Hq, 1, D))
+        full = gather_rows(torch.from_numpy(local.astype(np.float32)), parts)
+        ref = np.concatenate([O.sdpa(q[i:i + 1], *seqs[i]) for i in range(B)], axis=0)
+        q_list.put((rank, mine, float(np.abs(full.numpy() - ref).max())))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_two_rank_batch_sharding():
+    ctx = mp.get_context("spawn")
+    q_list = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_batch_worker, args=(r, 2, port, q_list)) for r in range(2)]
+    for p in procs:
+        p.start()
+    results = [q_list.get(timeout=240) for _ in procs]
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    owned = sorted(i for _, mine, _ in results for i in mine)
+    assert owned == list(range(6))
+    for rank, mine, err in results:
+        assert mine, f"rank {rank} got no sequences"
+        assert err < 1e-6, (rank, err)

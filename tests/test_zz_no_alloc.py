@@ -92,10 +92,11 @@ def test_noalloc_matches_decode_on_two_calls_in_a_row(lib):
 
 
 def test_noalloc_multi_query_cap(lib):
-    # 16 causal query positions per head: B * H_q * qL = 1,024 record rows,
-    # whose automatic plan needs more than the array; the capped call must
-    # still match qsdpa_decode, twice in a row
-    B, H, qL, D, N, bits, gs = 8, 8, 16, 128, 65536, 4, 32
+    # 16 query positions per head are 16 record rows per head; on the mma.sync
+    # kernel (two CTAs per SM) a single KV head at 75,776 keys is planned
+    # with 296 splits, whose records need more than the array: the capped call
+    # must still match qsdpa_decode, twice in a row
+    B, H, qL, D, N, bits, gs = 1, 1, 16, 256, 75776, 4, 32
     g = torch.Generator(device="cuda")
     g.manual_seed(7)
     pd, G = D * bits // 32, D // gs
@@ -112,11 +113,12 @@ def test_noalloc_multi_query_cap(lib):
     q = torch.randn((B, H, qL, D), generator=g, device="cuda").half()
     for _ in range(2):
         out = torch.full_like(q, float("nan"))
-        p = params(lib, q, pk, pv, ks, vs, kb, vb, out, bits, gs, qL=qL, mask_kind=lib.MASK_CAUSAL)
+        p = params(lib, q, pk, pv, ks, vs, kb, vb, out, bits, gs, qL=qL)
+        p.kernel = lib.KERNEL_MMA
         assert automatic_workspace(lib, p) > SCRATCH_BYTES
         call_noalloc(lib, p)
         ref = lib.decode(q, pk, pv, ks, vs, kb, vb, scale=D ** -0.5, bits=bits, group_size=gs,
-                         mask_kind=lib.MASK_CAUSAL)
+                         kernel=lib.KERNEL_MMA)
         torch.cuda.synchronize()
         assert_close(from_torch(out), from_torch(ref), what="noalloc qL=16 vs qsdpa_decode")
 
