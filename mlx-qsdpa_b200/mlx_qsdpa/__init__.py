@@ -14,6 +14,7 @@ from .cache import (
     QuantizedRotatingSDPACache,
     BatchQuantizedRotatingSDPACache,
 )
+from .serialize import load_prompt_cache, save_prompt_cache
 
 __version__ = "0.3.1+b200"
 
@@ -72,4 +73,6 @@ __all__ = [
     "BatchQuantizedRotatingSDPACache",
     "cache_sdpa",
     "KVRanges",
+    "save_prompt_cache",
+    "load_prompt_cache",
 ]

@@ -397,3 +397,61 @@ def test_gather_rows_matches_cpu_statement(qs, G):
         gi = got.view(torch.int32) if got.dtype == torch.uint32 else got.view(torch.int16)
         wi = want.view(torch.int32) if want.dtype == torch.uint32 else want.view(torch.int16)
         assert torch.equal(gi, wi)
+
+
+# ------------------------------------------------- prompt-cache files ----
+
+def test_prompt_cache_file_decodes_bit_identically(qs, tmp_path):
+    """A cache written with save_prompt_cache and read back with
+    load_prompt_cache decodes to the very same bits, and keeps appending in
+    step with the original (every class, including a wrapped ring)."""
+    f = Feed(77)
+    lin = qs.QuantizedSDPACache(bits=4, group_size=32)
+    _, _, kt, vt = f.kv(1, 2, 3000, 256)
+    lin.update_and_fetch(kt, vt)
+    singles = []
+    for n in (700, 1300):
+        c = qs.QuantizedSDPACache(bits=4, group_size=64)
+        _, _, kt, vt = f.kv(1, 2, n, 128)
+        c.update_and_fetch(kt, vt)
+        singles.append(c)
+    batch = qs.BatchQuantizedSDPACache.merge(singles)
+    rot = qs.QuantizedRotatingSDPACache(max_size=512, bits=8, group_size=64)
+    _, _, kt, vt = f.kv(1, 2, 500, 128)
+    rot.update_and_fetch(kt, vt)
+    for _ in range(40):  # wraps
+        _, _, kt, vt = f.kv(1, 2, 1, 128)
+        rot.update_and_fetch(kt, vt)
+    brot = qs.BatchQuantizedRotatingSDPACache.merge([rot, qs.QuantizedRotatingSDPACache(max_size=512, bits=8,
+                                                                                       group_size=64)])
+    caches = [lin, batch, rot, brot]
+    path = str(tmp_path / "prompt.safetensors")
+    qs.save_prompt_cache(path, caches, metadata={"tokens": "3000"})
+    back = qs.load_prompt_cache(path)
+
+    def decode(c, q):
+        if isinstance(c, qs.QuantizedSDPACache):
+            kq, vq = c.state
+            mask = None
+        elif isinstance(c, qs.BatchQuantizedSDPACache):
+            kq, vq = c.state[0], c.state[1]
+            mask = c.kv_ranges()
+        elif isinstance(c, qs.QuantizedRotatingSDPACache):
+            n = min(c.offset, c.max_size)
+            kq, vq = tuple(t[:, :, :n] for t in c._keys), tuple(t[:, :, :n] for t in c._values)
+            mask = None
+        else:
+            n = min(c._idx, c.max_size)
+            kq, vq = tuple(t[:, :, :n] for t in c._keys), tuple(t[:, :, :n] for t in c._values)
+            mask = c.kv_ranges()
+        return qs.cache_sdpa(q, kq, vq, c, mask=mask)
+
+    for a, b in zip(caches, back):
+        D = 256 if a is lin else 128
+        rows = a._keys[0].shape[0]
+        q = to_torch(normal(f.rng, (rows, 8, 1, D), O.F16), O.F16)
+        assert torch.equal(decode(a, q).view(torch.int16), decode(b, q).view(torch.int16))
+        _, _, kt, vt = f.kv(rows, 2, 1, D)
+        ka, _ = a.update_and_fetch(kt, vt)
+        kb_, _ = b.update_and_fetch(kt, vt)
+        assert torch.equal(ka[0].view(torch.int32), kb_[0].view(torch.int32))

@@ -321,3 +321,20 @@ def test_tensor_core_and_cuda_core_paths_agree(qs, dtype, bits, gs):
     ref = c.reference()
     assert_close(fast, ref, what="tensor-core path")
     assert_close(slow, ref, what="cuda-core path")
+
+
+def test_three_way_comparator(qs):
+    """The comparator's three paths (fp16 SDPA on dequantised K/V, the unfused
+    dequantise + matmul path, the fused kernel) agree with the oracle, and a
+    short measurement reports all three."""
+    from mlx_qsdpa import bench_comparison as bc
+    c = Case(1, 32, 2, 2048, 256, seed=71)
+    q, pk, pv, ks, vs, kb, vb = c.torch_args()
+    ref = c.reference()
+    two_call = from_torch(bc.dequant_mm_sdpa(q, (pk, ks, kb), (pv, vs, vb), 256 ** -0.5, 4, 32))
+    assert_close(two_call, ref, what="dequant_mm path")
+    fused = from_torch(qs.quantized_sdpa(q, pk, pv, ks, vs, kb, vb))
+    assert_close(fused, ref, what="fused path")
+    rows = bc.run_measurement(1, 32, 2, 4096, 256, 1, 4, 32, num_iters=5, warmup=2)
+    assert [r["path"] for r in rows] == ["fp16", "dequant_mm", "fused"]
+    assert all(r["p5_us"] <= r["median_us"] <= r["p95_us"] and r["achieved_gbps"] > 0 for r in rows)

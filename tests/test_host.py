@@ -263,3 +263,59 @@ def test_benchmarks_module_imports():
     assert set(bm.KERNELS) == {"auto", "tcgen05", "mma", "simt"}
     # config 2 bytes per call at 128K: q + out + 320 B per key per KV head
     assert bm.algorithmic_bytes(1, 32, 2, 131072, 256, 4, 32, True) == 2 * 32 * 256 * 2 + 2 * 2 * 131072 * 160
+
+
+def test_prompt_cache_file_roundtrip(cpu_kernels, tmp_path):
+    """save_prompt_cache / load_prompt_cache: every cache class, slots in their
+    physical order and the bookkeeping come back unchanged (CPU tensors)."""
+    rng = np.random.default_rng(9)
+    lin = mlx_qsdpa.QuantizedSDPACache(bits=4, group_size=32)
+    lin.update_and_fetch(*kv(rng, 1, 2, 37, 64))
+    singles = []
+    for n in (5, 9):
+        c = mlx_qsdpa.QuantizedSDPACache(bits=8, group_size=64)
+        c.update_and_fetch(*kv(rng, 1, 2, n, 64))
+        singles.append(c)
+    batch = mlx_qsdpa.BatchQuantizedSDPACache.merge(singles)
+    rot = mlx_qsdpa.QuantizedRotatingSDPACache(max_size=8)
+    for S in (6, 1, 1, 1, 1, 1):  # wrapped: _idx in the middle of the ring
+        rot.update_and_fetch(*kv(rng, 1, 2, S, 64))
+    brot = mlx_qsdpa.BatchQuantizedRotatingSDPACache([0, 2], max_size=8)
+    for _ in range(11):
+        brot.update_and_fetch(*kv(rng, 2, 2, 1, 64))
+    empty = mlx_qsdpa.QuantizedSDPACache()
+    caches = [lin, batch, rot, brot, empty]
+    path = str(tmp_path / "prompt.safetensors")
+    mlx_qsdpa.save_prompt_cache(path, caches, metadata={"model": "test"})
+    back, meta = mlx_qsdpa.load_prompt_cache(path, device="cpu", return_metadata=True)
+    assert meta == {"model": "test"}
+    assert [type(c) for c in back] == [type(c) for c in caches]
+    for a, b in zip(caches, back):
+        assert (a.bits, a.group_size, a.empty()) == (b.bits, b.group_size, b.empty())
+        if a.empty():
+            continue
+        n = b_visible(b)
+        assert n == b_visible(a)
+        for ta, tb in zip(a._keys + a._values, b._keys + b._values):
+            ia = ta.view(torch.int32) if ta.dtype == torch.uint32 else ta.view(torch.int16)
+            ib = tb.view(torch.int32) if tb.dtype == torch.uint32 else tb.view(torch.int16)
+            assert tb.shape[2] >= n and torch.equal(ia[:, :, :n], ib[:, :, :n])
+    assert back[0].offset == 37 and back[1]._idx == batch._idx
+    assert back[1].offset.tolist() == batch.offset.tolist() and back[1].left_padding.tolist() == [4, 0]
+    assert (back[2].offset, back[2]._idx) == (rot.offset, rot._idx)
+    assert back[3]._idx == 11 and back[3]._pad.tolist() == brot._pad.tolist()
+    with pytest.raises(ValueError):
+        bad = str(tmp_path / "bad.safetensors")
+        from safetensors.torch import save_file
+        save_file({"x": torch.zeros(1)}, bad, metadata={"format": "other"})
+        mlx_qsdpa.load_prompt_cache(bad, device="cpu")
+
+
+def b_visible(c):
+    if isinstance(c, mlx_qsdpa.QuantizedSDPACache):
+        return c.offset
+    if isinstance(c, mlx_qsdpa.BatchQuantizedSDPACache):
+        return c._idx
+    if isinstance(c, mlx_qsdpa.QuantizedRotatingSDPACache):
+        return min(c.offset, c.max_size)
+    return min(c._idx, c.max_size)

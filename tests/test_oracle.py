@@ -223,3 +223,14 @@ def test_c_oracle_matches_python():
         got = O.from_bits(out, dt)[:, :, None, :]
         err = np.abs(got - ref)
         assert np.all((err <= 2e-3) | (err <= 1e-2 * np.abs(ref)))
+
+
+def test_comparator_bytes_match_reference_pins(pins):
+    """mlx_qsdpa.bench_comparison.compute_bytes / compute_bandwidth_gbps give
+    the reference test's exact counts (tests/test_bench_comparison.py:112-160)."""
+    from mlx_qsdpa import bench_comparison as bc
+    for key in ("fp16", "quantized"):
+        p = pins["compute_bytes"][key]
+        assert bc.compute_bytes(*p["args"]) == (p["read"], p["written"])
+    b = pins["bandwidth"]
+    assert abs(bc.compute_bandwidth_gbps(b["bytes"], b["median_us"]) - b["gbps"]) < 1e-9
