@@ -39,6 +39,27 @@ namespace {
 // bit 1: a merge waited in vain for another rank (read by qsdpa_device_status)
 __device__ unsigned int g_shard_status = 0;
 
+// Optional per-CTA timeline of the fused step (builds with -DQSDPA_SHARD_TRACE
+// only): %globaltimer after the dependency wait (the decode is done), after
+// this rank's slice is stored to the peers, once every rank's words of the
+// slice have arrived, and at the end of the CTA's first slice.
+#ifdef QSDPA_SHARD_TRACE
+constexpr int kTraceSlots = 1024;
+__device__ unsigned long long g_shard_trace[4][kTraceSlots];
+#define SHARD_TRACE(ev, first)                                                         \
+    do {                                                                               \
+        if ((first) && threadIdx.x == 0 && blockIdx.x < kTraceSlots) {                 \
+            unsigned long long t_;                                                     \
+            asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t_));                    \
+            g_shard_trace[(ev)][blockIdx.x] = t_;                                      \
+        }                                                                              \
+    } while (0)
+#else
+#define SHARD_TRACE(ev, first) \
+    do {                       \
+    } while (0)
+#endif
+
 constexpr int kMaxWorld = 8;
 constexpr int kDims = 64;          // dims per slice and threads per CTA
 constexpr int kWords = kDims + 4;  // words per slice: o, m, l, padding
@@ -191,6 +212,7 @@ __global__ void __launch_bounds__(merge::kThreads)
 #endif
     static_assert(merge::kSlice == kDims, "a merge slice is an exchange slice");
     __shared__ merge::Smem sm;
+    SHARD_TRACE(0, true);
     const unsigned int e = state[0] + 1u;
     const int tid = threadIdx.x;
     const int ncta = rows * ((D + kDims - 1) / kDims);
@@ -208,18 +230,28 @@ __global__ void __launch_bounds__(merge::kThreads)
                 if (tid < 2) st_word(dst + kDims + tid, tid == 0 ? m_loc : l_loc, e);
             }
         }
+        SHARD_TRACE(1, c == (int)blockIdx.x);
         float ot = 0.f, lt = 0.f;
         const bool ok = tid < kDims ? merge_ranks(own, slab, c, world, e, tid, ot, lt) : true;
+        SHARD_TRACE(2, c == (int)blockIdx.x);
         if (__syncthreads_or(!ok)) {
             if (tid == 0) atomicOr(&g_shard_status, 2u);
             break;
         }
         if (tid < kDims && d < D) out[(int64_t)row * D + d] = Dt<T>::from_f(lt > 0.f ? ot / lt : 0.f);
+        SHARD_TRACE(3, c == (int)blockIdx.x);
     }
     finish_step(state, e);
 }
 
 }  // namespace
+
+#ifdef QSDPA_SHARD_TRACE
+extern "C" int qsdpa_shard_trace(unsigned long long* host, int* slots) {
+    *slots = kTraceSlots;
+    return cudaMemcpyFromSymbol(host, g_shard_trace, sizeof(g_shard_trace)) == cudaSuccess ? 0 : -1;
+}
+#endif
 
 int read_shard_status(int reset) {
     unsigned int v = 0;
