@@ -24,7 +24,7 @@ import qsdpa_oracle as O  # noqa: E402
 
 PINS = {
     "batch_mask_offsets_4_2": {
-        "source": "tests/test_cache.py:291-333 and tests/test_batch_rotating_cache.py:406-450",
+        "source": "tests/test_cache.py:291-333 and tests/test_batch_rotating_cache.py:73-117",
         "lengths": [4, 2],
         "N": 2,
         "shape": [2, 1, 2, 6],
