@@ -87,20 +87,26 @@ def algorithmic_bytes(ctx_tokens: int) -> int:
     return 2 * B * HQ * D * 2 + ctx_tokens * B * HKV * 2 * row
 
 
-def lib_md5(path: str) -> str:
-    h = hashlib.md5()
-    with open(path, "rb") as f:
-        for chunk in iter(lambda: f.read(1 << 20), b""):
-            h.update(chunk)
-    return h.hexdigest()
+# sources the decode kernel is compiled from: its DRAM traffic changes only
+# when one of them does
+KERNEL_SOURCES = ("qsdpa_decode_tc.cu", "qsdpa_regmath.cuh", "qsdpa_internal.cuh", "qsdpa_merge.cuh")
 
 
-def recorded_traffic(lib_path: str, keys: int):
+def kernel_digest() -> str:
+    """sha256 (first 16 hex digits) of the decode kernel's source files."""
+    h = hashlib.sha256()
+    for f in KERNEL_SOURCES:
+        with open(os.path.join(ROOT, "mlx-qsdpa_b200", "csrc", f), "rb") as fh:
+            h.update(f.encode() + b"\0" + fh.read())
+    return h.hexdigest()[:16]
+
+
+def recorded_traffic(keys: int):
     """DRAM bytes (read + write) of one decode launch over `keys` keys, from the
-    ncu capture recorded for exactly this build of libqsdpa.so (matched by the
-    library's md5; captured on a smaller context and scaled by the keys per
-    launch, as the kernel's traffic grows in proportion).  None when this
-    build has no capture."""
+    ncu capture recorded for exactly these kernel sources (matched by their
+    digest; captured on a smaller context and scaled by the keys per launch, as
+    the kernel's traffic grows in proportion).  None when the sources changed
+    since the capture."""
     path = os.path.join(ROOT, TRAFFIC_RECORD)
     if not os.path.isfile(path):
         return None, "no capture recorded"
@@ -109,8 +115,8 @@ def recorded_traffic(lib_path: str, keys: int):
         if ":" in line and not line.startswith("#"):
             k, v = line.split(":", 1)
             rec[k.strip()] = v.strip()
-    if rec.get("lib_md5") != lib_md5(lib_path):
-        return None, "no ncu capture of this build"
+    if rec.get("kernel_sources_sha256") != kernel_digest():
+        return None, "no ncu capture of these kernel sources"
     per_key = float(rec["traffic_bytes_per_launch"]) / float(rec["keys_per_launch"])
     return round(per_key * keys), f"{TRAFFIC_RECORD} (scaled from {rec['keys_per_launch']} keys)"
 
@@ -585,7 +591,7 @@ def main():
         bytes_call = algorithmic_bytes(ctx)
         achieved = bytes_call / (per_launch_ms * 1e-3) / 1e9
         splits = _lib.plan_splits(qs[0], pk, pv, ks, vs, kb, vb, BITS, GS, kernel=kern_code)
-        traffic, traffic_src = recorded_traffic(_lib.LIB_PATH, ctx)
+        traffic, traffic_src = recorded_traffic(ctx)
         # per layer call: the decode kernel and the split merge (N>1: the fused
         # split merge + exchange + rank merge kernel; over NCCL: the record merge)
         launches_per_call = (1 if splits == 1 else 2) + (1 if (world > 1 and exchange is None) else 0)

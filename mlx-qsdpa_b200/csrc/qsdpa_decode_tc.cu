@@ -142,6 +142,10 @@ constexpr bool kTcPdl = QSDPA_TC_PDL != 0;
 #ifndef QSDPA_TC_VHALF
 #define QSDPA_TC_VHALF 0
 #endif
+// most V^T operand buffers (1 leaves room for a third ring stage at D=256)
+#ifndef QSDPA_TC_VBMAX
+#define QSDPA_TC_VBMAX 2
+#endif
 
 template <int BITS, int D, int GS, bool SPLITP>
 struct TcCfg {
@@ -173,7 +177,7 @@ struct TcCfg {
     // two P^T buffers (softmax of tile j overlaps the P V MMA of tile j-1) and
     // two V^T buffers (values run a tile ahead) where they fit
     static constexpr int PBUFS = fits(2, VHALF ? 2 : 1) ? 2 : 1;
-    static constexpr int VBUFS = VHALF ? 2 : (fits(PBUFS, 2) ? 2 : 1);
+    static constexpr int VBUFS = VHALF ? 2 : ((QSDPA_TC_VBMAX >= 2 && fits(PBUFS, 2)) ? 2 : 1);
     static constexpr int FIXED = BASE + PBUFS * P_BUF;
     static constexpr int STAGES_FIT = (kSmemLimit - FIXED - VBUFS * V_BYTES) / STAGE_BYTES;
     static constexpr int STAGES = STAGES_FIT > 4 ? 4 : STAGES_FIT;
