@@ -179,6 +179,42 @@ def quantize(w, group_size: int, bits: int, dtype: str):
     return packed, round_to(scale, dtype), round_to(bias, dtype)
 
 
+def quantize_ties(w, group_size: int, bits: int, mask: bool = False):
+    """Count the codes of ``quantize(w, ...)`` that sit exactly on a rounding tie.
+
+    A code is a tie when ``(w - bias) / scale`` (float32, the quantizer's own
+    arithmetic, lines above) is exactly halfway between two integers inside
+    the code range: only those codes depend on the rounding rule (``rint``
+    rounds half to even; a half-away-from-zero rule would differ there), so the
+    count bounds the code mismatches a different tie rule in ``mx.quantize``
+    could cause.  Returns ``(ties, total codes)``, or with ``mask`` the
+    boolean array (shape of ``w``) marking the ties.
+    """
+    w = np.asarray(w, dtype=np.float32)
+    *lead, D = w.shape
+    G = D // group_size
+    wg = w.reshape(*lead, G, group_size)
+    n_bins = np.float32((1 << bits) - 1)
+    eps = np.float32(1e-7)
+    w_max = wg.max(axis=-1)
+    w_min = wg.min(axis=-1)
+    side = np.abs(w_min) > np.abs(w_max)
+    scale = np.maximum((w_max - w_min) / n_bins, eps).astype(np.float32)
+    scale = np.where(side, scale, -scale).astype(np.float32)
+    edge = np.where(side, w_min, w_max).astype(np.float32)
+    q0 = np.rint(edge / scale).astype(np.float32)
+    nz = q0 != 0
+    safe_q0 = np.where(nz, q0, np.float32(1)).astype(np.float32)
+    scale = np.where(nz, edge / safe_q0, scale).astype(np.float32)
+    bias = np.where(nz, edge, np.float32(0)).astype(np.float32)
+    x = ((wg - bias[..., None]) / scale[..., None]).astype(np.float32)
+    frac = x - np.floor(x)
+    tie = (frac == np.float32(0.5)) & (x > 0) & (x < n_bins)
+    if mask:
+        return tie.reshape(w.shape)
+    return int(tie.sum()), int(x.size)
+
+
 def dequantize(packed, scales, biases, group_size: int, bits: int, dtype: str):
     """``w = RN_dtype(scale*code + bias)``; ``biases=None`` means zero biases."""
     codes = unpack(packed, bits).astype(np.float64)

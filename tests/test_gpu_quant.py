@@ -59,6 +59,24 @@ def test_quantize_bit_exact(lib, dtype, bits, gs):
     assert not u32_from_torch(pk)[:, :, :3].any() and not u32_from_torch(pk)[:, :, 3 + S:].any()
 
 
+@pytest.mark.parametrize("bits,gs", [(4, 32), (8, 64)])
+def test_quantize_ties_match_oracle(lib, bits, gs):
+    """The codes on exact rounding ties (config 2's value distribution) equal
+    the oracle's half-to-even choice; the whole tensor is bit-exact too."""
+    rng = np.random.default_rng(7)
+    B, H, S, D = 1, 2, 8192, 256
+    x = rng.standard_normal((B, H, S, D)).astype(np.float16)
+    ties, _ = O.quantize_ties(x, gs, bits)
+    assert ties > 0
+    pk, sc, bi = alloc(B, H, S, D, bits, gs, O.F16)
+    lib.quantize_into(to_torch(x, O.F16), pk, sc, bi, 0, bits, gs)
+    torch.cuda.synchronize()
+    rp, rs, rb = O.quantize(x, gs, bits, O.F16)
+    assert np.array_equal(u32_from_torch(pk), rp)
+    assert np.array_equal(bits_of(sc), O.to_bits(rs, O.F16))
+    assert np.array_equal(bits_of(bi), O.to_bits(rb, O.F16))
+
+
 def test_quantize_ring_wraps(lib):
     rng = np.random.default_rng(5)
     B, H, S, D, cap = 1, 2, 6, 128, 8

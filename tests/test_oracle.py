@@ -109,6 +109,25 @@ def test_quantize_properties(bits, dtype):
     assert np.abs(d[..., ::7]).max() <= 2 * ulp * (np.abs(b).max() + np.abs(s).max() * ((1 << bits) - 1))
 
 
+@pytest.mark.parametrize("bits,gs", [(4, 32), (8, 64), (4, 128)])
+def test_quantize_ties_counted(bits, gs):
+    """Codes on an exact rounding tie are counted, and rounded half to even.
+
+    MLX cannot be installed here, so codes are never compared with a real
+    mx.quantize; the ties are the only codes a different tie rule would change,
+    so their count (config 2's K/V distribution: fp16 N(0,1), 8192 tokens x 2
+    heads x D=256) bounds the possible mismatches."""
+    rng = np.random.default_rng(0)
+    x = rng.standard_normal((2, 8192, 256)).astype(np.float16)
+    ties, total = O.quantize_ties(x, gs, bits)
+    print(f"\nquantizer ties bits={bits} gs={gs}: {ties} of {total} codes ({100.0 * ties / total:.3f} %)")
+    assert total == x.size and 0 < ties < total // 1000
+    # every tie takes the even code (round half to even)
+    tie = O.quantize_ties(x, gs, bits, mask=True)
+    codes = O.unpack(O.quantize(x, gs, bits, O.F16)[0], bits)
+    assert tie.sum() == ties and np.all(codes[tie] % 2 == 0)
+
+
 def test_quantize_degenerate_groups():
     x = np.zeros((1, 64), np.float32)
     x[0, 32:] = 0.75
