@@ -104,8 +104,8 @@ def kernel_digest() -> str:
 def recorded_traffic(keys: int):
     """DRAM bytes (read + write) of one decode launch over `keys` keys, from the
     ncu capture recorded for exactly these kernel sources (matched by their
-    digest; captured on a smaller context and scaled by the keys per launch, as
-    the kernel's traffic grows in proportion).  None when the sources changed
+    digest; captured on a smaller context: its reads scaled by the keys per
+    launch, its split-record writes kept).  None when the sources changed
     since the capture."""
     path = os.path.join(ROOT, TRAFFIC_RECORD)
     if not os.path.isfile(path):
@@ -117,8 +117,11 @@ def recorded_traffic(keys: int):
             rec[k.strip()] = v.strip()
     if rec.get("kernel_sources_sha256") != kernel_digest():
         return None, "no ncu capture of these kernel sources"
-    per_key = float(rec["traffic_bytes_per_launch"]) / float(rec["keys_per_launch"])
-    return round(per_key * keys), f"{TRAFFIC_RECORD} (scaled from {rec['keys_per_launch']} keys)"
+    # reads grow with the keys; the writes (split records) with the split
+    # count, which is the same one-wave plan at every context this bench runs
+    per_key = float(rec["read_bytes_per_launch"]) / float(rec["keys_per_launch"])
+    return (round(per_key * keys + float(rec["write_bytes_per_launch"])),
+            f"{TRAFFIC_RECORD} (reads scaled from {rec['keys_per_launch']} keys, split-record writes as captured)")
 
 
 # ------------------------------------------------------------ CPU side ----

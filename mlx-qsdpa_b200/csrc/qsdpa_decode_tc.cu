@@ -142,10 +142,6 @@ constexpr bool kTcPdl = QSDPA_TC_PDL != 0;
 #ifndef QSDPA_TC_VHALF
 #define QSDPA_TC_VHALF 0
 #endif
-// most V^T operand buffers (1 leaves room for a third ring stage at D=256)
-#ifndef QSDPA_TC_VBMAX
-#define QSDPA_TC_VBMAX 2
-#endif
 
 template <int BITS, int D, int GS, bool SPLITP>
 struct TcCfg {
@@ -177,7 +173,7 @@ struct TcCfg {
     // two P^T buffers (softmax of tile j overlaps the P V MMA of tile j-1) and
     // two V^T buffers (values run a tile ahead) where they fit
     static constexpr int PBUFS = fits(2, VHALF ? 2 : 1) ? 2 : 1;
-    static constexpr int VBUFS = VHALF ? 2 : ((QSDPA_TC_VBMAX >= 2 && fits(PBUFS, 2)) ? 2 : 1);
+    static constexpr int VBUFS = VHALF ? 2 : (fits(PBUFS, 2) ? 2 : 1);
     static constexpr int FIXED = BASE + PBUFS * P_BUF;
     static constexpr int STAGES_FIT = (kSmemLimit - FIXED - VBUFS * V_BYTES) / STAGE_BYTES;
     static constexpr int STAGES = STAGES_FIT > 4 ? 4 : STAGES_FIT;
@@ -528,6 +524,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(misc + 184);
     int* flags = reinterpret_cast<int*>(misc + 192);    // [4]
     float* red = reinterpret_cast<float*>(misc + 256);  // [4][16]
+    float* mfin = reinterpret_cast<float*>(misc + 512);  // [16] final running maxima
     const uint32_t sV_u = smem_u32(sV), sQ_u = smem_u32(sQ), sP_u = smem_u32(sP);
 
     const int split = blockIdx.x;
@@ -675,9 +672,6 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     bool dead = false;
     TC_TRACE_CTA(1);
 
-    float m_run[kTcHeads], l_run[kTcHeads];
-#pragma unroll
-    for (int h = 0; h < kTcHeads; ++h) m_run[h] = kNoMax, l_run[h] = 0.f;
     int n_active = 0;
 
     if (warp == kProdWarp) {
@@ -785,27 +779,52 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         // ================= key warps: K -> TMEM =================
         const uint32_t lane_off = (uint32_t)(warp * 32) << 16;
         const RowChunks<C::CPR> rows(t);
-        // dequantise the j-th active tile into K buffer j & 1 of TMEM lane t
+        constexpr int CPS = 32 / PPC;              // chunks per 32-column store
+        constexpr int NST = C::CPR / CPS;          // stores per row
+        constexpr int NG = (CPS * EPC + GS - 1) / GS;  // groups per store: 1 or 2
+        // the groups of store k: one or two halves, loaded as one word (a half
+        // per chunk would make 4-way bank conflicts on the 16-byte scale rows
+        // twice as often); half g_first in the low 16 bits
+        auto scale_word = [&](const char* s_sc, int k, uint32_t& sw, uint32_t& bw) {
+            const int g_first = (k * CPS * EPC) / GS;
+            bw = 0u;
+            if constexpr (NG == 2) {
+                sw = lds32(s_sc + g_first * 2);
+                if (has_bias) bw = lds32(s_sc + C::SC_BYTES + g_first * 2);
+            } else {
+                sw = lds16(s_sc + g_first * 2);
+                if (has_bias) bw = lds16(s_sc + C::SC_BYTES + g_first * 2);
+            }
+        };
+        // dequantise the chunks of store k into 32 TMEM columns of lane t
+        auto store_keys = [&](uint32_t kcol, int k, const uint4* w, uint32_t sw, uint32_t bw) {
+            uint32_t cols[32];
+#pragma unroll
+            for (int u = 0; u < CPS; ++u) {
+                const int gi = (u * EPC) / GS;  // 0 or 1 within this store
+                const uint32_t s2 = __byte_perm(sw, 0u, gi ? 0x3232 : 0x1010);
+                const uint32_t b2 = __byte_perm(bw, 0u, gi ? 0x3232 : 0x1010);
+                dequant_chunk<T, BITS>(w[u], s2, b2, &cols[u * PPC]);
+            }
+            tmem_st32(kcol + k * CPS * PPC, cols);
+        };
+        // the j-th active tile into K buffer j & 1 of TMEM lane t
         auto load_keys = [&](int j) {
             const int s = j % ST;
             mbar_wait(full_bar(s), (j / ST) & 1, dead);
             if (warp == 0) TC_TRACE(kEvKeyGo, j);
             const char* st = ring + s * C::STAGE_BYTES;
             const char* s_sc = st + 2 * C::PACK_BYTES + t * C::SROWB;
-            constexpr int CPS = 32 / PPC;  // chunks per 32-column store
             const uint32_t kcol = tbase + lane_off + kTmemK + (j & 1) * (D / 2);
+            if (j >= 2) mbar_wait(sready_bar(j & 1), ((j - 2) >> 1) & 1, dead);
 #pragma unroll 1
-            for (int c0 = 0; c0 < C::CPR; c0 += CPS) {
-                uint32_t cols[32];
+            for (int k = 0; k < NST; ++k) {
+                uint4 w[CPS];
 #pragma unroll
-                for (int u = 0; u < CPS; ++u) {
-                    const int c = c0 + u;
-                    const int g = (c * EPC) / GS;
-                    const uint32_t s2 = pair_at(s_sc + g * 2);
-                    const uint32_t b2 = has_bias ? pair_at(s_sc + C::SC_BYTES + g * 2) : 0u;
-                    dequant_chunk<T, BITS>(lds128(st + rows.off(c)), s2, b2, &cols[u * PPC]);
-                }
-                tmem_st32(kcol + c0 * PPC, cols);
+                for (int u = 0; u < CPS; ++u) w[u] = lds128(st + rows.off(k * CPS + u));
+                uint32_t sw, bw;
+                scale_word(s_sc, k, sw, bw);
+                store_keys(kcol, k, w, sw, bw);
             }
             __syncwarp();
             if (lane == 0) mbar_arrive(empty_bar(s));
@@ -818,13 +837,16 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 
         int n = 0;
         for (int i = advance(0); i < ntiles; i = advance(i + 1)) ++n;
-        for (int j = 0; j < n; ++j) {
-            // K buffer j & 1 was last read by the S MMA of tile j - 2
-            if (j >= 2) mbar_wait(sready_bar(j & 1), ((j - 2) >> 1) & 1, dead);
-            load_keys(j);
-        }
+        // K buffer j & 1 was last read by the S MMA of tile j - 2 (load_keys
+        // waits for it before writing)
+        for (int j = 0; j < n; ++j) load_keys(j);
     } else if (warp >= kSmWarp0) {
         // ================= softmax warps: S^T -> P^T =================
+        // running maximum and sum per head (the same in every softmax thread
+        // for m; per token lane for l), left in shared memory at the end
+        float m_run[kTcHeads], l_run[kTcHeads];
+#pragma unroll
+        for (int h = 0; h < kTcHeads; ++h) m_run[h] = kNoMax, l_run[h] = 0.f;
         {
             // the Q operand: rows h0.. of this KV head, K-major with the
             // 128-byte swizzle: 64-dim block kb at kb*2048, heads 8g.. at
@@ -1004,6 +1026,19 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             mbar_wait(pfree_bar((n_active - 1) % PB), ((n_active - 1) / PB) & 1, dead);
             tc_fence_after();
         }
+        // per-warp sums of l (red is no longer read by the tile loop: every
+        // softmax warp passed the last tile's barriers) and the final maxima
+#pragma unroll
+        for (int h = 0; h < kTcHeads; ++h) {
+            float v = l_run[h];
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+            if (lane == 0) red[qw * kTcHeads + h] = v;
+        }
+        if (warp == kSmWarp0 && lane == 0) {
+#pragma unroll
+            for (int h = 0; h < kTcHeads; ++h) mfin[h] = m_run[h];
+        }
     } else {
         // ================= value warps: V -> V^T operand =================
         if constexpr (C::VHALF) {
@@ -1176,13 +1211,6 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         const int qw = warp & 3;
         const uint32_t lane_off = (uint32_t)(qw * 32) << 16;
 #pragma unroll
-        for (int h = 0; h < kTcHeads; ++h) {
-            float v = l_run[h];
-#pragma unroll
-            for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-            if (lane == 0) red[qw * kTcHeads + h] = v;
-        }
-#pragma unroll
         for (int mb = 0; mb < C::MB; ++mb) {
             float o[kTcHeads];
             if (n_active > 0) {
@@ -1196,14 +1224,13 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 #pragma unroll
             for (int h = 0; h < kTcHeads; ++h) mo[h * D + d] = o[h];
         }
-        if (warp == kSmWarp0 && lane == 0) {
-#pragma unroll
-            for (int h = 0; h < kTcHeads; ++h) mm[h] = m_run[h] == kNoMax ? -INFINITY : m_run[h];
-        }
     }
     tc_fence_before();
     __syncthreads();
-    if (tid < kTcHeads) ml[tid] = red[tid] + red[16 + tid] + red[32 + tid] + red[48 + tid];
+    if (tid < kTcHeads) {
+        ml[tid] = red[tid] + red[16 + tid] + red[32 + tid] + red[48 + tid];
+        mm[tid] = mfin[tid] == kNoMax ? -INFINITY : mfin[tid];
+    }
     __syncthreads();
     if (warp == kMmaWarp) {
         tc_fence_after();
