@@ -30,10 +30,15 @@ constexpr int kMmaMaxChunk = 4096;
 // QSDPA_KERNEL_AUTO takes the tcgen05 kernel from this many keys per KV head
 // and GQA groups of at least kAutoTcMinGqa heads; below either the mma.sync
 // kernel wins (measured: GQA-16 D=256 10.3 vs 9.2 us at 1K keys, 14.0 vs 14.6
-// at 16K, 35.0 vs 39.3 at 128K; one head per KV head, D=128 8-bit at 128K:
-// 162 vs 102 us)
+// at 16K, 35.0 vs 39.3 at 128K)
 constexpr int kAutoTcMinKeys = 16384;
 constexpr int kAutoTcMinGqa = 8;
+// smaller GQA groups (e.g. one head per KV head, D=128, 8-bit, 8 KV heads):
+// tcgen05 with one CTA per SM from this many keys (measured at 16K / 32K /
+// 64K / 128K keys: 17.8 vs 18.5, 26.8 vs 31.0, 46.3 vs 55.7, 83.4 vs 101.7 us;
+// symmetric 4-bit gs128 15.7 vs 14.4, 23.2 vs 23.5, 38.0 vs 40.5, 68.1 vs
+// 74.4); more units than SMs (32 rows x 8 KV heads) stay on mma.sync
+constexpr int kAutoTcMinKeysSmall = 32768;
 }  // namespace
 
 int set_error(int code, const char* fmt, ...) {
@@ -197,10 +202,16 @@ int make_plan(const qsdpa_decode_params* p, const DecodeArgs& a, Plan& pl) {
         case QSDPA_KERNEL_SIMT:
             pl.kern = Kern::Simt;
             break;
-        default:
-            pl.kern = tc_ok && (a.causal_qL || (p->N >= kAutoTcMinKeys && a.gqa >= kAutoTcMinGqa)) ? Kern::Tc
-                      : mma_ok                                                                       ? Kern::Mma
-                                                                                                     : Kern::Simt;
+        default: {
+            // groups of fewer heads (padded to 16 on both tensor-core kernels)
+            // go to tcgen05 only when its one-wave plan covers them: at most one
+            // 16-head block per SM
+            const int tc_units = a.B * a.Hkv * ((a.gqa + 15) / 16);
+            const bool tc_auto =
+                a.causal_qL || (p->N >= kAutoTcMinKeys && a.gqa >= kAutoTcMinGqa) ||
+                (p->N >= kAutoTcMinKeysSmall && tc_units <= sm_count());
+            pl.kern = tc_ok && tc_auto ? Kern::Tc : mma_ok ? Kern::Mma : Kern::Simt;
+        }
     }
     if (a.causal_qL && pl.kern != Kern::Tc)
         return set_error(QSDPA_ERR_UNSUPPORTED,
@@ -216,11 +227,12 @@ int make_plan(const qsdpa_decode_params* p, const DecodeArgs& a, Plan& pl) {
         // chunk holds kLongChunk keys; CUDA-core kernel: two waves of 4 per SM.
         // No chunk below kMinChunk.
         if (pl.kern == Kern::Tc) {
-            // one CTA per SM (its shared memory fills the SM) and exactly one
+            // one CTA per SM (its shared memory fills the SM) and at most one
             // wave, however long the chunks get: a second, ragged wave costs
             // more than the longer walk (measured at 1M keys, GQA-16 D=256:
-            // 148 CTAs 171.8 us, 256 CTAs 197.5 us, 294 CTAs 179.2 us)
-            splits = (sm_count() + units - 1) / units;
+            // 148 CTAs 171.8 us, 256 CTAs 197.5 us, 294 CTAs 179.2 us), so the
+            // split count rounds down (8 KV heads: 18 splits, 144 CTAs)
+            splits = sm_count() / units;
         } else if (pl.use_mma) {
             const int lo = (sm_count() + units - 1) / units, hi = (2 * sm_count() + units - 1) / units;
             const int by_long = (p->N + kLongChunk - 1) / kLongChunk;

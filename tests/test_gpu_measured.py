@@ -3,7 +3,7 @@
 The other GPU tests run the reference tests' shapes at small contexts; these
 run the measured configurations themselves: the headline GQA-16 decode at
 131,072 keys with the automatic split plan, the non-GQA configuration at
-16,384 keys (bfloat16 8-bit gs64, and symmetric 4-bit gs128), and one
+16,384 and 65,536 keys (bfloat16 8-bit gs64, and symmetric 4-bit gs128), and one
 continuous-batching decode step at batch 32 with per-row lengths drawn from
 U[2048, 32768].  K/V are fp16/bf16 N(0, std) quantised on the GPU by the
 library's own quantize kernel (bit-exact with the oracle's quantizer, tested
@@ -75,22 +75,28 @@ def test_config2_131072_keys_automatic_splits(qs):
 
 
 @pytest.mark.slow
+@pytest.mark.parametrize("N,kernel", [(16384, "mma"), (65536, "tcgen05")])
 @pytest.mark.parametrize("variant", ["bf16_8bit_gs64", "bf16_sym_4bit_gs128"])
-def test_config3_16384_keys(qs, variant):
-    """Non-GQA configuration (H_q = H_kv = 8, D=128, bfloat16, K/V ~ N(0, 0.5))
-    at 16,384 keys: affine 8-bit gs64, and the symmetric variant (affine
-    codes, biases=None) at 4-bit gs128."""
-    B, H, N, D = 1, 8, 16384, 128
+def test_config3_keys(qs, variant, N, kernel):
+    """Non-GQA configuration (H_q = H_kv = 8, D=128, bfloat16, K/V ~ N(0, 0.5)):
+    affine 8-bit gs64, and the symmetric variant (affine codes, biases=None)
+    at 4-bit gs128.  The automatic choice takes the mma.sync kernel at 16,384
+    keys and the tcgen05 kernel (one CTA per SM, 18 splits of 8 KV heads) at
+    65,536."""
+    from mlx_qsdpa import _lib
+    B, H, D = 1, 8, 128
     bits, gs, sym = (8, 64, False) if variant == "bf16_8bit_gs64" else (4, 128, True)
     (pk, ks, kb), (pv, vs, vb) = quantized_kv(B, H, N, D, bits, gs, torch.bfloat16, 0.5, seed=3 + bits)
     rng = np.random.default_rng(3)
     qn = normal(rng, (B, H, 1, D), O.BF16)
     q = to_torch(qn, O.BF16)
-    out = from_torch(qs.quantized_sdpa(q, pk, pv, ks, vs, None if sym else kb, None if sym else vb, bits=bits,
-                                       group_size=gs))
+    kb_, vb_ = (None, None) if sym else (kb, vb)
+    chosen = _lib.plan_kernel(q, pk, pv, ks, vs, kb_, vb_, bits, gs)
+    assert chosen == {"mma": _lib.KERNEL_MMA, "tcgen05": _lib.KERNEL_TCGEN05}[kernel]
+    out = from_torch(qs.quantized_sdpa(q, pk, pv, ks, vs, kb_, vb_, bits=bits, group_size=gs))
     ref = O.sdpa(qn, oracle_kv((pk, ks, kb), bits, gs, O.BF16, sym), oracle_kv((pv, vs, vb), bits, gs, O.BF16, sym),
                  dtype=O.BF16)
-    assert_close(out, ref, what=f"config 3 {variant}")
+    assert_close(out, ref, what=f"config 3 {variant} at {N} keys ({kernel})")
 
 
 @pytest.mark.slow
