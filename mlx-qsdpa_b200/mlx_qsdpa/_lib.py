@@ -196,7 +196,8 @@ def _stream(dev: torch.device) -> int:
 
 def rows_contiguous(t: torch.Tensor) -> torch.Tensor:
     """Return ``t`` (or a copy) whose last two dims are densely packed."""
-    if t.stride(-1) == 1 and (t.shape[-2] <= 1 or t.stride(-2) == t.shape[-1]):
+    st, sh = t.stride(), t.shape
+    if st[-1] == 1 and (sh[-2] <= 1 or st[-2] == sh[-1]):
         return t
     return t.contiguous()
 
@@ -294,7 +295,8 @@ def decode(q: torch.Tensor, kp, vp, ks, vs, kb, vb, *, scale: float, bits: int, 
     ref = ctypes.byref(p)
     if shard is not None:
         bufs, state, rank, world = shard
-        ptrs = (_c_vp * world)(*[int(b) for b in bufs])
+        # a ctypes array of the peers' buffer pointers (PeerExchange builds it once)
+        ptrs = bufs if isinstance(bufs, ctypes.Array) else (_c_vp * world)(*[int(b) for b in bufs])
         call = lambda: lib.qsdpa_decode_shard(ref, ptrs, state.data_ptr(), rank, world, stream)  # noqa: E731
         what = "qsdpa_decode_shard"
     else:

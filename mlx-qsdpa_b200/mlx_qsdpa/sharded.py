@@ -24,6 +24,8 @@ own rows.
 
 from __future__ import annotations
 
+import ctypes
+
 import warnings
 
 from typing import Callable, Optional
@@ -106,7 +108,12 @@ class PeerExchange:
         self.buf.zero_()
         self.handle = symm.rendezvous(self.buf, self.group)
         self.ptrs = list(self.handle.buffer_ptrs)
+        self._ptr_array = (ctypes.c_void_p * self.world)(*[int(b) for b in self.ptrs])
         self.state = torch.zeros(2, dtype=torch.int32, device=dev)
+        # this rank's record of a step, [o (rows x D) | m, l (rows x 2)]: scratch
+        # of the fused decode + exchange; steps on one exchange run in stream order
+        self.rec = torch.empty(rows * (D + 2), dtype=torch.float32, device=dev)
+        self.part = (self.rec[: rows * D].view(rows, D), self.rec[rows * D:].view(rows, 2))
         torch.cuda.synchronize(dev)
         dist.barrier(group=self.group)
 
@@ -116,7 +123,7 @@ class PeerExchange:
 
     def shard_args(self):
         """(bufs, state, rank, world) for ``_lib.decode(..., shard=...)`` (qsdpa_decode_shard)."""
-        return self.ptrs, self.state, self.rank, self.world
+        return self._ptr_array, self.state, self.rank, self.world
 
 
 def _gather(t: torch.Tensor, group) -> torch.Tensor:
@@ -161,15 +168,17 @@ def sharded_quantized_sdpa(q, k_quant, v_quant, *, bits=4, group_size=32, scale=
     if scale is None:
         scale = D ** -0.5
     rows = B * Hq
+    if exchange is not None and partial_fn is None:
+        # decode and peer merge in one call (the split records merged and
+        # exchanged by one kernel); the exchange holds the record scratch
+        if (exchange.rows, exchange.D) != (rows, D):
+            raise ValueError(f"exchange built for {exchange.rows} rows x D={exchange.D}, call has {rows} x {D}")
+        out = torch.empty((B, Hq, 1, D), dtype=q.dtype, device=q.device)
+        return _partial_cuda(q, k_quant, v_quant, scale, bits, group_size, mask, exchange.part, out=out,
+                             shard=exchange.shard_args())
     # one packed record per rank, [o (rows x D) | m, l (rows x 2)]: one all-gather
     rec = torch.empty(rows * (D + 2), dtype=torch.float32, device=q.device)
     part = (rec[: rows * D].view(rows, D), rec[rows * D:].view(rows, 2))
-    if exchange is not None and partial_fn is None:
-        # decode and peer merge in one call (the split records merged and
-        # exchanged by one kernel)
-        out = torch.empty((B, Hq, 1, D), dtype=q.dtype, device=q.device)
-        return _partial_cuda(q, k_quant, v_quant, scale, bits, group_size, mask, part, out=out,
-                             shard=exchange.shard_args())
     if partial_fn is None:
         _partial_cuda(q, k_quant, v_quant, scale, bits, group_size, mask, part)
     else:
