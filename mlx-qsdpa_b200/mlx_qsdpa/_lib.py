@@ -394,18 +394,22 @@ def quantize_into(x: torch.Tensor, packed: torch.Tensor, scales: torch.Tensor, b
                   slot0: int, bits: int, group_size: int, ring: bool = False):
     """Quantize x (B, H, S, D) into cache slots [slot0, slot0+S) (mod cap if ring)."""
     lib = load()
-    if x.stride(-1) != 1:
+    xs = x.stride()
+    if xs[-1] != 1:
         x = x.contiguous()
+        xs = x.stride()
     B, H, S, D = x.shape
-    cap = packed.shape[2]
+    strides = []
     for t in (packed, scales, biases):
-        if t.stride(-1) != 1 or (t.shape[2] > 1 and t.stride(2) != t.shape[3]):
+        ts, tsh = t.stride(), t.shape
+        if ts[3] != 1 or (tsh[2] > 1 and ts[2] != tsh[3]):
             raise ValueError("cache buffers must have contiguous token rows")
-    p = QuantizeParams()
-    p.x = x.data_ptr(); p.x_sb, p.x_sh, p.x_ss = x.stride(0), x.stride(1), x.stride(2)
-    p.packed = packed.data_ptr(); p.p_sb, p.p_sh = packed.stride(0), packed.stride(1)
-    p.scales = scales.data_ptr(); p.s_sb, p.s_sh = scales.stride(0), scales.stride(1)
-    p.biases = biases.data_ptr(); p.b_sb, p.b_sh = biases.stride(0), biases.stride(1)
+        strides.append(ts)
+    cap = packed.shape[2]
+    p = QuantizeParams(x=x.data_ptr(), x_sb=xs[0], x_sh=xs[1], x_ss=xs[2],
+                       packed=packed.data_ptr(), p_sb=strides[0][0], p_sh=strides[0][1],
+                       scales=scales.data_ptr(), s_sb=strides[1][0], s_sh=strides[1][1],
+                       biases=biases.data_ptr(), b_sb=strides[2][0], b_sh=strides[2][1])
     p.B, p.H, p.S, p.D = B, H, S, D
     p.bits, p.group_size, p.dtype = bits, group_size, dtype_code(x.dtype)
     p.slot0, p.cap, p.ring = int(slot0), int(cap), int(bool(ring))

@@ -33,6 +33,7 @@ from __future__ import annotations
 
 from typing import List
 
+import numpy as np
 import torch
 
 from . import _lib
@@ -388,10 +389,9 @@ class BatchQuantizedSDPACache:
 
     def kv_ranges(self) -> KVRanges:
         """Physically valid keys of every row: slots [left_padding_b, _idx)."""
-        start = self.left_padding.clamp(min=0)
-        length = (self._idx - start).clamp(min=0)
-        r = KVRanges(start, length)
-        return r.to(self._device()) if self._device() is not None else r
+        start = np.maximum(self.left_padding.numpy(), 0)
+        length = np.maximum(self._idx - start, 0)
+        return KVRanges.from_host(start, length, self._device())
 
     def filter(self, batch_indices):
         """Keep the given rows (cache.py:378-391); slots every kept row pads drop."""
@@ -693,14 +693,21 @@ class BatchQuantizedRotatingSDPACache:
         """cache.py:796-811."""
         slot = self._idx % self.max_size
         if self._idx >= self.max_size:
-            # the write replaces each row's oldest visible slot
-            self._pad = (self._pad - 1).clamp(min=0)
+            # the write replaces each row's oldest visible slot (the padding
+            # count is this cache's own host array: updated in place)
+            pad = self._pad.numpy()
+            np.maximum(pad - 1, 0, out=pad)
         _quantize(self, keys, self._keys, slot)
         _quantize(self, values, self._values, slot)
         self.offset = self.offset + 1
         self._idx += 1
         n = min(self._idx, self.max_size)
-        return _view(self._keys, n), _view(self._values, n)
+        # once the ring is full every decode returns the same views: keep them
+        cached = getattr(self, "_views", None)
+        if cached is None or cached[0] != n or cached[1] is not self._keys or cached[2] is not self._values:
+            cached = (n, self._keys, self._values, _view(self._keys, n), _view(self._values, n))
+            self._views = cached
+        return cached[3], cached[4]
 
     def _update_prefill(self, keys, values):
         """cache.py:813-840."""
@@ -743,11 +750,8 @@ class BatchQuantizedRotatingSDPACache:
         """Each row's valid ring window over the visible slots (padding excluded)."""
         n = min(self._idx, self.max_size)
         oldest = self._idx % self.max_size if self._idx >= self.max_size else 0
-        pad = self._pad.clamp(min=0, max=n)
-        start = (oldest + pad) % max(n, 1)
-        length = n - pad
-        r = KVRanges(start, length)
-        return r.to(self._device()) if self._device() is not None else r
+        pad = np.minimum(np.maximum(self._pad.numpy(), 0), n)
+        return KVRanges.from_host((oldest + pad) % max(n, 1), n - pad, self._device())
 
     def filter(self, batch_indices):
         """Keep the given rows (cache.py:868-876)."""

@@ -57,6 +57,19 @@ class KVRanges:
     def to(self, device) -> "KVRanges":
         return KVRanges(self.start.to(device, non_blocking=True), self.length.to(device, non_blocking=True))
 
+    @classmethod
+    def from_host(cls, start, length, device) -> "KVRanges":
+        """Windows computed on the host (integer arrays of one row each):
+        one copy of [start | length] from pinned memory to ``device``."""
+        n = len(start)
+        buf = torch.empty(2 * n, dtype=torch.int32, pin_memory=device is not None and torch.device(device).type == "cuda")
+        v = buf.numpy()
+        v[:n] = start
+        v[n:] = length
+        if device is not None:
+            buf = buf.to(device, non_blocking=True)
+        return cls(buf[:n], buf[n:])
+
     def as_mask(self, N: int) -> torch.Tensor:
         """Equivalent boolean mask of shape (B, 1, 1, N)."""
         i = torch.arange(N, device=self.start.device)
