@@ -83,8 +83,11 @@ class PeerExchange:
     """Peer-memory merge of the ranks' partial records (qsdpa_shard_merge).
 
     Allocates this rank's symmetric buffer (torch symmetric memory, addressable
-    by every rank of ``group`` over NVLink) and a two-word device step counter.
-    Collective: every rank of the group constructs it with the same sizes.
+    by every rank of ``group`` over NVLink), a two-word device step counter and
+    the record scratch of one step.  Collective: every rank of the group
+    constructs it with the same sizes.  One exchange runs one step at a time:
+    its steps must be ordered on one stream (as a model's layers are), every
+    rank taking the same steps in the same order.
     """
 
     def __init__(self, rows: int, D: int, group=None, device=None):
