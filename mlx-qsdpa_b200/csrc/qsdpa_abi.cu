@@ -25,7 +25,10 @@ constexpr int kMaxSplits = 1024;
 constexpr int kMinChunk = 64;  // keys per CTA below which splitting stops paying
 constexpr int kLongChunk = 256;  // keys per CTA from which a second CTA per SM pays off
 constexpr int kMinChunkTc = 128;  // one tile of the tcgen05 kernel
-constexpr int kMaxQL = 16;        // queries per head of one call
+constexpr int kMaxQL = 65536;     // queries per head of one call
+constexpr int kMaxQLDecode = 16;  // up to this many: the decode kernels (a head row each)
+constexpr int kPrefillRows = 128;  // rows per CTA of the fused prefill
+constexpr int kPrefillMinChunk = 512;  // keys per split of the fused prefill, at least
 constexpr int kMmaMaxChunk = 4096;
 // QSDPA_KERNEL_AUTO takes the tcgen05 kernel from this many keys per KV head
 // and GQA groups of at least kAutoTcMinGqa heads; below either the mma.sync
@@ -73,7 +76,7 @@ int mma_tile();
 
 namespace {
 
-enum class Kern { Tc, Mma, Simt };
+enum class Kern { Tc, Mma, Simt, Prefill };
 
 struct Plan {
     Kern kern;
@@ -190,6 +193,42 @@ void fill_args(const qsdpa_decode_params* p, DecodeArgs& a) {
 // error.
 int make_plan(const qsdpa_decode_params* p, const DecodeArgs& a, Plan& pl) {
     const bool tc_ok = tc_supported(a), mma_ok = mma_supported(a);
+    if (p->qL > kMaxQLDecode) {
+        // many queries per head: the fused prefill (tcgen05), 128 rows per CTA
+        if (p->kernel != QSDPA_KERNEL_AUTO && p->kernel != QSDPA_KERNEL_TCGEN05)
+            return set_error(QSDPA_ERR_UNSUPPORTED, "qL > %d runs on the tcgen05 fused prefill only", kMaxQLDecode);
+        if (!prefill_supported(a, p->dtype))
+            return set_error(QSDPA_ERR_UNSUPPORTED,
+                             "fused prefill: needs D 128/256, 16-byte aligned rows, and not 8-bit D=256 in bfloat16");
+        if (p->kv_len)
+            return set_error(QSDPA_ERR_UNSUPPORTED, "fused prefill: per-row key windows are not supported");
+        pl.kern = Kern::Prefill;
+        pl.use_mma = true;
+        pl.heads_per_block = kPrefillRows;
+        pl.head_blocks = (a.gqa + kPrefillRows - 1) / kPrefillRows;
+        const int units = a.B * a.Hkv * pl.head_blocks;
+        int splits = p->splits;
+        if (splits == 0) {
+            // one wave of one CTA per SM, no split under kPrefillMinChunk keys
+            splits = sm_count() / units;
+            const int by_len = (p->N + kPrefillMinChunk - 1) / kPrefillMinChunk;
+            if (splits > by_len) splits = by_len;
+            if (splits < 1) splits = 1;
+            if (splits > kMaxSplits) splits = kMaxSplits;
+        }
+        // chunks of whole 64-key tiles
+        pl.chunk = p->N > 0 ? ((p->N + splits - 1) / splits + 63) / 64 * 64 : 0;
+        if (p->N > 0) splits = (p->N + pl.chunk - 1) / pl.chunk;
+        pl.splits = splits;
+        if (splits == 1) {
+            pl.ws_bytes = 0;
+        } else {
+            const size_t rows = (size_t)a.B * a.Hq;
+            pl.ws_bytes =
+                align256(rows * splits * a.D * sizeof(float)) + align256(rows * splits * 2 * sizeof(float));
+        }
+        return QSDPA_OK;
+    }
     switch (p->kernel) {
         case QSDPA_KERNEL_TCGEN05:
             if (!tc_ok) return set_error(QSDPA_ERR_UNSUPPORTED, "tcgen05 kernel: needs D 128/256 and 16-byte aligned K/V rows, scales, biases");
@@ -289,7 +328,9 @@ extern "C" int qsdpa_decode_kernel(const qsdpa_decode_params* p) {
     Plan pl;
     rc = make_plan(p, a, pl);
     if (rc) return rc;
-    return pl.kern == Kern::Tc ? QSDPA_KERNEL_TCGEN05 : pl.kern == Kern::Mma ? QSDPA_KERNEL_MMA : QSDPA_KERNEL_SIMT;
+    return (pl.kern == Kern::Tc || pl.kern == Kern::Prefill) ? QSDPA_KERNEL_TCGEN05
+           : pl.kern == Kern::Mma                              ? QSDPA_KERNEL_MMA
+                                                               : QSDPA_KERNEL_SIMT;
 }
 
 extern "C" size_t qsdpa_decode_workspace_size(const qsdpa_decode_params* p) {
@@ -327,9 +368,10 @@ int launch_decode(const qsdpa_decode_params* p, cudaStream_t st, DecodeArgs& a, 
         a.ws_o = reinterpret_cast<float*>(ws);
         a.ws_ml = reinterpret_cast<float*>(ws + align256(rows * pl.splits * a.D * sizeof(float)));
     }
-    return pl.kern == Kern::Tc    ? launch_decode_tc(a, p->dtype, st)
-           : pl.kern == Kern::Mma ? launch_decode_mma(a, p->dtype, st)
-                                  : launch_decode_simt(a, p->dtype, st);
+    return pl.kern == Kern::Tc        ? launch_decode_tc(a, p->dtype, st)
+           : pl.kern == Kern::Prefill ? launch_prefill_tc(a, p->dtype, st)
+           : pl.kern == Kern::Mma     ? launch_decode_mma(a, p->dtype, st)
+                                      : launch_decode_simt(a, p->dtype, st);
 }
 
 }  // namespace

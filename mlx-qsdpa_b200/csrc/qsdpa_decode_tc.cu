@@ -1424,6 +1424,495 @@ int launch_tc2(const DecodeArgs& a, cudaStream_t st) {
     return set_error(QSDPA_ERR_UNSUPPORTED, "tcgen05 decode: D=%d", a.D);
 }
 
+// ============================ fused prefill ============================
+// Many queries per head (qL > 16: a prompt chunk or speculative drafts
+// against a quantized cache).  Each CTA takes 128 (head, position) rows of
+// one KV head -- the M of both MMAs -- and streams the keys of its split in
+// 64-key tiles, each dequantised once for all 128 rows:
+//   S (128 rows x 64 keys)  = Q (128 x D) . K_tile^T          A, B K-major
+//   O (128 rows x D)       += P (128 x 64) . V_tile (64 x D)  A K-major, B MN-major
+// The softmax of a row is one thread's loop over its TMEM lane (lane = row):
+// no reduction across threads.  Roles (10 warps): four dequantising warps
+// (the key tile into the K operand, then the value tile into the V operand;
+// two threads per key, half of the head dims each), four softmax warps (stage
+// Q, then per tile read S, online softmax, write P; at the end read O), a
+// producer warp (16-byte cp.async of packed rows, scales and biases into a
+// ring) and an MMA warp (TMEM owner, issues both products from one elected
+// lane).  The K, V and P operands are single buffers, S has two TMEM buffers.
+// Same conventions as the decode kernel: log2-domain softmax with the running
+// maximum raised only past 2^8, bounded mbarrier waits, head dims of 4-bit
+// words in the order 0,4,1,5,2,6,3,7 (put back at the output).
+constexpr int kPfRows = 128;    // query rows per CTA: M of both MMAs
+constexpr int kPfKeys = 64;     // keys per tile: N of the S MMA, K of the P V MMA
+constexpr int kPfSmWarp0 = 4;   // warps 0-3 dequantise, 4-7 run the softmax
+constexpr int kPfProdWarp = 8;
+constexpr int kPfMmaWarp = 9;
+constexpr int kPfThreads = 10 * 32;
+constexpr int kPfTmemS = 0;     // two S buffers of 64 columns
+constexpr int kPfTmemO = 128;   // O: D columns
+
+template <int BITS, int D, int GS, bool SPLITP>
+struct PfCfg {
+    static constexpr int EPW = 32 / BITS;
+    static constexpr int PD = D / EPW;
+    static constexpr int ROWB = PD * 4;
+    static constexpr int CPR = ROWB / 16;                  // 16-byte chunks per packed row
+    static constexpr int G = D / GS;
+    static constexpr int SROWB = G * 2;
+    static constexpr int PACK_BYTES = kPfKeys * ROWB;
+    static constexpr int SC_BYTES = kPfKeys * SROWB;       // a multiple of 16 (64 rows)
+    static constexpr int SC_CHUNKS = SC_BYTES / 16;
+    static constexpr int STAGE_BYTES = (2 * PACK_BYTES + 4 * SC_BYTES + 1023) / 1024 * 1024;
+    static constexpr int Q_BYTES = kPfRows * D * 2;
+    static constexpr int OP_BYTES = kPfKeys * D * 2;       // K operand; V operand
+    static constexpr int OP_LBO = kPfKeys * 128;           // between 64-dim blocks of an operand
+    static constexpr int P_BYTES = kPfRows * kPfKeys * 2;  // one P operand (hi or lo)
+    static constexpr int P_ALL = (SPLITP ? 2 : 1) * P_BYTES;
+    static constexpr int MISC_BYTES = 1024;
+    static constexpr int FIXED = 1024 + Q_BYTES + 2 * OP_BYTES + P_ALL + MISC_BYTES;
+    static constexpr int STAGES_FIT = (kSmemLimit - FIXED) / STAGE_BYTES;
+    // 256-byte rows in bfloat16 leave room for one stage only: not supported
+    static constexpr bool SUPPORTED = STAGES_FIT >= 2;
+    static constexpr int STAGES = STAGES_FIT > 4 ? 4 : (STAGES_FIT < 2 ? 2 : STAGES_FIT);
+    static constexpr int SMEM_RAW = FIXED + STAGES * STAGE_BYTES;
+    static constexpr int SMEM = SMEM_RAW > 116 * 1024 ? SMEM_RAW : 116 * 1024;
+    static constexpr int EPC = 128 / BITS;                 // codes per 16-byte chunk
+    static constexpr int PPC = EPC / 2;                    // half2 pairs per chunk
+    static constexpr int HALF_CHUNKS = CPR / 2;            // chunks of a dequantising thread
+    static_assert(kPfTmemO + D <= 512, "TMEM budget");
+    static_assert(CPR % 2 == 0 && (kPfKeys * CPR) % 32 == 0 && SC_BYTES % 16 == 0, "copy plan");
+};
+
+__device__ __forceinline__ void tmem_ld32f(uint32_t taddr, float v[32]) {
+    uint32_t r[32];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,"
+        "%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];\n"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+          "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+          "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+        : "r"(taddr)
+        : "memory");
+#pragma unroll
+    for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+template <typename T, int BITS, int D, int GS>
+__global__ void __launch_bounds__(kPfThreads, 1) prefill_tc_kernel(const DecodeArgs a) {
+    using C = PfCfg<BITS, D, GS, Ops<T>::kSplitP>;
+    constexpr bool kBf16 = !std::is_same<T, __half>::value;
+    constexpr uint32_t IDESC_S = make_idesc(kBf16, false, false, kPfRows, kPfKeys);
+    constexpr uint32_t IDESC_PV = make_idesc(kBf16, false, true, kPfRows, D);
+    constexpr int ST = C::STAGES;
+    constexpr int EPC = C::EPC, PPC = C::PPC;
+
+    extern __shared__ __align__(1024) char smem_raw[];
+    const uint32_t raw_u32 = smem_u32(smem_raw);
+    char* smem = smem_raw + (((raw_u32 + 1023u) & ~1023u) - raw_u32);
+    char* sQ = smem;                    // Q: 64-dim blocks of 128 rows x 128 B
+    char* sK = sQ + C::Q_BYTES;         // K operand: 64-dim blocks of 64 key rows x 128 B
+    char* sVo = sK + C::OP_BYTES;       // V operand: the same layout, read MN-major
+    char* sP = sVo + C::OP_BYTES;       // P: 128 rows x 128 B (hi, then lo for bf16)
+    char* ring = sP + C::P_ALL;
+    char* misc = ring + ST * C::STAGE_BYTES;
+    const uint32_t mb0 = smem_u32(misc);
+    auto full_bar = [&](int s) { return mb0 + 8u * s; };            // count 32: producer lanes
+    auto empty_bar = [&](int s) { return mb0 + 8u * (4 + s); };     // count 4: dequantising warps
+    const uint32_t kready_bar = mb0 + 8u * 8;                       // count 4: K operand written
+    const uint32_t vready_bar = mb0 + 8u * 9;                       // count 4: V operand written
+    auto sready_bar = [&](int k) { return mb0 + 8u * (10 + k); };   // commit: S of a tile (K operand free)
+    auto sfree_bar = [&](int k) { return mb0 + 8u * (12 + k); };    // count 4: softmax read S buffer k
+    const uint32_t pready_bar = mb0 + 8u * 14;                      // count 4: P written
+    const uint32_t pvdone_bar = mb0 + 8u * 15;                      // commit: P V of a tile (V, P free)
+    const uint32_t qready_bar = mb0 + 8u * 16;                      // count 4: Q staged
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(misc + 192);
+
+    const int split = blockIdx.x;
+    const int unit = blockIdx.y;
+    const int b = unit / a.Hkv;
+    const int kvh = unit - b * a.Hkv;
+    const int r0 = blockIdx.z * kPfRows;          // first row of the block among the KV head's rows
+    const int nrows = min(kPfRows, a.gqa - r0);   // rows of the block that exist
+    const int tid = threadIdx.x;
+    const int warp = tid >> 5;
+    const int lane = tid & 31;
+    const int p_lo = split * a.chunk;
+    const int p_hi = min(a.N, p_lo + a.chunk);
+    const int ntiles = p_hi > p_lo ? (p_hi - p_lo + kPfKeys - 1) / kPfKeys : 0;
+
+    const char* kp_b = reinterpret_cast<const char*>(a.kp + (int64_t)b * a.kp_sb + (int64_t)kvh * a.kp_sh);
+    const char* vp_b = reinterpret_cast<const char*>(a.vp + (int64_t)b * a.vp_sb + (int64_t)kvh * a.vp_sh);
+    const char* ks = static_cast<const char*>(a.ks) + ((int64_t)b * a.ks_sb + (int64_t)kvh * a.ks_sh) * 2;
+    const char* vs = static_cast<const char*>(a.vs) + ((int64_t)b * a.vs_sb + (int64_t)kvh * a.vs_sh) * 2;
+    const bool has_bias = a.kb != nullptr;
+    const char* kb = has_bias ? static_cast<const char*>(a.kb) + ((int64_t)b * a.kb_sb + (int64_t)kvh * a.kb_sh) * 2
+                              : nullptr;
+    const char* vb = has_bias ? static_cast<const char*>(a.vb) + ((int64_t)b * a.vb_sb + (int64_t)kvh * a.vb_sh) * 2
+                              : nullptr;
+    bool dead = false;
+
+    // ---- producer: stage of tile j = packed K and V rows, scale / bias rows ----
+    auto issue_stage = [&](int j) {
+        const int s = j % ST;
+        const int p0 = p_lo + j * kPfKeys;
+        char* st = ring + s * C::STAGE_BYTES;
+        const int rows_valid = min(kPfKeys, p_hi - p0);
+        const char* ksrc = kp_b + (int64_t)p0 * C::ROWB + lane * 16;
+        const char* vsrc = vp_b + (int64_t)p0 * C::ROWB + lane * 16;
+        // chunk k = lane + 32m (row k / CPR): swizzled line k/8 = lane/8 + 4m
+        const uint32_t d_even = (uint32_t)swz<8>(lane >> 3, lane & 7) * 16u;
+        const uint32_t d_odd = (uint32_t)swz<8>((lane >> 3) + 4, lane & 7) * 16u - 512u;
+        constexpr int M = kPfKeys * C::CPR / 32;
+        const int kvalid = rows_valid * C::CPR;
+#pragma unroll 4
+        for (int m = 0; m < M; ++m) {
+            const uint32_t dst = (m & 1 ? d_odd : d_even) + m * 512u;
+            const bool ok = lane + 32 * m < kvalid;
+            cp_async16(st + dst, ok ? ksrc + m * 512 : kp_b, ok ? 16 : 0);
+            cp_async16(st + C::PACK_BYTES + dst, ok ? vsrc + m * 512 : vp_b, ok ? 16 : 0);
+        }
+        const int sbytes = rows_valid * C::SROWB;
+        char* s0 = st + 2 * C::PACK_BYTES;
+        for (int k = lane; k < C::SC_CHUNKS; k += 32) {
+            const int off = k * 16;
+            const int nb = max(0, min(16, sbytes - off));
+            const int64_t goff = (int64_t)p0 * C::SROWB + (nb > 0 ? off : 0);
+            cp_async16(s0 + off, ks + goff, nb);
+            cp_async16(s0 + 2 * C::SC_BYTES + off, vs + goff, nb);
+            if (has_bias) {
+                cp_async16(s0 + C::SC_BYTES + off, kb + goff, nb);
+                cp_async16(s0 + 3 * C::SC_BYTES + off, vb + goff, nb);
+            }
+        }
+        cp_async_mbar_arrive(full_bar(s));
+    };
+
+    if (warp == kPfProdWarp) {
+        if (lane == 0) {
+#pragma unroll
+            for (int s = 0; s < ST; ++s) {
+                mbar_init(full_bar(s), 32);
+                mbar_init(empty_bar(s), 4);
+            }
+            mbar_init(kready_bar, 4);
+            mbar_init(vready_bar, 4);
+            mbar_init(sready_bar(0), 1);
+            mbar_init(sready_bar(1), 1);
+            mbar_init(sfree_bar(0), 4);
+            mbar_init(sfree_bar(1), 4);
+            mbar_init(pready_bar, 4);
+            mbar_init(pvdone_bar, 1);
+            mbar_init(qready_bar, 4);
+            asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
+        }
+        __syncwarp();
+        for (int j = 0; j < ST && j < ntiles; ++j) issue_stage(j);
+    }
+    if (warp == kPfMmaWarp) {
+        tmem_alloc(smem_u32(tmem_slot), kTmemCols);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tbase = *tmem_slot;
+
+    if (warp == kPfProdWarp) {
+        // ================= producer: the remaining stages =================
+        for (int j = ST; j < ntiles && !dead; ++j) {
+            mbar_wait(empty_bar(j % ST), ((j / ST) - 1) & 1, dead);
+            if (dead) break;
+            issue_stage(j);
+        }
+        cp_async_wait<0>();
+    } else if (warp == kPfMmaWarp) {
+        // ================= MMA issuer =================
+        const uint64_t qdesc = smem_desc(smem_u32(sQ), 16, 1024, kSw128);
+        const uint64_t kdesc = smem_desc(smem_u32(sK), 16, 1024, kSw128);
+        const uint64_t pdesc = smem_desc(smem_u32(sP), 16, 1024, kSw128);
+        const uint64_t vdesc = smem_desc(smem_u32(sVo), C::OP_LBO, 1024, kSw128);
+        mbar_wait(qready_bar, 0, dead);
+        for (int j = 0; j < ntiles && !dead; ++j) {
+            // S of tile j once its keys are in the K operand and the softmax
+            // warps have read S buffer j & 1 (tile j - 2)
+            mbar_wait(kready_bar, j & 1, dead);
+            if (j >= 2) mbar_wait(sfree_bar(j & 1), ((j - 2) >> 1) & 1, dead);
+            if (dead) break;
+            tc_fence_after();
+            if (elect_one()) {
+#pragma unroll
+                for (int k = 0; k < D / 16; ++k) {
+                    const uint64_t qa = qdesc + (uint64_t)(((k >> 2) * (kPfRows * 128) + (k & 3) * 32) >> 4);
+                    const uint64_t kk = kdesc + (uint64_t)(((k >> 2) * C::OP_LBO + (k & 3) * 32) >> 4);
+                    mma_ss(tbase + kPfTmemS + 64 * (j & 1), qa, kk, IDESC_S, k > 0 ? 1u : 0u);
+                }
+                mma_commit(sready_bar(j & 1));
+            }
+            __syncwarp();
+            // P V of tile j once P and the V operand are written
+            mbar_wait(pready_bar, j & 1, dead);
+            mbar_wait(vready_bar, j & 1, dead);
+            if (dead) break;
+            tc_fence_after();
+            if (elect_one()) {
+#pragma unroll
+                for (int k = 0; k < kPfKeys / 16; ++k) {
+                    const uint64_t pa = pdesc + (uint64_t)((k * 32) >> 4);
+                    const uint64_t vv = vdesc + (uint64_t)((2 * k * 1024) >> 4);
+                    mma_ss(tbase + kPfTmemO, pa, vv, IDESC_PV, (j > 0 || k > 0) ? 1u : 0u);
+                    if constexpr (Ops<T>::kSplitP)
+                        mma_ss(tbase + kPfTmemO, pa + (uint64_t)(C::P_BYTES >> 4), vv, IDESC_PV, 1u);
+                }
+                mma_commit(pvdone_bar);
+            }
+            __syncwarp();
+        }
+    } else if (warp < kPfSmWarp0) {
+        // ================= dequantising warps: K and V operands =================
+        const int t = tid & (kPfKeys - 1), hf = tid / kPfKeys;  // key t, half hf of its dims
+        const RowChunks<C::CPR> rows(t);
+        const uint32_t tx = (uint32_t)(t & 7) << 4;
+        char* const krow = sK + (t >> 3) * 1024 + (t & 7) * 128;
+        char* const vrow = sVo + (t >> 3) * 1024 + (t & 7) * 128;
+        // chunks [hf * HALF_CHUNKS, + HALF_CHUNKS) of key t's packed row, each 8
+        // dims one 16-byte store: 64-dim block w8 / 8, slot (w8 % 8) ^ (t % 8)
+        auto dequant_half = [&](const char* rows_base, const char* sc_row, char* row) {
+#pragma unroll
+            for (int cc = 0; cc < C::HALF_CHUNKS; ++cc) {
+                const int c = hf * C::HALF_CHUNKS + cc;
+                const int g = (c * EPC) / GS;
+                const uint32_t s2 = pair_at(sc_row + g * 2);
+                const uint32_t b2 = has_bias ? pair_at(sc_row + C::SC_BYTES + g * 2) : 0u;
+                uint32_t o[PPC];
+                dequant_chunk<T, BITS>(lds128(rows_base + rows.off(c)), s2, b2, o);
+#pragma unroll
+                for (int e = 0; e < PPC / 4; ++e) {
+                    const int w8 = c * (PPC / 4) + e;
+                    *reinterpret_cast<uint4*>(row + (w8 >> 3) * C::OP_LBO + (((uint32_t)(w8 & 7) << 4) ^ tx)) =
+                        make_uint4(o[4 * e], o[4 * e + 1], o[4 * e + 2], o[4 * e + 3]);
+                }
+            }
+        };
+        for (int j = 0; j < ntiles && !dead; ++j) {
+            const int s = j % ST;
+            mbar_wait(full_bar(s), (j / ST) & 1, dead);
+            const char* st = ring + s * C::STAGE_BYTES;
+            // the K operand is free once the S MMA of tile j - 1 completed
+            if (j >= 1) mbar_wait(sready_bar((j - 1) & 1), ((j - 1) >> 1) & 1, dead);
+            dequant_half(st, st + 2 * C::PACK_BYTES + t * C::SROWB, krow);
+            fence_proxy_async();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(kready_bar);
+            // the V operand once the P V MMA of tile j - 1 completed
+            if (j >= 1) mbar_wait(pvdone_bar, (j - 1) & 1, dead);
+            dequant_half(st + C::PACK_BYTES, st + 2 * C::PACK_BYTES + 2 * C::SC_BYTES + t * C::SROWB, vrow);
+            fence_proxy_async();
+            __syncwarp();
+            if (lane == 0) {
+                mbar_arrive(vready_bar);
+                mbar_arrive(empty_bar(s));
+            }
+        }
+    } else if (warp < kPfSmWarp0 + 4) {
+        // ================= softmax warps: thread = row = TMEM lane =================
+        const int r = tid - kPfSmWarp0 * 32;
+        const uint32_t lane_off = (uint32_t)((warp & 3) * 32) << 16;
+        {
+            // Q: rows r0.. of this KV head, K-major with the 128-byte swizzle (64-dim
+            // block kb at kb * 16 KB, row h at (h / 8) * 1024 + (h % 8) * 128)
+            const T* q = static_cast<const T*>(a.q) + (int64_t)b * a.q_sb + (int64_t)(kvh * a.gqa + r0) * a.q_sh;
+            const bool q_vec = ((uintptr_t)q % 16 == 0) && ((a.q_sh * 2) % 16 == 0);
+            constexpr int CH = kPfRows * D / 8;
+            for (int i = r; i < CH; i += kPfRows) {
+                const int h = i / (D / 8), w = i - h * (D / 8);  // chunk w = dims 8w..8w+7
+                uint32_t sq[4] = {0u, 0u, 0u, 0u};
+                if (h < nrows) {
+                    const T* src = q + (int64_t)h * a.q_sh + w * 8;
+                    if (q_vec) {
+                        const uint4 v = *reinterpret_cast<const uint4*>(src);
+                        sq[0] = v.x, sq[1] = v.y, sq[2] = v.z, sq[3] = v.w;
+                    } else {
+                        const uint16_t* s16 = reinterpret_cast<const uint16_t*>(src);
+#pragma unroll
+                        for (int e = 0; e < 4; ++e) sq[e] = (uint32_t)s16[2 * e] | ((uint32_t)s16[2 * e + 1] << 16);
+                    }
+                }
+                uint4 d;
+                if constexpr (BITS == 4) {  // positions 0..7 <- dims 0,4,1,5,2,6,3,7
+                    d.x = __byte_perm(sq[0], sq[2], 0x5410);
+                    d.y = __byte_perm(sq[0], sq[2], 0x7632);
+                    d.z = __byte_perm(sq[1], sq[3], 0x5410);
+                    d.w = __byte_perm(sq[1], sq[3], 0x7632);
+                } else {
+                    d = make_uint4(sq[0], sq[1], sq[2], sq[3]);
+                }
+                const int kblk = w >> 3, c = w & 7;
+                *reinterpret_cast<uint4*>(sQ + kblk * (kPfRows * 128) + (h >> 3) * 1024 + (h & 7) * 128 +
+                                          ((c ^ (h & 7)) * 16)) = d;
+            }
+            fence_proxy_async();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(qready_bar);
+        }
+        // causal: row r is query position (r0 + r) % qL, which sees keys up to
+        // N - qL + position
+        const int lim = a.causal_qL ? a.N - a.causal_qL + (r0 + r) % a.causal_qL : a.N - 1;
+        float m_run = kNoMax, l_run = 0.f;
+        char* const prow = sP + (r >> 3) * 1024 + (r & 7) * 128;
+        const uint32_t px = (uint32_t)(r & 7) << 4;
+        for (int j = 0; j < ntiles && !dead; ++j) {
+            mbar_wait(sready_bar(j & 1), (j >> 1) & 1, dead);
+            tc_fence_after();
+            float sv[kPfKeys];
+            tmem_ld32f(tbase + lane_off + kPfTmemS + 64 * (j & 1), sv);
+            tmem_ld32f(tbase + lane_off + kPfTmemS + 64 * (j & 1) + 32, sv + 32);
+            tmem_wait_ld();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(sfree_bar(j & 1));
+            const int p0 = p_lo + j * kPfKeys;
+            float mx = -INFINITY;
+#pragma unroll
+            for (int c = 0; c < kPfKeys; ++c) {
+                const int p = p0 + c;
+                const float v = (p < p_hi && p <= lim) ? sv[c] * a.scale_log2 : -INFINITY;
+                sv[c] = v;
+                mx = fmaxf(mx, v);
+            }
+            // the running maximum rises: rescale l and the row of O (the TMEM
+            // accesses are warp-wide, so a warp rescales when any of its rows
+            // does, the others with factor 1)
+            const bool up = mx > m_run + kRescaleTc;
+            const float alpha = up ? ex2(m_run - mx) : 1.f;
+            if (j >= 1 && __any_sync(0xffffffffu, up)) {
+                mbar_wait(pvdone_bar, (j - 1) & 1, dead);  // O holds P V of tile j - 1
+                tc_fence_after();
+#pragma unroll 1
+                for (int c0 = 0; c0 < D; c0 += 32) {
+                    float o[32];
+                    tmem_ld32f(tbase + lane_off + kPfTmemO + c0, o);
+                    tmem_wait_ld();
+                    uint32_t u[32];
+#pragma unroll
+                    for (int e = 0; e < 32; ++e) u[e] = __float_as_uint(o[e] * alpha);
+                    tmem_st32(tbase + lane_off + kPfTmemO + c0, u);
+                }
+                tmem_wait_st();
+            }
+            if (up) {
+                l_run *= alpha;
+                m_run = mx;
+            }
+            // the P operand is free once the P V MMA of tile j - 1 completed
+            if (j >= 1) {
+                mbar_wait(pvdone_bar, (j - 1) & 1, dead);
+                tc_fence_after();
+            }
+#pragma unroll
+            for (int c8 = 0; c8 < kPfKeys / 8; ++c8) {
+                uint32_t hi[4], lo[4];
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    const float pa = ex2(sv[8 * c8 + 2 * e] - m_run);
+                    const float pb = ex2(sv[8 * c8 + 2 * e + 1] - m_run);
+                    l_run += pa + pb;
+                    hi[e] = Ops<T>::pack(pa, pb);
+                    if constexpr (Ops<T>::kSplitP)
+                        lo[e] = Ops<T>::pack(pa - __uint_as_float(hi[e] << 16), pb - __uint_as_float(hi[e] & 0xffff0000u));
+                }
+                const uint32_t off = ((uint32_t)c8 << 4) ^ px;
+                *reinterpret_cast<uint4*>(prow + off) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+                if constexpr (Ops<T>::kSplitP)
+                    *reinterpret_cast<uint4*>(prow + C::P_BYTES + off) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+            }
+            fence_proxy_async();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(pready_bar);
+        }
+        // ---- the row's output: O / l (one split), or its record ----
+        if (ntiles > 0) {
+            mbar_wait(pvdone_bar, (ntiles - 1) & 1, dead);
+            tc_fence_after();
+        }
+        const int64_t grow = (int64_t)b * a.Hq + (int64_t)kvh * a.gqa + r0 + r;  // global row
+        const bool final_out = a.splits == 1 && a.out_mode == QSDPA_OUT_FINAL;
+        const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
+#pragma unroll 1
+        for (int c0 = 0; c0 < D; c0 += 32) {
+            float o[32];
+            if (ntiles > 0) {
+                tmem_ld32f(tbase + lane_off + kPfTmemO + c0, o);
+                tmem_wait_ld();
+            } else {
+#pragma unroll
+                for (int e = 0; e < 32; ++e) o[e] = 0.f;
+            }
+            if (r < nrows) {
+                if (final_out) {
+                    T* out = static_cast<T*>(a.out) + grow * D;
+#pragma unroll
+                    for (int e = 0; e < 32; ++e) out[tc_dim<BITS>(c0 + e)] = Dt<T>::from_f(o[e] * inv);
+                } else {
+                    float* dst = a.splits == 1 ? a.out_o + grow * D : a.ws_o + (grow * a.splits + split) * D;
+#pragma unroll
+                    for (int e = 0; e < 32; ++e) dst[tc_dim<BITS>(c0 + e)] = o[e];
+                }
+            }
+        }
+        if (r < nrows && !final_out) {
+            float* ml = a.splits == 1 ? a.out_ml + grow * 2 : a.ws_ml + (grow * a.splits + split) * 2;
+            ml[0] = m_run == kNoMax ? -INFINITY : m_run;
+            ml[1] = l_run;
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == kPfMmaWarp) {
+        tc_fence_after();
+        tmem_dealloc(tbase, kTmemCols);
+    }
+}
+
+template <typename T, int BITS, int D, int GS>
+int launch_pf4(const DecodeArgs& a, cudaStream_t st) {
+    using C = PfCfg<BITS, D, GS, Ops<T>::kSplitP>;
+    if constexpr (!C::SUPPORTED) {
+        return set_error(QSDPA_ERR_UNSUPPORTED, "fused prefill: D=%d at %d bits in bfloat16 does not fit", D, BITS);
+    } else {
+        auto kern = prefill_tc_kernel<T, BITS, D, GS>;
+        static bool attr_set[64] = {};
+        int dev = 0;
+        cudaGetDevice(&dev);
+        if (dev >= 0 && dev < 64 && !attr_set[dev]) {
+            cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
+            if (e != cudaSuccess) return set_error(QSDPA_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
+            attr_set[dev] = true;
+        }
+        const dim3 grid(a.splits, a.B * a.Hkv, a.head_blocks);
+        kern<<<grid, kPfThreads, C::SMEM, st>>>(a);
+        return check_launch("qsdpa_decode (fused prefill)");
+    }
+}
+
+template <typename T, int BITS, int D>
+int launch_pf3(const DecodeArgs& a, cudaStream_t st) {
+    switch (a.gs) {
+        case 32: return launch_pf4<T, BITS, D, 32>(a, st);
+        case 64: return launch_pf4<T, BITS, D, 64>(a, st);
+        case 128: return launch_pf4<T, BITS, D, 128>(a, st);
+    }
+    return set_error(QSDPA_ERR_INVALID, "group_size %d", a.gs);
+}
+
+template <typename T, int BITS>
+int launch_pf2(const DecodeArgs& a, cudaStream_t st) {
+    if (a.D == 128) return launch_pf3<T, BITS, 128>(a, st);
+    if (a.D == 256) return launch_pf3<T, BITS, 256>(a, st);
+    return set_error(QSDPA_ERR_UNSUPPORTED, "fused prefill: D=%d", a.D);
+}
+
 // 16-byte aligned base and (batch, head) strides; the stride of a size-1
 // dimension is never applied and does not count
 bool aligned16_tc(const void* p, int64_t sb, int64_t sh, int elt, int B, int H) {
@@ -1444,6 +1933,17 @@ bool tc_supported(const DecodeArgs& a) {
     if (a.kb && (!aligned16_tc(a.kb, a.kb_sb, a.kb_sh, 2, B, H) || !aligned16_tc(a.vb, a.vb_sb, a.vb_sh, 2, B, H)))
         return false;
     return true;
+}
+
+// The fused prefill supports what the tcgen05 decode supports (16-byte aligned
+// rows, D of 128 or 256) except 256-byte rows in bfloat16 (8-bit D=256).
+bool prefill_supported(const DecodeArgs& a, int dtype) {
+    return tc_supported(a) && !(a.D == 256 && a.bits == 8 && dtype != QSDPA_F16);
+}
+
+int launch_prefill_tc(const DecodeArgs& a, int dtype, cudaStream_t st) {
+    if (dtype == QSDPA_F16) return a.bits == 4 ? launch_pf2<__half, 4>(a, st) : launch_pf2<__half, 8>(a, st);
+    return a.bits == 4 ? launch_pf2<__nv_bfloat16, 4>(a, st) : launch_pf2<__nv_bfloat16, 8>(a, st);
 }
 
 int launch_decode_tc(const DecodeArgs& a, int dtype, cudaStream_t st) {

@@ -163,6 +163,9 @@ int launch_decode_simt(const DecodeArgs& a, int dtype, cudaStream_t s);
 int launch_decode_mma(const DecodeArgs& a, int dtype, cudaStream_t s);
 int launch_decode_tc(const DecodeArgs& a, int dtype, cudaStream_t s);
 bool tc_supported(const DecodeArgs& a);
+// Fused prefill (many queries per head) on tcgen05 (qsdpa_decode_tc.cu).
+int launch_prefill_tc(const DecodeArgs& a, int dtype, cudaStream_t s);
+bool prefill_supported(const DecodeArgs& a, int dtype);
 // Device-side fault bits of the tcgen05 kernel and of the sharded merge
 // (each file keeps its own word); reset clears them.
 int read_tc_status(int reset);

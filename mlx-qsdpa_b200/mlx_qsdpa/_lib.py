@@ -321,8 +321,10 @@ def decode(q: torch.Tensor, kp, vp, ks, vs, kb, vb, *, scale: float, bits: int, 
 
 
 def _plan_params(q, kp, vp, ks, vs, kb, vb, bits: int, group_size: int, splits: int, kernel: int) -> DecodeParams:
-    B, Hq, _, D = q.shape
+    B, Hq, qL, D = q.shape
     p = DecodeParams()
+    if qL > 1:
+        p.qL = qL  # q rows of a head contiguous: q_sh = qL * D
     p.q, p.q_sb, p.q_sh = q.data_ptr(), q.stride(0), q.stride(1)
     p.k_packed, p.kp_sb, p.kp_sh = kp.data_ptr(), kp.stride(0), kp.stride(1)
     p.v_packed, p.vp_sb, p.vp_sh = vp.data_ptr(), vp.stride(0), vp.stride(1)

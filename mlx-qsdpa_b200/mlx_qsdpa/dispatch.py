@@ -128,7 +128,7 @@ class _NotFusable(Exception):
     pass
 
 
-_MAX_FUSED_QL = 16  # queries per head the fused path takes (qsdpa_decode_params.qL)
+_MAX_FUSED_QL = 65536  # queries per head the fused path takes (qsdpa_decode_params.qL)
 
 
 def _causal_bool(qL: int, N: int, device) -> torch.Tensor:

@@ -63,16 +63,20 @@ def test_invalid_args_rejected_without_gpu(lib_path):
 
 
 def test_multi_query_arguments_checked_without_gpu(lib_path):
-    """qL > 1: at most 16 queries per head, only QSDPA_MASK_NONE / _CAUSAL,
-    each head's query rows contiguous (q_sh = qL * D); checked on the host."""
+    """qL > 1: at most 65,536 queries per head (more than 16: the fused
+    prefill), only QSDPA_MASK_NONE / _CAUSAL, each head's query rows
+    contiguous (q_sh = qL * D); checked on the host."""
     from mlx_qsdpa import _lib
     lib = _lib.load()
     p = _lib.DecodeParams()
     p.B, p.Hq, p.Hkv, p.N, p.D, p.bits, p.group_size = 1, 32, 2, 4096, 256, 4, 32
     p.q = p.k_packed = p.v_packed = p.k_scales = p.v_scales = p.out = 1
-    p.qL, p.q_sh = 17, 17 * 256
+    p.qL, p.q_sh = 65537, 65537 * 256
     assert lib.qsdpa_decode(ctypes.byref(p), None) == -1
     assert b"qL" in lib.qsdpa_last_error()
+    p.qL, p.q_sh = 17, 17 * 256  # the fused prefill needs 16-byte aligned rows
+    assert lib.qsdpa_decode(ctypes.byref(p), None) == -2
+    assert b"prefill" in lib.qsdpa_last_error()
     p.qL, p.q_sh = 4, 256  # rows of a head not contiguous
     assert lib.qsdpa_decode(ctypes.byref(p), None) == -1
     assert b"contiguous" in lib.qsdpa_last_error()
