@@ -22,7 +22,8 @@ CPU baseline (C restatement of the reference's dequantise + SDPA branch), the
 SM clocks sampled during the timed region, a correctness check of the timed
 path, and (N=1) the other configurations: the GQA-16 context sweep 1K-128K,
 the non-GQA 8-bit and symmetric 4-bit decode, continuous batching with the
-linear and rotating batch caches, and the CPU-runnable 8K cache_sdpa case.
+linear and rotating batch caches, the CPU-runnable 8K cache_sdpa case, and
+the fused prefill against dequantise + SDPA.
 """
 
 from __future__ import annotations
@@ -298,6 +299,8 @@ def extras(torch, peak):
     res["config4_decode"] = bm.config4_decode("auto", peak, emit=False)
     res["config4_steps"] = bm.config4(peak=peak, emit=False)
     torch.cuda.empty_cache()
+    # the fused prefill (qL > 16) against dequantise + SDPA, three points
+    res["prefill"] = bm.prefill(emit=False, points=[(0, 32768, 64), (0, 32768, 1024), (1, 32768, 256)])
     # configuration 1: the 8K cache_sdpa case, on the GPU and with the CPU port
     dev = torch.device("cuda")
     g = torch.Generator(device=dev)

@@ -143,12 +143,16 @@ typedef struct qsdpa_decode_params {
     int32_t out_mode;   /* QSDPA_OUT_* */
     int32_t kernel;     /* QSDPA_KERNEL_*; a kernel that cannot run the call
                          * is an error (QSDPA_ERR_UNSUPPORTED), not a fallback */
-    /* queries per head (0 or 1: decode).  qL > 1 (at most 16; e.g. the draft
-     * tokens of speculative decoding): q is (B, H_q, qL, D) with each head's
-     * qL rows contiguous (stride D, q_sh = qL * D), out is (B, H_q, qL, D)
-     * contiguous and part_o / part_ml have B * H_q * qL rows; mask_kind must
-     * be QSDPA_MASK_NONE or QSDPA_MASK_CAUSAL, and a causal call runs on the
-     * tcgen05 kernel only */
+    /* queries per head (0 or 1: decode).  qL > 1 (at most 65536): q is
+     * (B, H_q, qL, D) with each head's qL rows contiguous (stride D,
+     * q_sh = qL * D), out is (B, H_q, qL, D) contiguous and part_o / part_ml
+     * have B * H_q * qL rows; mask_kind must be QSDPA_MASK_NONE or
+     * QSDPA_MASK_CAUSAL.  Up to 16 (e.g. the draft tokens of speculative
+     * decoding) every query position is a head row of the decode kernels (a
+     * causal call on the tcgen05 kernel only); more (a prompt chunk) run on
+     * the tcgen05 fused prefill, which takes no per-row key window
+     * (kv_start / kv_len) and no 8-bit D=256 in bfloat16
+     * (QSDPA_ERR_UNSUPPORTED: the caller dequantises instead) */
     int32_t qL;
 } qsdpa_decode_params;
 

@@ -4,6 +4,7 @@ reference's mlx_qsdpa/bench.py:84-97 sweep and mlx_qsdpa/bench_comparison.py).
     python -m mlx_qsdpa.benchmarks --config 2 [--kernel auto|tcgen05|mma|simt]
     python -m mlx_qsdpa.benchmarks --config 3 [--kernel ...]
     python -m mlx_qsdpa.benchmarks --config 4
+    python -m mlx_qsdpa.benchmarks --config prefill
 
 Config 2: fused GQA-16 decode, B=1, H_q=32, H_kv=2, D=256, 4-bit gs32 with
 biases, fp16, K/V ~N(0,1); context sweep N = 1K, 4K, 16K, 32K, 64K, 128K.
@@ -229,15 +230,75 @@ def config4(steps=64, seed=0, peak=None, emit=True):
     return lines
 
 
+def prefill(seed=0, emit=True, points=None):
+    """Fused prefill (qL > 16 queries per head, causal) against the dequantise
+    + SDPA route the reference takes for such calls (dispatch.py:68-83): a
+    GQA-16 D=256 4-bit fp16 cache and a non-GQA D=128 8-bit bf16 cache, 4K
+    and 32K keys, 17-1,024 queries per head; each call timed alone with CUDA
+    events (3 warm-up, 10 timed).  ``points``: (cache index, N, qL) to run
+    instead of the whole sweep.  Returns the lines (printed when ``emit``)."""
+    from .dispatch import dequant_sdpa
+    lines = []
+    dev = torch.device("cuda")
+
+    def timeit(fn, reps=10):
+        for _ in range(3):
+            fn()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(reps):
+            fn()
+        e1.record()
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) * 1e3 / reps
+
+    caches = ((32, 2, 256, 4, 32, torch.float16), (8, 8, 128, 8, 64, torch.bfloat16))
+    for ci, (Hq, Hkv, D, bits, gs, dt) in enumerate(caches):
+        for N in (4096, 32768):
+            if points is not None and not any(p[0] == ci and p[1] == N for p in points):
+                continue
+            gen = torch.Generator(device=dev)
+            gen.manual_seed(seed)
+            k = _quantized(1, Hkv, N, D, bits, gs, dt, 1.0, False, gen, dev)
+            v = _quantized(1, Hkv, N, D, bits, gs, dt, 1.0, False, gen, dev)
+            for qL in (17, 64, 256, 1024):
+                if points is not None and (ci, N, qL) not in points:
+                    continue
+                q = torch.randn((1, Hq, qL, D), generator=gen, device=dev).to(dt)
+
+                def fused():
+                    return _lib.decode(q, k[0], v[0], k[1], v[1], k[2], v[2], scale=D ** -0.5, bits=bits,
+                                       group_size=gs, mask_kind=_lib.MASK_CAUSAL)
+
+                def fallback():
+                    return dequant_sdpa(q, k[0], v[0], k[1], v[1], k[2], v[2], D ** -0.5, "causal", bits, gs)
+
+                diff = (fused().float() - fallback().float()).abs().max().item()
+                tf, tb = timeit(fused), timeit(fallback)
+                line = {"prefill": True, "Hq": Hq, "Hkv": Hkv, "D": D, "bits": bits,
+                        "dtype": str(dt).replace("torch.", ""), "N": N, "qL": qL,
+                        "fused_us": round(tf, 1), "fallback_us": round(tb, 1), "speedup": round(tb / tf, 2),
+                        "fused_tflops": round(4 * Hq * qL * N * D / tf / 1e6, 1), "max_abs_diff": diff}
+                lines.append(line)
+                if emit:
+                    print(json.dumps(line), flush=True)
+            del k, v
+            torch.cuda.empty_cache()
+    return lines
+
+
 def main(argv=None):
-    ap = argparse.ArgumentParser(description="decode benchmarks of configurations 2-4")
-    ap.add_argument("--config", type=int, choices=[2, 3, 4], required=True)
+    ap = argparse.ArgumentParser(description="decode benchmarks of configurations 2-4, and the fused prefill")
+    ap.add_argument("--config", choices=["2", "3", "4", "prefill"], required=True)
     ap.add_argument("--kernel", choices=list(KERNELS), default="auto")
     ap.add_argument("--peak-gbs", type=float, default=None, help="HBM peak for frac_of_peak")
     args = ap.parse_args(argv)
-    if args.config == 2:
+    if args.config == "prefill":
+        prefill()
+    elif args.config == "2":
         config2(args.kernel, args.peak_gbs)
-    elif args.config == 3:
+    elif args.config == "3":
         config3(args.kernel, args.peak_gbs)
     else:
         config4_decode(args.kernel, args.peak_gbs)
