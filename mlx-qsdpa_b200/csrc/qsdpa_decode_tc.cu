@@ -142,6 +142,13 @@ constexpr bool kTcPdl = QSDPA_TC_PDL != 0;
 #ifndef QSDPA_TC_VHALF
 #define QSDPA_TC_VHALF 0
 #endif
+// ring stages at most (short rows fit more of them in the shared memory the
+// V^T operands leave: D=128 4-bit stages are 17-18 KB)
+#ifndef QSDPA_TC_MAX_STAGES
+#define QSDPA_TC_MAX_STAGES 8
+#endif
+constexpr int kTcMaxStages = QSDPA_TC_MAX_STAGES;
+static_assert(kTcMaxStages >= 2 && kTcMaxStages <= 8, "barrier block holds 8 full / empty pairs");
 
 template <int BITS, int D, int GS, bool SPLITP>
 struct TcCfg {
@@ -176,7 +183,7 @@ struct TcCfg {
     static constexpr int VBUFS = VHALF ? 2 : (fits(PBUFS, 2) ? 2 : 1);
     static constexpr int FIXED = BASE + PBUFS * P_BUF;
     static constexpr int STAGES_FIT = (kSmemLimit - FIXED - VBUFS * V_BYTES) / STAGE_BYTES;
-    static constexpr int STAGES = STAGES_FIT > 4 ? 4 : STAGES_FIT;
+    static constexpr int STAGES = STAGES_FIT > kTcMaxStages ? kTcMaxStages : STAGES_FIT;
     // at least 116 KB so no second CTA shares the SM (and its tensor memory)
     static constexpr int SMEM_RAW = FIXED + VBUFS * V_BYTES + STAGES * STAGE_BYTES;
     static constexpr int SMEM = SMEM_RAW > 116 * 1024 ? SMEM_RAW : 116 * 1024;
@@ -512,19 +519,19 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     // mbarriers (8 bytes each)
     const uint32_t mb0 = smem_u32(misc);
     auto full_bar = [&](int s) { return mb0 + 8u * s; };                // count 32 (producer lanes)
-    auto empty_bar = [&](int s) { return mb0 + 8u * (4 + s); };         // count 8 (consumer warps)
-    auto kready_bar = [&](int k) { return mb0 + 8u * (8 + k); };        // count 4 (key warps)
-    auto sready_bar = [&](int k) { return mb0 + 8u * (10 + k); };       // count 1 (commit)
-    auto pready_bar = [&](int k) { return mb0 + 8u * (12 + k); };       // count 4 (softmax warps)
-    auto pfree_bar = [&](int k) { return mb0 + 8u * (14 + k); };        // count 1 (commit)
-    auto vready_bar = [&](int v) { return mb0 + 8u * (16 + v); };       // count 4 (value warps)
-    auto vfree_bar = [&](int v) { return mb0 + 8u * (18 + v); };        // count 1 (commit)
-    auto sfree_bar = [&](int k) { return mb0 + 8u * (20 + k); };        // count 4 (softmax warps read S)
-    const uint32_t qready_bar = mb0 + 8u * 22;                          // count 4 (softmax warps staged Q)
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(misc + 184);
-    int* flags = reinterpret_cast<int*>(misc + 192);    // [4]
-    float* red = reinterpret_cast<float*>(misc + 256);  // [4][16]
-    float* mfin = reinterpret_cast<float*>(misc + 512);  // [16] final running maxima
+    auto empty_bar = [&](int s) { return mb0 + 8u * (8 + s); };         // count 8 (consumer warps)
+    auto kready_bar = [&](int k) { return mb0 + 8u * (16 + k); };       // count 4 (key warps)
+    auto sready_bar = [&](int k) { return mb0 + 8u * (18 + k); };       // count 1 (commit)
+    auto pready_bar = [&](int k) { return mb0 + 8u * (20 + k); };       // count 4 (softmax warps)
+    auto pfree_bar = [&](int k) { return mb0 + 8u * (22 + k); };        // count 1 (commit)
+    auto vready_bar = [&](int v) { return mb0 + 8u * (24 + v); };       // count 4 (value warps)
+    auto vfree_bar = [&](int v) { return mb0 + 8u * (26 + v); };        // count 1 (commit)
+    auto sfree_bar = [&](int k) { return mb0 + 8u * (28 + k); };        // count 4 (softmax warps read S)
+    const uint32_t qready_bar = mb0 + 8u * 30;                          // count 4 (softmax warps staged Q)
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(misc + 256);
+    int* flags = reinterpret_cast<int*>(misc + 264);    // [4]
+    float* red = reinterpret_cast<float*>(misc + 320);  // [4][16]
+    float* mfin = reinterpret_cast<float*>(misc + 576);  // [16] final running maxima
     const uint32_t sV_u = smem_u32(sV), sQ_u = smem_u32(sQ), sP_u = smem_u32(sP);
 
     const int split = blockIdx.x;
