@@ -238,6 +238,24 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float v[16]) {
 #pragma unroll
     for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
 }
+__device__ __forceinline__ void tmem_ld4(uint32_t taddr, float v[4]) {
+    uint32_t r[4];
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x4.b32 {%0,%1,%2,%3}, [%4];\n"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"(taddr)
+                 : "memory");
+#pragma unroll
+    for (int i = 0; i < 4; ++i) v[i] = __uint_as_float(r[i]);
+}
+// N = 4 or 16 consecutive columns of the thread's lane
+template <int N>
+__device__ __forceinline__ void tmem_ld_cols(uint32_t taddr, float v[N]) {
+    static_assert(N == 4 || N == 16, "4 or 16 columns");
+    if constexpr (N == 16)
+        tmem_ld16(taddr, v);
+    else
+        tmem_ld4(taddr, v);
+}
 __device__ __forceinline__ void tmem_st16(uint32_t taddr, const float v[16]) {
     asm volatile(
         "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};\n" ::"r"(
@@ -529,7 +547,6 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     auto sfree_bar = [&](int k) { return mb0 + 8u * (28 + k); };        // count 4 (softmax warps read S)
     const uint32_t qready_bar = mb0 + 8u * 30;                          // count 4 (softmax warps staged Q)
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(misc + 256);
-    int* flags = reinterpret_cast<int*>(misc + 264);    // [4]
     float* red = reinterpret_cast<float*>(misc + 320);  // [4][16]
     float* mfin = reinterpret_cast<float*>(misc + 576);  // [16] final running maxima
     const uint32_t sV_u = smem_u32(sV), sQ_u = smem_u32(sQ), sP_u = smem_u32(sP);
@@ -895,140 +912,147 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         const uint32_t lane_off = (uint32_t)(qw * 32) << 16;
         const int64_t mrow = a.mask ? (int64_t)b * a.m_sb : 0;
         const int hq0 = kvh * a.gqa + h0;
-        int js = 0;
-        for (int i = advance(0); i < ntiles; i = advance(i + 1), ++js) {
-            mbar_wait(sready_bar(js & 1), (js >> 1) & 1, dead);
-            if (warp == kSmWarp0) TC_TRACE(kEvSmGo, js);
-            tc_fence_after();
-            float s[kTcHeads];
-            tmem_ld16(tbase + lane_off + kTmemS + 16 * (js & 1), s);
-            tmem_wait_ld();
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(sfree_bar(js & 1));  // S buffer js & 1 is read
-            if (js >= PB) {  // P^T buffer js % PB was read by the P V MMA of tile js - PB
-                mbar_wait(pfree_bar(js % PB), ((js - PB) / PB) & 1, dead);
+        // the tile loop, compiled for NHA = 4 and 16 active heads of the 16-head
+        // block: GQA groups of up to 4 heads (one head per KV head, GQA-4) skip
+        // the padded heads' exponentials, sums and maxima; their P^T entries
+        // are written as zeros (the O^T columns of padded heads are not read)
+        auto tile_loop = [&](auto nha_c) -> int {
+            constexpr int NHA = decltype(nha_c)::value;
+            int js = 0;
+            for (int i = advance(0); i < ntiles; i = advance(i + 1), ++js) {
+                mbar_wait(sready_bar(js & 1), (js >> 1) & 1, dead);
+                if (warp == kSmWarp0) TC_TRACE(kEvSmGo, js);
                 tc_fence_after();
-            }
-
-            // ---------------- online softmax for token p0 + t ----------------
-            // log2-domain scores; m_run starts at kNoMax (finite), so s - m_run
-            // is never NaN: +huge for a first finite score, -inf for a masked key
-            const int p0 = p_lo + i * kTcTile;
-            const int tok = p0 + t;
-#pragma unroll
-            for (int h = 0; h < kTcHeads; ++h) s[h] *= a.scale_log2;
-            bool valid = true;
-            if (!(win.full && p0 + kTcTile <= p_hi)) {  // a tile cut by the chunk end or the window
-                valid = tok < p_hi && win.contains(tok);
-                if (!valid) {
-#pragma unroll
-                    for (int h = 0; h < kTcHeads; ++h) s[h] = -INFINITY;
-                }
-            }
-            if (a.mask && valid) {
-#pragma unroll
-                for (int h = 0; h < kTcHeads; ++h)
-                    if (h < nh) s[h] += mask_offset(a.mask, a.mask_kind, mrow + (int64_t)(hq0 + h) * a.m_sh + tok);
-            }
-            if (CAUSAL && valid) {
-                // qL > 1, causal: head row h0 + h is query position (h0 + h) % qL,
-                // which sees the window's keys up to logical position len - qL + position
-                int rel = tok - win.start;
-                if (rel < 0) rel += a.N;
-                const int lim0 = win.len - a.causal_qL;
-#pragma unroll
-                for (int h = 0; h < kTcHeads; ++h)
-                    if (rel > lim0 + (h0 + h) % a.causal_qL) s[h] = -INFINITY;
-            }
-            // p[h] holds the exponent s - m_run until the 2^ below
-            float p[kTcHeads];
-            float dmax = -INFINITY;
-#pragma unroll
-            for (int h = 0; h < kTcHeads; ++h) {
-                p[h] = s[h] - m_run[h];
-                dmax = fmaxf(dmax, p[h]);
-            }
-            const bool wup = __any_sync(0xffffffffu, dmax > kRescaleTc);
-            if (lane == 0) flags[qw] = wup ? 1 : 0;
-            named_barrier(1, kSmWarps * 32);
-            const bool tile_up = (flags[0] | flags[1] | flags[2] | flags[3]) != 0;
-            named_barrier(1, kSmWarps * 32);  // flags read before the next tile's writes
-            if (tile_up) {
-                // a score rose past the running maximum: tile maxima per head
-                float mx[kTcHeads];
-#pragma unroll
-                for (int h = 0; h < kTcHeads; ++h) {
-                    float v = s[h];
-#pragma unroll
-                    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
-                    mx[h] = v;
-                }
-                if (lane == 0) {
-#pragma unroll
-                    for (int h = 0; h < kTcHeads; ++h) red[qw * kTcHeads + h] = mx[h];
-                }
-                named_barrier(1, kSmWarps * 32);
-                float alpha[kTcHeads];
-#pragma unroll
-                for (int h = 0; h < kTcHeads; ++h) {
-                    const float v = fmaxf(fmaxf(red[h], red[16 + h]), fmaxf(red[32 + h], red[48 + h]));
-                    const bool u = v > m_run[h] + kRescaleTc;
-                    alpha[h] = u ? ex2(m_run[h] - v) : 1.f;
-                    if (u) m_run[h] = v;
-                    l_run[h] *= alpha[h];
-                    p[h] = s[h] - m_run[h];
-                }
-                named_barrier(1, kSmWarps * 32);  // red read before it is written again
-                if (js > 0) {
-                    // O^T must hold the P V product of tile js - 1 before it is scaled
-                    mbar_wait(pfree_bar((js - 1) % PB), ((js - 1) / PB) & 1, dead);
+                float s[NHA];
+                tmem_ld_cols<NHA>(tbase + lane_off + kTmemS + 16 * (js & 1), s);
+                tmem_wait_ld();
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(sfree_bar(js & 1));  // S buffer js & 1 is read
+                if (js >= PB) {  // P^T buffer js % PB was read by the P V MMA of tile js - PB
+                    mbar_wait(pfree_bar(js % PB), ((js - PB) / PB) & 1, dead);
                     tc_fence_after();
-                    // O^T lane t holds head dims t (+128): scale column h by alpha[h]
-#pragma unroll
-                    for (int mb = 0; mb < C::MB; ++mb) {
-                        float o[kTcHeads];
-                        tmem_ld16(tbase + lane_off + kTmemO + mb * 16, o);
-                        tmem_wait_ld();
-#pragma unroll
-                        for (int h = 0; h < kTcHeads; ++h) o[h] *= alpha[h];
-                        tmem_st16(tbase + lane_off + kTmemO + mb * 16, o);
+                }
+
+                // ---------------- online softmax for token p0 + t ----------------
+                // log2-domain scores; m_run starts at kNoMax (finite), so s - m_run
+                // is never NaN: +huge for a first finite score, -inf for a masked key
+                const int p0 = p_lo + i * kTcTile;
+                const int tok = p0 + t;
+    #pragma unroll
+                for (int h = 0; h < NHA; ++h) s[h] *= a.scale_log2;
+                bool valid = true;
+                if (!(win.full && p0 + kTcTile <= p_hi)) {  // a tile cut by the chunk end or the window
+                    valid = tok < p_hi && win.contains(tok);
+                    if (!valid) {
+    #pragma unroll
+                        for (int h = 0; h < NHA; ++h) s[h] = -INFINITY;
                     }
-                    tmem_wait_st();
                 }
-            }
-#pragma unroll
-            for (int h = 0; h < kTcHeads; ++h) {
-                p[h] = ex2(p[h]);
-                l_run[h] += p[h];
-            }
-            // row t of P^T: 32 bytes, halves swapped on rows 4-7 of each 8 (32-byte swizzle)
-            uint32_t hi[8];
-#pragma unroll
-            for (int e = 0; e < 8; ++e) hi[e] = Ops<T>::pack(p[2 * e], p[2 * e + 1]);
-            char* prow = sP + (js % PB) * C::P_BUF + t * 32;
-            const int sw = ((t >> 2) & 1) * 16;
-            *reinterpret_cast<uint4*>(prow + sw) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
-            *reinterpret_cast<uint4*>(prow + (16 ^ sw)) = make_uint4(hi[4], hi[5], hi[6], hi[7]);
-            if constexpr (Ops<T>::kSplitP) {
-                uint32_t lo[8];
-#pragma unroll
-                for (int e = 0; e < 8; ++e) {
-                    const float r0 = p[2 * e] - __uint_as_float(hi[e] << 16);
-                    const float r1 = p[2 * e + 1] - __uint_as_float(hi[e] & 0xffff0000u);
-                    lo[e] = Ops<T>::pack(r0, r1);
+                if (a.mask && valid) {
+    #pragma unroll
+                    for (int h = 0; h < NHA; ++h)
+                        if (h < nh) s[h] += mask_offset(a.mask, a.mask_kind, mrow + (int64_t)(hq0 + h) * a.m_sh + tok);
                 }
-                char* lrow = prow + C::P_BYTES;
-                *reinterpret_cast<uint4*>(lrow + sw) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
-                *reinterpret_cast<uint4*>(lrow + (16 ^ sw)) = make_uint4(lo[4], lo[5], lo[6], lo[7]);
+                if (CAUSAL && valid) {
+                    // qL > 1, causal: head row h0 + h is query position (h0 + h) % qL,
+                    // which sees the window's keys up to logical position len - qL + position
+                    int rel = tok - win.start;
+                    if (rel < 0) rel += a.N;
+                    const int lim0 = win.len - a.causal_qL;
+    #pragma unroll
+                    for (int h = 0; h < NHA; ++h)
+                        if (rel > lim0 + (h0 + h) % a.causal_qL) s[h] = -INFINITY;
+                }
+                // p[h] holds the exponent s - m_run until the 2^ below
+                float p[NHA];
+                float dmax = -INFINITY;
+    #pragma unroll
+                for (int h = 0; h < NHA; ++h) {
+                    p[h] = s[h] - m_run[h];
+                    dmax = fmaxf(dmax, p[h]);
+                }
+                // did any score of the tile (any softmax thread) rise past its running maximum?
+                const bool tile_up = named_barrier_or(1, kSmWarps * 32, dmax > kRescaleTc);
+                if (tile_up) {
+                    // a score rose past the running maximum: tile maxima per head
+                    float mx[NHA];
+    #pragma unroll
+                    for (int h = 0; h < NHA; ++h) {
+                        float v = s[h];
+    #pragma unroll
+                        for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+                        mx[h] = v;
+                    }
+                    if (lane == 0) {
+    #pragma unroll
+                        for (int h = 0; h < NHA; ++h) red[qw * kTcHeads + h] = mx[h];
+                    }
+                    named_barrier(1, kSmWarps * 32);
+                    float alpha[NHA];
+    #pragma unroll
+                    for (int h = 0; h < NHA; ++h) {
+                        const float v = fmaxf(fmaxf(red[h], red[16 + h]), fmaxf(red[32 + h], red[48 + h]));
+                        const bool u = v > m_run[h] + kRescaleTc;
+                        alpha[h] = u ? ex2(m_run[h] - v) : 1.f;
+                        if (u) m_run[h] = v;
+                        l_run[h] *= alpha[h];
+                        p[h] = s[h] - m_run[h];
+                    }
+                    named_barrier(1, kSmWarps * 32);  // red read before it is written again
+                    if (js > 0) {
+                        // O^T must hold the P V product of tile js - 1 before it is scaled
+                        mbar_wait(pfree_bar((js - 1) % PB), ((js - 1) / PB) & 1, dead);
+                        tc_fence_after();
+                        // O^T lane t holds head dims t (+128): scale column h by alpha[h]
+    #pragma unroll
+                        for (int mb = 0; mb < C::MB; ++mb) {
+                            float o[kTcHeads];
+                            tmem_ld16(tbase + lane_off + kTmemO + mb * 16, o);
+                            tmem_wait_ld();
+    #pragma unroll
+                            for (int h = 0; h < NHA; ++h) o[h] *= alpha[h];
+                            tmem_st16(tbase + lane_off + kTmemO + mb * 16, o);
+                        }
+                        tmem_wait_st();
+                    }
+                }
+    #pragma unroll
+                for (int h = 0; h < NHA; ++h) {
+                    p[h] = ex2(p[h]);
+                    l_run[h] += p[h];
+                }
+                // row t of P^T: 32 bytes, halves swapped on rows 4-7 of each 8 (32-byte swizzle)
+                uint32_t hi[8];
+    #pragma unroll
+                for (int e = 0; e < 8; ++e)
+                    hi[e] = 2 * e < NHA ? Ops<T>::pack(p[min(2 * e, NHA - 2)], p[min(2 * e + 1, NHA - 1)]) : 0u;
+                char* prow = sP + (js % PB) * C::P_BUF + t * 32;
+                const int sw = ((t >> 2) & 1) * 16;
+                *reinterpret_cast<uint4*>(prow + sw) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+                *reinterpret_cast<uint4*>(prow + (16 ^ sw)) = make_uint4(hi[4], hi[5], hi[6], hi[7]);
+                if constexpr (Ops<T>::kSplitP) {
+                    uint32_t lo[8];
+    #pragma unroll
+                    for (int e = 0; e < 8; ++e) {
+                        const float r0 = p[min(2 * e, NHA - 2)] - __uint_as_float(hi[e] << 16);
+                        const float r1 = p[min(2 * e + 1, NHA - 1)] - __uint_as_float(hi[e] & 0xffff0000u);
+                        lo[e] = 2 * e < NHA ? Ops<T>::pack(r0, r1) : 0u;
+                    }
+                    char* lrow = prow + C::P_BYTES;
+                    *reinterpret_cast<uint4*>(lrow + sw) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+                    *reinterpret_cast<uint4*>(lrow + (16 ^ sw)) = make_uint4(lo[4], lo[5], lo[6], lo[7]);
+                }
+                fence_proxy_async();
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(pready_bar(js % PB));
+                if (warp == kSmWarp0) TC_TRACE(kEvSmEnd, js);
             }
-            fence_proxy_async();
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(pready_bar(js % PB));
-            if (warp == kSmWarp0) TC_TRACE(kEvSmEnd, js);
-        }
-        n_active = js;
+            return js;
+        };
+        n_active = nh <= 4 ? tile_loop(std::integral_constant<int, 4>{})
+                           : tile_loop(std::integral_constant<int, kTcHeads>{});
         if (n_active > 0) {  // the last P V product
             mbar_wait(pfree_bar((n_active - 1) % PB), ((n_active - 1) / PB) & 1, dead);
             tc_fence_after();

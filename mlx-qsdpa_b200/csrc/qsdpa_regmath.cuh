@@ -29,6 +29,18 @@ __device__ __forceinline__ void named_barrier(int id, int count) {
     asm volatile("bar.sync %0, %1;\n" ::"r"(id), "r"(count) : "memory");
 }
 
+// named barrier that also returns the OR of every participating thread's
+// predicate (one barrier instead of flags in shared memory and two barriers)
+__device__ __forceinline__ bool named_barrier_or(int id, int count, bool pred) {
+    uint32_t r;
+    asm volatile(
+        "{\n .reg .pred p, q;\n setp.ne.u32 q, %1, 0;\n bar.red.or.pred p, %2, %3, q;\n selp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(r)
+        : "r"((uint32_t)pred), "r"(id), "r"(count)
+        : "memory");
+    return r != 0;
+}
+
 // 2^x on the MUFU unit (flushes results below 2^-126 to zero, which only
 // touches probabilities far below the fp16/bf16 resolution of P)
 __device__ __forceinline__ float ex2(float x) {
