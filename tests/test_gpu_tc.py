@@ -208,6 +208,35 @@ def test_small_gqa_groups(lib, shape, bits, gs):
     check(lib, c, kernel=lib.KERNEL_MMA, cap=cap)
 
 
+@pytest.mark.parametrize("gqa", [1, 2, 4])
+def test_small_groups_masks_windows_rescale(lib, gqa):
+    """Blocks of up to 4 active heads (the softmax loop compiled for 4 heads):
+    masks, key windows, the lazy rescale and causal query rows there too."""
+    from qsdpa_testlib import normal, to_torch
+    Hkv = 2
+    c = Case(2, gqa * Hkv, Hkv, 900, 128, seed=300 + gqa)
+    rng = np.random.default_rng(gqa)
+    m = rng.random((2, gqa * Hkv, 1, 900)) < 0.6
+    check(lib, c, mask_np=m, mask=torch.from_numpy(m).cuda(), mask_kind=lib.MASK_BOOL)
+    start, length = [5, 400], [850, 300]
+    w = np.zeros((2, 1, 1, 900), bool)
+    for b in range(2):
+        w[b, 0, 0, (start[b] + np.arange(length[b])) % 900] = True
+    check(lib, c, mask_np=w, kv=(start, length), splits=1)
+    r = Case(1, gqa * Hkv, Hkv, 2000, 256, kv_std=16.0, seed=310 + gqa)
+    check(lib, r, splits=1)
+    check(lib, r)
+    qL = max(1, 4 // gqa)  # gqa * qL head rows: at most 4
+    q = Case(1, gqa * Hkv, Hkv, 1500, 256, seed=320 + gqa)
+    qn = normal(np.random.default_rng(qL * 7 + gqa), (1, gqa * Hkv, qL, 256), q.dtype)
+    ref = O.sdpa(qn, q.k, q.v, mask="causal", dtype=q.dtype)
+    _, pk, pv, ks, vs, kb, vb = q.torch_args()
+    out = lib.decode(to_torch(qn, q.dtype), pk, pv, ks, vs, kb, vb, scale=256 ** -0.5, bits=4, group_size=32,
+                     kernel=lib.KERNEL_TCGEN05, mask_kind=lib.MASK_CAUSAL)
+    torch.cuda.synchronize()
+    assert_close(from_torch(out), ref, what=f"gqa={gqa} qL={qL} causal")
+
+
 @pytest.mark.parametrize("qL,causal,N", [(4, True, 3000), (2, True, 129), (8, True, 700), (16, True, 1000),
                                          (4, False, 2000), (3, True, 2500)])
 @pytest.mark.parametrize("splits", [0, 1])
