@@ -36,12 +36,17 @@ constexpr int kMmaMaxChunk = 4096;
 // at 16K, 35.0 vs 39.3 at 128K)
 constexpr int kAutoTcMinKeys = 16384;
 constexpr int kAutoTcMinGqa = 8;
-// smaller GQA groups (e.g. one head per KV head, D=128, 8-bit, 8 KV heads):
-// tcgen05 with one CTA per SM from this many keys (measured at 16K / 32K /
-// 64K / 128K keys: 17.8 vs 18.5, 26.8 vs 31.0, 46.3 vs 55.7, 83.4 vs 101.7 us;
-// symmetric 4-bit gs128 15.7 vs 14.4, 23.2 vs 23.5, 38.0 vs 40.5, 68.1 vs
-// 74.4); more units than SMs (32 rows x 8 KV heads) stay on mma.sync
-constexpr int kAutoTcMinKeysSmall = 32768;
+// smaller GQA groups (e.g. one head per KV head, D=128, 8 KV heads): tcgen05
+// from this many bytes of packed codes per KV head (measured, tcgen05 vs
+// mma.sync, at 16K / 32K / 64K / 128K keys: 8-bit gs64 16.3 vs 18.6, 25.4 vs
+// 31.1, 43.9 vs 55.4, 78.6 vs 101.9 us; symmetric 4-bit gs128 15.2 vs 14.5,
+// 21.4 vs 23.5, 35.5 vs 40.3, 63.1 vs 74.8)
+constexpr int64_t kAutoTcMinBytesSmall = 3 << 19;  // 1.5 MiB
+// tcgen05 with more 16-head units than SMs: chunks of about this many keys,
+// so the ragged waves of short rows balance (32 rows x 8 KV heads, GQA-4,
+// D=128, 3.5K-32K keys per row: 1 / 2 / 3 / 4 / 6 / 8 splits 434 / 366 / 350 /
+// 339 / 343 / 349 us, mma.sync 366 us)
+constexpr int kTcManyUnitsChunk = 8192;
 }  // namespace
 
 int set_error(int code, const char* fmt, ...) {
@@ -243,12 +248,10 @@ int make_plan(const qsdpa_decode_params* p, const DecodeArgs& a, Plan& pl) {
             break;
         default: {
             // groups of fewer heads (padded to 16 on both tensor-core kernels)
-            // go to tcgen05 only when its one-wave plan covers them: at most one
-            // 16-head block per SM
-            const int tc_units = a.B * a.Hkv * ((a.gqa + 15) / 16);
-            const bool tc_auto =
-                a.causal_qL || (p->N >= kAutoTcMinKeys && a.gqa >= kAutoTcMinGqa) ||
-                (p->N >= kAutoTcMinKeysSmall && tc_units <= sm_count());
+            // go to tcgen05 once a KV head holds kAutoTcMinBytesSmall of codes
+            const int64_t code_bytes = (int64_t)p->N * a.D * a.bits / 8;
+            const bool tc_auto = a.causal_qL || (p->N >= kAutoTcMinKeys && a.gqa >= kAutoTcMinGqa) ||
+                                 (a.gqa < kAutoTcMinGqa && code_bytes >= kAutoTcMinBytesSmall);
             pl.kern = tc_ok && tc_auto ? Kern::Tc : mma_ok ? Kern::Mma : Kern::Simt;
         }
     }
@@ -272,6 +275,8 @@ int make_plan(const qsdpa_decode_params* p, const DecodeArgs& a, Plan& pl) {
             // 148 CTAs 171.8 us, 256 CTAs 197.5 us, 294 CTAs 179.2 us), so the
             // split count rounds down (8 KV heads: 18 splits, 144 CTAs)
             splits = sm_count() / units;
+            // more units than SMs: several waves anyway, of ~kTcManyUnitsChunk-key chunks
+            if (units > sm_count()) splits = (p->N + kTcManyUnitsChunk - 1) / kTcManyUnitsChunk;
         } else if (pl.use_mma) {
             const int lo = (sm_count() + units - 1) / units, hi = (2 * sm_count() + units - 1) / units;
             const int by_long = (p->N + kLongChunk - 1) / kLongChunk;

@@ -75,14 +75,16 @@ def test_config2_131072_keys_automatic_splits(qs):
 
 
 @pytest.mark.slow
-@pytest.mark.parametrize("N,kernel", [(16384, "mma"), (65536, "tcgen05")])
-@pytest.mark.parametrize("variant", ["bf16_8bit_gs64", "bf16_sym_4bit_gs128"])
+@pytest.mark.parametrize("variant,N,kernel", [("bf16_8bit_gs64", 16384, "tcgen05"),
+                                               ("bf16_sym_4bit_gs128", 16384, "mma"),
+                                               ("bf16_8bit_gs64", 65536, "tcgen05"),
+                                               ("bf16_sym_4bit_gs128", 65536, "tcgen05")])
 def test_config3_keys(qs, variant, N, kernel):
     """Non-GQA configuration (H_q = H_kv = 8, D=128, bfloat16, K/V ~ N(0, 0.5)):
     affine 8-bit gs64, and the symmetric variant (affine codes, biases=None)
-    at 4-bit gs128.  The automatic choice takes the mma.sync kernel at 16,384
-    keys and the tcgen05 kernel (one CTA per SM, 18 splits of 8 KV heads) at
-    65,536."""
+    at 4-bit gs128.  The automatic choice takes the tcgen05 kernel (one CTA per
+    SM, 18 splits of 8 KV heads) from 1.5 MiB of codes per KV head (8-bit at
+    16,384 keys) and the mma.sync kernel below (4-bit at 16,384 keys)."""
     from mlx_qsdpa import _lib
     B, H, D = 1, 8, 128
     bits, gs, sym = (8, 64, False) if variant == "bf16_8bit_gs64" else (4, 128, True)

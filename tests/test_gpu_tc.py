@@ -223,7 +223,7 @@ def test_small_groups_masks_windows_rescale(lib, gqa):
     for b in range(2):
         w[b, 0, 0, (start[b] + np.arange(length[b])) % 900] = True
     check(lib, c, mask_np=w, kv=(start, length), splits=1)
-    r = Case(1, gqa * Hkv, Hkv, 2000, 256, kv_std=16.0, seed=310 + gqa)
+    r = Case(1, gqa * Hkv, Hkv, 2000, 256, kv_std=4.0, seed=310 + gqa)
     check(lib, r, splits=1)
     check(lib, r)
     qL = max(1, 4 // gqa)  # gqa * qL head rows: at most 4
