@@ -1463,9 +1463,11 @@ int launch_tc2(const DecodeArgs& a, cudaStream_t st) {
 //   S (128 rows x 64 keys)  = Q (128 x D) . K_tile^T          A, B K-major
 //   O (128 rows x D)       += P (128 x 64) . V_tile (64 x D)  A K-major, B MN-major
 // The softmax of a row is one thread's loop over its TMEM lane (lane = row):
-// no reduction across threads.  Roles (10 warps): four dequantising warps
-// (the key tile into the K operand, then the value tile into the V operand;
-// two threads per key, half of the head dims each), four softmax warps (stage
+// no reduction across threads.  Roles (14 warps): four warps dequantise the
+// key tile into the K operand and four others the value tile into the V
+// operand (two threads per key, half of the head dims each; the key warps of
+// tile j + 1 run while the value warps wait for the P V MMA of tile j - 1 to
+// free the V operand), four softmax warps (stage
 // Q, then per tile read S, online softmax, write P; at the end read O), a
 // producer warp (16-byte cp.async of packed rows, scales and biases into a
 // ring) and an MMA warp (TMEM owner, issues both products from one elected
@@ -1475,10 +1477,11 @@ int launch_tc2(const DecodeArgs& a, cudaStream_t st) {
 // words in the order 0,4,1,5,2,6,3,7 (put back at the output).
 constexpr int kPfRows = 128;    // query rows per CTA: M of both MMAs
 constexpr int kPfKeys = 64;     // keys per tile: N of the S MMA, K of the P V MMA
-constexpr int kPfSmWarp0 = 4;   // warps 0-3 dequantise, 4-7 run the softmax
+constexpr int kPfSmWarp0 = 4;   // warps 0-3 dequantise keys, 4-7 run the softmax
 constexpr int kPfProdWarp = 8;
 constexpr int kPfMmaWarp = 9;
-constexpr int kPfThreads = 10 * 32;
+constexpr int kPfVWarp0 = 10;   // warps 10-13 dequantise values
+constexpr int kPfThreads = 14 * 32;
 constexpr int kPfTmemS = 0;     // two S buffers of 64 columns
 constexpr int kPfTmemO = 128;   // O: D columns
 
@@ -1498,9 +1501,13 @@ struct PfCfg {
     static constexpr int OP_BYTES = kPfKeys * D * 2;       // K operand; V operand
     static constexpr int OP_LBO = kPfKeys * 128;           // between 64-dim blocks of an operand
     static constexpr int P_BYTES = kPfRows * kPfKeys * 2;  // one P operand (hi or lo)
-    static constexpr int P_ALL = (SPLITP ? 2 : 1) * P_BYTES;
+    static constexpr int P_ALL = (SPLITP ? 2 : 1) * P_BYTES;  // one P buffer (hi, lo)
     static constexpr int MISC_BYTES = 1024;
-    static constexpr int FIXED = 1024 + Q_BYTES + 2 * OP_BYTES + P_ALL + MISC_BYTES;
+    static constexpr int fixed(int pbufs) { return 1024 + Q_BYTES + 2 * OP_BYTES + pbufs * P_ALL + MISC_BYTES; }
+    // two P buffers (the softmax of tile j + 1 writes while the P V MMA of tile j
+    // reads) where two ring stages still fit
+    static constexpr int PBUFS = (kSmemLimit - fixed(2)) / STAGE_BYTES >= 2 ? 2 : 1;
+    static constexpr int FIXED = fixed(PBUFS);
     static constexpr int STAGES_FIT = (kSmemLimit - FIXED) / STAGE_BYTES;
     // 256-byte rows in bfloat16 leave room for one stage only: not supported
     static constexpr bool SUPPORTED = STAGES_FIT >= 2;
@@ -1545,18 +1552,21 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_tc_kernel(const DecodeA
     char* sK = sQ + C::Q_BYTES;         // K operand: 64-dim blocks of 64 key rows x 128 B
     char* sVo = sK + C::OP_BYTES;       // V operand: the same layout, read MN-major
     char* sP = sVo + C::OP_BYTES;       // P: 128 rows x 128 B (hi, then lo for bf16)
-    char* ring = sP + C::P_ALL;
+    char* ring = sP + C::PBUFS * C::P_ALL;
     char* misc = ring + ST * C::STAGE_BYTES;
     const uint32_t mb0 = smem_u32(misc);
     auto full_bar = [&](int s) { return mb0 + 8u * s; };            // count 32: producer lanes
-    auto empty_bar = [&](int s) { return mb0 + 8u * (4 + s); };     // count 4: dequantising warps
+    auto empty_bar = [&](int s) { return mb0 + 8u * (4 + s); };     // count 8: dequantising warps
     const uint32_t kready_bar = mb0 + 8u * 8;                       // count 4: K operand written
     const uint32_t vready_bar = mb0 + 8u * 9;                       // count 4: V operand written
     auto sready_bar = [&](int k) { return mb0 + 8u * (10 + k); };   // commit: S of a tile (K operand free)
     auto sfree_bar = [&](int k) { return mb0 + 8u * (12 + k); };    // count 4: softmax read S buffer k
-    const uint32_t pready_bar = mb0 + 8u * 14;                      // count 4: P written
+    // count 4: P buffer k written (one barrier per buffer: the softmax may write
+    // buffer (j + 1) % 2 before the P V of tile j has consumed its own)
+    auto pready_bar = [&](int k) { return mb0 + 8u * (k ? 19 : 14); };
     const uint32_t pvdone_bar = mb0 + 8u * 15;                      // commit: P V of a tile (V, P free)
     const uint32_t qready_bar = mb0 + 8u * 16;                      // count 4: Q staged
+    auto pfree_bar = [&](int k) { return mb0 + 8u * (17 + k); };    // commit: P buffer k read by its P V
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(misc + 192);
 
     const int split = blockIdx.x;
@@ -1624,7 +1634,7 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_tc_kernel(const DecodeA
 #pragma unroll
             for (int s = 0; s < ST; ++s) {
                 mbar_init(full_bar(s), 32);
-                mbar_init(empty_bar(s), 4);
+                mbar_init(empty_bar(s), 8);
             }
             mbar_init(kready_bar, 4);
             mbar_init(vready_bar, 4);
@@ -1632,9 +1642,12 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_tc_kernel(const DecodeA
             mbar_init(sready_bar(1), 1);
             mbar_init(sfree_bar(0), 4);
             mbar_init(sfree_bar(1), 4);
-            mbar_init(pready_bar, 4);
+            mbar_init(pready_bar(0), 4);
+            mbar_init(pready_bar(1), 4);
             mbar_init(pvdone_bar, 1);
             mbar_init(qready_bar, 4);
+            mbar_init(pfree_bar(0), 1);
+            mbar_init(pfree_bar(1), 1);
             asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
         }
         __syncwarp();
@@ -1664,12 +1677,13 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_tc_kernel(const DecodeA
         const uint64_t pdesc = smem_desc(smem_u32(sP), 16, 1024, kSw128);
         const uint64_t vdesc = smem_desc(smem_u32(sVo), C::OP_LBO, 1024, kSw128);
         mbar_wait(qready_bar, 0, dead);
-        for (int j = 0; j < ntiles && !dead; ++j) {
-            // S of tile j once its keys are in the K operand and the softmax
-            // warps have read S buffer j & 1 (tile j - 2)
+        // S of tile j once its keys are in the K operand and the softmax warps
+        // have read S buffer j & 1 (tile j - 2); issued a tile ahead of the P V
+        // product, so the softmax of tile j + 1 finds its scores ready
+        auto issue_s = [&](int j) {
             mbar_wait(kready_bar, j & 1, dead);
             if (j >= 2) mbar_wait(sfree_bar(j & 1), ((j - 2) >> 1) & 1, dead);
-            if (dead) break;
+            if (dead) return;
             tc_fence_after();
             if (elect_one()) {
 #pragma unroll
@@ -1681,27 +1695,36 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_tc_kernel(const DecodeA
                 mma_commit(sready_bar(j & 1));
             }
             __syncwarp();
-            // P V of tile j once P and the V operand are written
-            mbar_wait(pready_bar, j & 1, dead);
+        };
+        if (ntiles > 0) issue_s(0);
+        for (int j = 0; j < ntiles && !dead; ++j) {
+            if (j + 1 < ntiles) issue_s(j + 1);
+            // P V of tile j once P (buffer j % PBUFS) and the V operand are written
+            mbar_wait(pready_bar(j % C::PBUFS), (j / C::PBUFS) & 1, dead);
             mbar_wait(vready_bar, j & 1, dead);
             if (dead) break;
             tc_fence_after();
             if (elect_one()) {
+                const int pb = j % C::PBUFS;
+                const uint64_t pd0 = pdesc + (uint64_t)((pb * C::P_ALL) >> 4);
 #pragma unroll
                 for (int k = 0; k < kPfKeys / 16; ++k) {
-                    const uint64_t pa = pdesc + (uint64_t)((k * 32) >> 4);
+                    const uint64_t pa = pd0 + (uint64_t)((k * 32) >> 4);
                     const uint64_t vv = vdesc + (uint64_t)((2 * k * 1024) >> 4);
                     mma_ss(tbase + kPfTmemO, pa, vv, IDESC_PV, (j > 0 || k > 0) ? 1u : 0u);
                     if constexpr (Ops<T>::kSplitP)
                         mma_ss(tbase + kPfTmemO, pa + (uint64_t)(C::P_BYTES >> 4), vv, IDESC_PV, 1u);
                 }
+                mma_commit(pfree_bar(pb));
                 mma_commit(pvdone_bar);
             }
             __syncwarp();
         }
-    } else if (warp < kPfSmWarp0) {
-        // ================= dequantising warps: K and V operands =================
-        const int t = tid & (kPfKeys - 1), hf = tid / kPfKeys;  // key t, half hf of its dims
+    } else if (warp < kPfSmWarp0 || warp >= kPfVWarp0) {
+        // ================= dequantising warps: K operand (warps 0-3), V operand (10-13) =================
+        const bool vrole = warp >= kPfVWarp0;
+        const int dt = vrole ? tid - kPfVWarp0 * 32 : tid;
+        const int t = dt & (kPfKeys - 1), hf = dt / kPfKeys;  // key t, half hf of its dims
         const RowChunks<C::CPR> rows(t);
         const uint32_t tx = (uint32_t)(t & 7) << 4;
         char* const krow = sK + (t >> 3) * 1024 + (t & 7) * 128;
@@ -1729,19 +1752,19 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_tc_kernel(const DecodeA
             const int s = j % ST;
             mbar_wait(full_bar(s), (j / ST) & 1, dead);
             const char* st = ring + s * C::STAGE_BYTES;
-            // the K operand is free once the S MMA of tile j - 1 completed
-            if (j >= 1) mbar_wait(sready_bar((j - 1) & 1), ((j - 1) >> 1) & 1, dead);
-            dequant_half(st, st + 2 * C::PACK_BYTES + t * C::SROWB, krow);
-            fence_proxy_async();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(kready_bar);
-            // the V operand once the P V MMA of tile j - 1 completed
-            if (j >= 1) mbar_wait(pvdone_bar, (j - 1) & 1, dead);
-            dequant_half(st + C::PACK_BYTES, st + 2 * C::PACK_BYTES + 2 * C::SC_BYTES + t * C::SROWB, vrow);
+            if (!vrole) {
+                // the K operand is free once the S MMA of tile j - 1 completed
+                if (j >= 1) mbar_wait(sready_bar((j - 1) & 1), ((j - 1) >> 1) & 1, dead);
+                dequant_half(st, st + 2 * C::PACK_BYTES + t * C::SROWB, krow);
+            } else {
+                // the V operand once the P V MMA of tile j - 1 completed
+                if (j >= 1) mbar_wait(pvdone_bar, (j - 1) & 1, dead);
+                dequant_half(st + C::PACK_BYTES, st + 2 * C::PACK_BYTES + 2 * C::SC_BYTES + t * C::SROWB, vrow);
+            }
             fence_proxy_async();
             __syncwarp();
             if (lane == 0) {
-                mbar_arrive(vready_bar);
+                mbar_arrive(vrole ? vready_bar : kready_bar);
                 mbar_arrive(empty_bar(s));
             }
         }
@@ -1790,7 +1813,7 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_tc_kernel(const DecodeA
         // N - qL + position
         const int lim = a.causal_qL ? a.N - a.causal_qL + (r0 + r) % a.causal_qL : a.N - 1;
         float m_run = kNoMax, l_run = 0.f;
-        char* const prow = sP + (r >> 3) * 1024 + (r & 7) * 128;
+        char* const prow0 = sP + (r >> 3) * 1024 + (r & 7) * 128;
         const uint32_t px = (uint32_t)(r & 7) << 4;
         for (int j = 0; j < ntiles && !dead; ++j) {
             mbar_wait(sready_bar(j & 1), (j >> 1) & 1, dead);
@@ -1835,11 +1858,13 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_tc_kernel(const DecodeA
                 l_run *= alpha;
                 m_run = mx;
             }
-            // the P operand is free once the P V MMA of tile j - 1 completed
-            if (j >= 1) {
-                mbar_wait(pvdone_bar, (j - 1) & 1, dead);
+            // P buffer j % PBUFS is free once the P V MMA of tile j - PBUFS read it
+            constexpr int PB = C::PBUFS;
+            if (j >= PB) {
+                mbar_wait(pfree_bar(j % PB), ((j - PB) / PB) & 1, dead);
                 tc_fence_after();
             }
+            char* const prow = prow0 + (j % PB) * C::P_ALL;
 #pragma unroll
             for (int c8 = 0; c8 < kPfKeys / 8; ++c8) {
                 uint32_t hi[4], lo[4];
@@ -1860,7 +1885,7 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_tc_kernel(const DecodeA
             fence_proxy_async();
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(pready_bar);
+            if (lane == 0) mbar_arrive(pready_bar(j % PB));
         }
         // ---- the row's output: O / l (one split), or its record ----
         if (ntiles > 0) {
