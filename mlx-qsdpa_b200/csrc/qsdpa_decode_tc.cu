@@ -1471,7 +1471,9 @@ int launch_tc2(const DecodeArgs& a, cudaStream_t st) {
 // Q, then per tile read S, online softmax, write P; at the end read O), a
 // producer warp (16-byte cp.async of packed rows, scales and biases into a
 // ring) and an MMA warp (TMEM owner, issues both products from one elected
-// lane).  The K, V and P operands are single buffers, S has two TMEM buffers.
+// lane; the S product of tile j + 1 goes out before the P V product of tile j).
+// The K and V operands are single buffers, P has two buffers where shared
+// memory allows, S has two TMEM buffers.
 // Same conventions as the decode kernel: log2-domain softmax with the running
 // maximum raised only past 2^8, bounded mbarrier waits, head dims of 4-bit
 // words in the order 0,4,1,5,2,6,3,7 (put back at the output).
