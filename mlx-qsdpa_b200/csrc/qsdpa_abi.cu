@@ -269,8 +269,9 @@ int make_plan(const qsdpa_decode_params* p, const DecodeArgs& a, Plan& pl) {
         // chunk holds kLongChunk keys; CUDA-core kernel: two waves of 4 per SM.
         // No chunk below kMinChunk.
         if (pl.kern == Kern::Tc) {
-            // one CTA per SM (its shared memory fills the SM) and at most one
-            // wave, however long the chunks get: a second, ragged wave costs
+            // one CTA per SM (its shared memory fills the SM) and, while the
+            // units fit the SMs, at most one wave however long the chunks
+            // get: a second, ragged wave costs
             // more than the longer walk (measured at 1M keys, GQA-16 D=256:
             // 148 CTAs 171.8 us, 256 CTAs 197.5 us, 294 CTAs 179.2 us), so the
             // split count rounds down (8 KV heads: 18 splits, 144 CTAs)
